@@ -1,0 +1,264 @@
+/* irodori_b200.h — C ABI of the B200 (sm_100a) W8A8 int8 linear/GEMM path.
+ *
+ * Part 1 keeps the reference operator API of irodori-c's ops.h for the int8
+ * path, same names, argument meaning and error behaviour, so the C engine's
+ * dit.c and dacvae.c link against this library unchanged.  Those calls take
+ * HOST pointers (as the reference does); each one stages its operands into
+ * device memory, runs the CUDA kernels on the library's stream of the
+ * current CUDA device and copies the results back before returning.
+ *
+ * Part 2 is the stream-ordered DEVICE-pointer family that the fast path
+ * uses: quantisers, the tcgen05 GEMM with fused epilogues, the fused QKVG
+ * split, the fused SwiGLU block and the kernel-7 codec convolution as an
+ * implicit GEMM.  Weights live on the device as IroInt8DevWeight.
+ *
+ * There is no CPU implementation behind any entry point.  Without a usable
+ * sm_100 device every call fails: int-returning calls return a negative
+ * IRO_ERR_* code, void calls leave their outputs untouched and record the
+ * code for iro_cuda_last_error().
+ *
+ * Plain C types only; `stream` arguments are cudaStream_t passed as void*
+ * (NULL = the library's own stream for the current device).
+ */
+#ifndef IRODORI_B200_H
+#define IRODORI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    IRO_OK = 0,
+    IRO_ERR_INVALID = -1,        /* bad argument / shape (reference's -1)   */
+    IRO_ERR_NO_DEVICE = -2,      /* no sm_100 CUDA device                   */
+    IRO_ERR_CUDA = -3,           /* a CUDA runtime call failed              */
+    IRO_ERR_OOM = -4,            /* device or host allocation failed        */
+    IRO_ERR_DEVICE_TIMEOUT = -5, /* a bounded in-kernel wait gave up        */
+    IRO_ERR_UNSUPPORTED = -6,    /* shape outside what a kernel supports    */
+    IRO_ERR_SELFCHECK = -7       /* the exact-sum probe failed              */
+};
+
+/* ======================================================================= */
+/* Part 1 — the reference operator API (ops.h), host pointers.             */
+/* ======================================================================= */
+
+/* Quantised weight, identical layout to the reference (ops.h:23-28):
+   data int8 [N,K] row-major, scale f32 [N], colsum i32 [N] = sum_k data.
+   The three buffers are host malloc()s owned by the struct.  The library
+   also keeps a device copy per (device, data pointer), made on first use
+   and dropped by iro_int8_weight_free (the packed-weight cache). */
+typedef struct {
+    int8_t *data;
+    float *scale;
+    int32_t *colsum;
+    int N, K;
+} IroInt8Weight;
+
+/* ops.h:30 / ops.c:259-293.  Per output channel symmetric s8,
+   scale = amax/127.  Computed on the GPU; returns 0, or -1 on NULL, N/K <= 0,
+   allocation or device failure (partial state freed). */
+int iro_int8_weight_quantize(IroInt8Weight *dst, const float *w, int N, int K);
+
+/* ops.h:33-35 / ops.c:295-306.  Source stored [K,N] row-major. */
+int iro_int8_weight_quantize_transposed(IroInt8Weight *dst, const float *w,
+                                        int N, int K);
+
+/* ops.h:36 / ops.c:308-314.  Frees, zeroes, drops the device copies. */
+void iro_int8_weight_free(IroInt8Weight *w);
+
+/* ops.h:37 / ops.c:316-319. */
+size_t iro_int8_weight_bytes(const IroInt8Weight *w);
+
+/* ops.h:39-40 / ops.c:321-348.  Per-row asymmetric u8 with zero point. */
+void iro_int8_quantize_rows(const float *x, int M, int K,
+                            uint8_t *q, float *scale, int32_t *zero);
+
+/* ops.h:45-47 / ops.c:444-448. */
+void iro_int8_linear(const uint8_t *q, const float *scale,
+                     const int32_t *zero, const IroInt8Weight *w,
+                     const float *bias, float *y, int M, int32_t *work);
+
+/* ops.h:48-51 / ops.c:450-491.  work (M*N int32) receives the raw integer
+   sums, as in the reference (its selfcheck reads them back). */
+void iro_int8_linear_ex(const uint8_t *q, const float *scale,
+                        const int32_t *zero, const IroInt8Weight *w,
+                        const float *bias, float *y, int M, int32_t *work,
+                        int accumulate);
+
+/* ops.h:57-60 / ops.c:427-442.  residual receives the first-term remainder. */
+void iro_int8_quantize_rows_residual(const float *x, int M, int K,
+                                     uint8_t *q1, float *scale1, int32_t *zero1,
+                                     float *residual,
+                                     uint8_t *q2, float *scale2, int32_t *zero2);
+
+/* ops.h:64 / ops.c:367-373.  1 when an sm_100 device is usable. */
+int iro_int8_fast_available(void);
+
+/* ops.h:72 / ops.c:400-425.  Initialises the current device's context and
+   returns the backend name, or NULL when no device is usable. */
+const char *iro_int8_prepare_backend(void);
+
+/* ops.h:78 / ops.c:375-398.  Runs the reference's extreme-value exact-sum
+   probe through the tensor-core GEMM; 0 when exact, -1 otherwise. */
+int iro_int8_selfcheck(void);
+
+/* ops.h:143 / ops.c:706-716. */
+const char *iro_ops_backend_name(void);
+
+/* ======================================================================= */
+/* Part 2 — B200 runtime and the device-pointer family.                    */
+/* ======================================================================= */
+
+/* Runtime ------------------------------------------------------------------ */
+
+/* Select `device` for this host thread and create its context (stream,
+   device error word).  Returns 0 or IRO_ERR_*.  Implicit in every call. */
+int iro_cuda_init(int device);
+/* Last error recorded on this host thread by a void call (0 = none); reading
+   clears it. */
+int iro_cuda_last_error(void);
+const char *iro_cuda_error_string(int code);
+/* Number of sm_100 devices visible (0 when none). */
+int iro_cuda_device_count(void);
+/* The library stream of the current device (cudaStream_t as void*). */
+void *iro_cuda_stream(void);
+/* Block until the library stream (or `stream`) is idle; returns status,
+   including a pending in-kernel timeout report. */
+int iro_cuda_synchronize(void *stream);
+
+/* Device memory helpers for callers without their own allocator. */
+void *iro_dev_malloc(size_t bytes);
+void iro_dev_free(void *p);
+int iro_memcpy_htod(void *dst, const void *src, size_t bytes, void *stream);
+int iro_memcpy_dtoh(void *dst, const void *src, size_t bytes, void *stream);
+int iro_memcpy_dtod(void *dst, const void *src, size_t bytes, void *stream);
+int iro_memset_dev(void *dst, int value, size_t bytes, void *stream);
+void *iro_host_alloc_pinned(size_t bytes);
+void iro_host_free_pinned(void *p);
+
+/* Device weights -------------------------------------------------------------
+   data int8 [N, ld] row-major on the device, ld = K rounded up to 16 bytes
+   (zero padded), plus scale/colsum [N] and an optional per-channel bias.
+   layout PLAIN is the reference [N,K] order.  layout GATED_PAIR is the
+   fused W1|W3 order: for each block of `pair` hidden channels, `pair` W1 rows
+   then the matching `pair` W3 rows, so one GEMM tile holds both halves of
+   silu(W1 x) * (W3 x) (N = 2 * round_up(H, pair); hidden = H). */
+enum { IRO_LAYOUT_PLAIN = 0, IRO_LAYOUT_GATED_PAIR = 1 };
+
+typedef struct {
+    int8_t *data;
+    float *scale;
+    int32_t *colsum;
+    float *bias;
+    int N, K, ld;
+    int layout;
+    int pair;    /* GATED_PAIR: channels per half block */
+    int hidden;  /* GATED_PAIR: H */
+    int device;
+    void *priv;  /* library-owned (cached TMA descriptor) */
+} IroInt8DevWeight;
+
+/* Upload a host-quantised weight (PLAIN).  bias may be NULL. */
+int iro_int8_dev_weight_upload(IroInt8DevWeight *dst, const IroInt8Weight *src,
+                               const float *bias);
+/* Quantise fp32 device weights [N,K] on the device (same numerics as
+   iro_int8_weight_quantize).  bias_dev may be NULL. */
+int iro_int8_dev_weight_quantize(IroInt8DevWeight *dst, const float *w_dev,
+                                 int N, int K, const float *bias_dev, void *stream);
+/* Concatenate host weights along N (fused QKVG: Q|K|V|gate, dit.c:785-792).
+   All parts share K; biases (host, per part) may be NULL. */
+int iro_int8_dev_weight_concat(IroInt8DevWeight *dst, const IroInt8Weight *const *parts,
+                               const float *const *biases, int nparts);
+/* Build the GATED_PAIR layout from host W1 and W3 (dit.c:943-947). */
+int iro_int8_dev_weight_gated_pair(IroInt8DevWeight *dst, const IroInt8Weight *w1,
+                                   const IroInt8Weight *w3, const float *b1,
+                                   const float *b3);
+void iro_int8_dev_weight_free(IroInt8DevWeight *w);
+
+/* Quantisers (device pointers, stream ordered) ------------------------------ */
+
+/* ops.c:321-348 on the device: q u8 [M,K], scale [M], zero [M]. */
+int iro_int8_quantize_rows_dev(const float *x, int M, int K, uint8_t *q,
+                               float *scale, int32_t *zero, void *stream);
+/* Symmetric absmax/127 (tests/bench_vnni_linear.c:82-101), stored u8 = s8+128
+   with zero[m] = 128, so it feeds the same linear. */
+int iro_int8_quantize_rows_sym_dev(const float *x, int M, int K, uint8_t *q,
+                                   float *scale, int32_t *zero, void *stream);
+/* ops.c:427-442; residual may be NULL (not stored). */
+int iro_int8_quantize_rows_residual_dev(const float *x, int M, int K,
+                                        uint8_t *q1, float *scale1, int32_t *zero1,
+                                        float *residual,
+                                        uint8_t *q2, float *scale2, int32_t *zero2,
+                                        void *stream);
+
+/* GEMM + fused epilogues ------------------------------------------------------ */
+
+/* ops.c:450-491 on the device: y[M,N] (=|+=) (acc - zero*colsum)*(scale*wscale)
+   (+ bias).  work (M*N int32) is optional (NULL = not stored).  q rows are
+   K bytes apart; K % 16 != 0 is supported through an internal repack. */
+int iro_int8_linear_dev(const uint8_t *q, const float *scale, const int32_t *zero,
+                        const IroInt8DevWeight *w, const float *bias, float *y,
+                        int M, int32_t *work, int accumulate, void *stream);
+
+/* Two-term residual linear in one pass (dit.c:479-486): y = linear(q1) [+bias]
+   then += linear(q2), with both accumulators in TMEM. */
+int iro_int8_linear2_dev(const uint8_t *q1, const float *scale1, const int32_t *zero1,
+                         const uint8_t *q2, const float *scale2, const int32_t *zero2,
+                         const IroInt8DevWeight *w, const float *bias, float *y,
+                         int M, void *stream);
+
+/* Fused QKVG (dit.c:785-792): one GEMM over the concatenated weight, output
+   column block g of width `seg` written to outputs[g] ([M, seg] each). */
+int iro_int8_linear_split_dev(const uint8_t *q, const float *scale,
+                              const int32_t *zero, const IroInt8DevWeight *w,
+                              float *const *outputs, int nout, int seg, int M,
+                              void *stream);
+
+/* Fused W1|W3 GEMM with the silu gate in the epilogue (dit.c:943-956):
+   hidden[M,H] = silu(W1 x + b1) * (W3 x + b3), w13 in GATED_PAIR layout. */
+int iro_int8_gated_dev(const uint8_t *q, const float *scale, const int32_t *zero,
+                       const IroInt8DevWeight *w13, float *hidden, int M,
+                       void *stream);
+
+/* Whole int8 SwiGLU block (dit.c:913-969): quantise x [M,D], fused W1|W3 +
+   gate, quantise the hidden (two-term when residual_w2), W2 (+ b2) into
+   out [M,D].  workspace of iro_int8_swiglu_workspace_bytes() bytes, or NULL
+   for the library's own device arena. */
+size_t iro_int8_swiglu_workspace_bytes(int M, int D, int H, int residual_w2);
+int iro_int8_swiglu_dev(const float *x, int M, const IroInt8DevWeight *w13,
+                        const IroInt8DevWeight *w2, const float *b2, float *out,
+                        int residual_w2, void *workspace, void *stream);
+/* Host-pointer form of the block: x and out on the host (e2e path). */
+int iro_int8_swiglu(const float *x, int M, const IroInt8DevWeight *w13,
+                    const IroInt8DevWeight *w2, const float *b2, float *out,
+                    int residual_w2);
+
+/* Codec convolution ------------------------------------------------------------ */
+
+/* dacvae.c:543-688 (no snake): W8A8 conv1d over time-major input [T_in, C]
+   with per-output-row quantisation over the union of the kernel taps'
+   rows (padding taps = zero point), weight [N, kernel*C] tap-major, output
+   [T_out, N] (+ bias); residual adds the s/255, zero-point-128 second term.
+   Returns T_out (> 0) or IRO_ERR_*. */
+int iro_conv1d_out_len(int T_in, int kernel, int stride, int dilation, int padding);
+int iro_int8_conv1d_dev(const float *input, int T_in, int C,
+                        const IroInt8DevWeight *w, int kernel, int stride,
+                        int dilation, int padding, const float *bias,
+                        int residual, float *output, void *stream);
+
+/* Failure detection ------------------------------------------------------------- */
+
+/* Launches one block that waits on a device barrier nothing ever completes,
+   with an in-kernel limit of `limit_ns`; returns the status the host then
+   reads (IRO_ERR_DEVICE_TIMEOUT when the bounded wait gave up as designed). */
+int iro_debug_bounded_wait_probe(uint64_t limit_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IRODORI_B200_H */

@@ -1,0 +1,43 @@
+// gemm_i8.cuh — host interface of the tcgen05 int8 GEMM (gemm_i8.cu).
+#pragma once
+
+#include "runtime.cuh"
+
+namespace iro {
+
+enum EpiKind {
+  EPI_LINEAR = 0,  // y (=|+=) dequant (+bias); optional raw s32 sums
+  EPI_SPLIT = 1,   // as LINEAR, column block g written to outs[g]
+  EPI_GATED = 2,   // hidden = silu(dequant W1 + b1) * (dequant W3 + b3)
+  EPI_DUAL = 3     // y = (dequant(q1) + bias) + dequant(q2)
+};
+
+// One GEMM request: A (u8 codes, rows of `lda` bytes, K valid) against the
+// device weight w (N rows of w->ld bytes).
+struct GemmRequest {
+  int epi = EPI_LINEAR;
+  int M = 0;
+  const uint8_t* a = nullptr;
+  int lda = 0;
+  const float* sx = nullptr;
+  const int32_t* zp = nullptr;
+  const uint8_t* a2 = nullptr;  // EPI_DUAL
+  const float* sx2 = nullptr;
+  const int32_t* zp2 = nullptr;
+  const IroInt8DevWeight* w = nullptr;
+  const float* bias = nullptr;  // per weight row; GATED uses w->bias
+  float* y = nullptr;
+  int ldy = 0;
+  int32_t* work = nullptr;
+  int ldw = 0;
+  int accumulate = 0;
+  float* outs[4] = {nullptr, nullptr, nullptr, nullptr};
+  int nout = 0, seg = 0;
+  float* hidden = nullptr;  // GATED: [M, w->hidden], row pitch ldh
+  int ldh = 0;
+  int force_bn = 0;         // 0 = heuristic
+};
+
+int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
+
+}  // namespace iro

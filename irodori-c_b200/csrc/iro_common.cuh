@@ -1,0 +1,283 @@
+// iro_common.cuh — shared device helpers for the sm_100a int8 path:
+// IEEE-exact quantisation arithmetic, bounded mbarrier waits, TMA loads and
+// the tcgen05 (5th-gen tensor core / TMEM) primitives, all as inline PTX.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "irodori_b200.h"
+
+namespace iro {
+
+// ---------------------------------------------------------------------------
+// Device error word.  Bounded waits that run out record a code here (the
+// first one wins) instead of trapping, so the context stays usable and the
+// host reports a status.
+struct DevError {
+  int code;      // IRO_ERR_* (0 = none)
+  int where;     // which wait gave up
+  int block;     // blockIdx.x of the reporter
+  int pad;
+};
+
+__device__ __forceinline__ void report_error(DevError* e, int code, int where) {
+  if (e == nullptr) return;
+  if (atomicCAS(&e->code, 0, code) == 0) {
+    e->where = where;
+    e->block = blockIdx.x;
+  }
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// Quantisation arithmetic.  Every operation is an explicit round-to-nearest
+// intrinsic so that nvcc cannot contract a multiply-add into an FMA: the CPU
+// reference computes each product and sum as a separately rounded binary32
+// operation.
+
+// float -> int32 with the x86-64 cvttss2si result for NaN / out of range
+// (INT32_MIN), which is what the reference's plain C casts produce on its
+// host.  `v` is integral here (already rounded), so truncation is exact.
+__device__ __forceinline__ int f2i_x86(float v) {
+  return (v >= -2147483648.0f && v < 2147483648.0f) ? __float2int_rz(v)
+                                                     : (int)0x80000000;
+}
+
+// Row parameters from a range [lo, hi] that includes 0:
+// s = (hi-lo)/255 (1 if not > 0); inv = 1/s; zp = clamp(rint(-lo*inv),0,255).
+__device__ __forceinline__ void row_params(float lo, float hi, float& s,
+                                           float& inv, int& zp) {
+  s = __fdiv_rn(__fsub_rn(hi, lo), 255.0f);
+  if (!(s > 0.0f)) s = 1.0f;
+  inv = __fdiv_rn(1.0f, s);
+  int z = f2i_x86(rintf(__fmul_rn(-lo, inv)));
+  z = z < 0 ? 0 : z;
+  z = z > 255 ? 255 : z;
+  zp = z;
+}
+
+// One asymmetric code: clamp(rint(x*inv + zp), 0, 255); NaN -> 0 as the
+// reference's (uint8_t) cast gives on x86-64.
+__device__ __forceinline__ uint32_t quant_code(float x, float inv, float zpf) {
+  float v = rintf(__fadd_rn(__fmul_rn(x, inv), zpf));
+  v = v < 0.0f ? 0.0f : v;
+  v = v > 255.0f ? 255.0f : v;
+  return (v == v) ? (uint32_t)__float2int_rz(v) : 0u;
+}
+
+// The same code, also returning the clamped float value (needed by the
+// remainder of the two-term residual quantiser).
+__device__ __forceinline__ uint32_t quant_code_v(float x, float inv, float zpf,
+                                                 float& vout) {
+  float v = rintf(__fadd_rn(__fmul_rn(x, inv), zpf));
+  v = v < 0.0f ? 0.0f : v;
+  v = v > 255.0f ? 255.0f : v;
+  vout = v;
+  return (v == v) ? (uint32_t)__float2int_rz(v) : 0u;
+}
+
+// Running min/max with the reference's strict comparisons: a NaN never
+// replaces the running value, -0.0 never replaces +0.0.
+__device__ __forceinline__ float run_lo(float v, float lo) { return v < lo ? v : lo; }
+__device__ __forceinline__ float run_hi(float v, float hi) { return v > hi ? v : hi; }
+
+__device__ __forceinline__ void warp_minmax(float& lo, float& hi) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float l2 = __shfl_xor_sync(0xffffffffu, lo, o);
+    float h2 = __shfl_xor_sync(0xffffffffu, hi, o);
+    lo = run_lo(l2, lo);
+    hi = run_hi(h2, hi);
+  }
+}
+
+__device__ __forceinline__ float warp_max(float a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float b = __shfl_xor_sync(0xffffffffu, a, o);
+    a = b > a ? b : a;
+  }
+  return a;
+}
+
+// Dequantised output of one accumulator:
+// (float)(acc - zp*colsum) * (sx*sw) [+ bias], each step rounded.
+__device__ __forceinline__ float dequant(int acc, int zp, int colsum, float sx,
+                                         float sw) {
+  return __fmul_rn(__int2float_rn(acc - zp * colsum), __fmul_rn(sx, sw));
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory addresses and mbarriers.
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete, giving up after
+// `limit_ns` of wall time (or when `abort` is raised by another role).
+// Returns false on give-up, after recording the error.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  DevError* err, int where,
+                                                  volatile int* abort_flag,
+                                                  uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        report_error(err, IRO_ERR_DEVICE_TIMEOUT, where);
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor) loads, no multicast.
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map,
+                                            uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: TMEM allocation, MMA issue, commit, loads and fences.
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] . B[smem]^T, kind::i8, one CTA.  `accumulate` = 0
+// overwrites D.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread
+// has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit TMEM into 32 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored as rows
+// of 128 bytes with the 128-byte swizzle (the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B): 8-row core groups 1024 bytes apart, version 1,
+// layout type 2 (SWIZZLE_128B).  The tile base must be 1024-byte aligned;
+// K steps inside the 128-byte row advance the start address.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused)
+  d |= (uint64_t)(1024 >> 4) << 32;                // stride byte offset
+  d |= (uint64_t)1 << 46;                          // descriptor version
+  d |= (uint64_t)2 << 61;                          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::i8: D = s32, A = u8 (0) or s8 (1),
+// B = s8, both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N, int a_signed) {
+  return (2u << 4) | ((uint32_t)a_signed << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+}  // namespace iro

@@ -1,0 +1,61 @@
+"""CPU checks of the C ABI library: it loads without a GPU, exports every
+symbol the public header declares, and fails loudly (no CPU fallback) when
+no device is usable."""
+import ctypes
+import os
+
+import pytest
+
+import iro_b200 as iro
+
+
+def test_library_exports_every_header_symbol():
+    L = ctypes.CDLL(iro.LIB_PATH)
+    declared = iro.header_symbols()
+    assert len(declared) >= 40
+    missing = [s for s in declared if not hasattr(L, s)]
+    assert not missing, f"declared but not exported: {missing}"
+    # The binding covers the header exactly.
+    assert set(declared) == set(iro.SIGNATURES), set(declared) ^ set(iro.SIGNATURES)
+
+
+def test_no_cpu_fallback_without_device():
+    if iro.device_count() > 0:
+        pytest.skip("a GPU is present")
+    L = iro.lib()
+    assert L.iro_int8_fast_available() == 0
+    assert L.iro_int8_prepare_backend() is None
+    assert L.iro_cuda_init(0) == iro.IRO_ERR_NO_DEVICE
+    assert L.iro_int8_selfcheck() == -1
+    import numpy as np
+    x = np.ones((2, 8), np.float32)
+    q = np.full((2, 8), 7, np.uint8)
+    s = np.zeros(2, np.float32)
+    z = np.zeros(2, np.int32)
+    L.iro_cuda_last_error()
+    L.iro_int8_quantize_rows(iro._p(x), 2, 8, iro._p(q), iro._p(s), iro._p(z))
+    assert L.iro_cuda_last_error() < 0
+    assert (q == 7).all(), "outputs must stay untouched without a device"
+    w = iro.IroInt8Weight()
+    assert L.iro_int8_weight_quantize(ctypes.byref(w), iro._p(x), 2, 8) == -1
+    assert not w.data
+
+
+def test_conv_output_length_matches_reference_rule():
+    # dacvae.c:340-348
+    assert iro.conv1d_out_len(48000, 7, 1, 1, 3) == 48000
+    assert iro.conv1d_out_len(100, 7, 1, 9, 27) == 100
+    assert iro.conv1d_out_len(10, 7, 2, 1, 0) == 2
+    assert iro.conv1d_out_len(3, 7, 1, 1, 0) < 0
+
+
+def test_built_for_sm100a():
+    so = open(iro.LIB_PATH, "rb").read()
+    assert b"sm_100a" in so or b"compute_100a" in so
+
+
+def test_header_has_reference_citations():
+    txt = open(iro.HEADER_PATH).read()
+    for cite in ("ops.c:259-293", "ops.c:321-348", "ops.c:450-491", "ops.c:427-442",
+                 "ops.c:375-398", "dacvae.c:543-688", "dit.c:785-792", "dit.c:913-969"):
+        assert cite in txt, cite
