@@ -1,0 +1,523 @@
+"""Benchmark of the B200 int8 W8A8 path (one JSON line on rank 0).
+
+Workload (default): the int8 SwiGLU MLP block of the DiT,
+x fp32 [M=2048, D=1024] N(0,1); W1, W3 [2816, 1024] and W2 [1024, 2816]
+N(0,0.02) quantised per output channel; a seeded fp32 bias on every
+projection; per-row activation quantisation (the reference's asymmetric
+u8 + zero point, ops.c:321-348), silu(W1 x) * (W3 x), per-row
+requantisation, single-term W2 (IRO_INT8_RESIDUAL=0).  Synthetic data:
+there is no dataset or checkpoint for this path.
+
+A step is one pass of the block over one batch of M rows.  Metric: int8
+TOPS = algorithmic ops (2*M*N*K per GEMM) / time.  `value` has inputs
+resident in HBM; `e2e` goes through the host-pointer C-ABI call
+iro_int8_swiglu() with the step's x copied in from pinned host memory and
+the output copied back inside the timed region.  Both rotate through
+NSETS distinct input/weight sets whose total exceeds the 126 MB L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun); rows are sharded by whole
+batches, weights replicated, no collective on the data path (weak scaling).
+The device time is the max over ranks.
+"""
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for sub in ("irodori-c_b200", "oracle"):
+    sys.path.insert(0, os.path.join(ROOT, sub))
+
+M, D, H = 2048, 1024, 2816
+NSETS = 16
+METRIC = "int8 GEMM TOPS (% B200 INT8 peak); DiT Euler steps/sec at 1/2/4/8 GPUs"
+WORKLOAD = ("cfg2 int8 SwiGLU MLP block: x[2048,1024] -> quantise -> fused W1|W3 [2x2816,1024] "
+            "+ silu gate -> requantise -> W2 [1024,2816]; seeded biases; single-term W2")
+OPS_W13 = 2.0 * M * D * (2 * H)
+OPS_W2 = 2.0 * M * H * D
+OPS_STEP = OPS_W13 + OPS_W2
+
+
+def peaks():
+    """Roofline denominators: MEASURED_PEAKS.json (driver-written), else the
+    pool's stated fallback.  The int8 dense tensor rate of sm_100 is twice its
+    bf16 rate, so the int8 peak is 2x the measured cuBLAS bf16 figure."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/), or None."""
+    path = os.path.join(ROOT, "profiles", "gemm_i8_gated_cfg2.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        load = [v for v in sm if smax and v > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+def physical_gpu(local):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+def make_sets(rng, iro, oracle_mod):
+    """NSETS synthetic (x, W1, W3, W2, biases) sets on the device."""
+    sets = []
+    for i in range(NSETS):
+        x = rng.standard_normal((M, D), dtype=np.float32)
+        if i == 0:
+            x_host0 = x
+        w1 = (rng.standard_normal((H, D), dtype=np.float32) * np.float32(0.02))
+        w3 = (rng.standard_normal((H, D), dtype=np.float32) * np.float32(0.02))
+        w2 = (rng.standard_normal((D, H), dtype=np.float32) * np.float32(0.02))
+        b1 = (rng.standard_normal(H, dtype=np.float32) * np.float32(0.01))
+        b3 = (rng.standard_normal(H, dtype=np.float32) * np.float32(0.01))
+        b2 = (rng.standard_normal(D, dtype=np.float32) * np.float32(0.01))
+        # Weights are quantised on the device (iro_int8_weight_quantize).
+        hw1, hw3, hw2 = iro.HostWeight(w1), iro.HostWeight(w3), iro.HostWeight(w2)
+        w13 = iro.DevWeight.gated_pair(hw1, hw3, b1, b3)
+        dw2 = iro.DevWeight.upload(hw2, b2)
+        xd = iro.DevBuf.from_host(x)
+        qx = iro.DevBuf((M, D), np.uint8)
+        sx = iro.DevBuf(M, np.float32)
+        zx = iro.DevBuf(M, np.int32)
+        iro.quantize_rows_dev(xd, M, D, qx, sx, zx)
+        out = iro.DevBuf((M, D), np.float32)
+        hid = iro.DevBuf((M, H), np.float32)
+        sets.append(dict(x=x, xd=xd, w13=w13, w2=dw2, qx=qx, sx=sx, zx=zx, out=out, hid=hid,
+                         hw=(hw1, hw3, hw2), b=(b1, b3, b2)))
+    iro.synchronize()
+    return sets
+
+
+def check_parity(iro, oracle_mod, s0):
+    """Spot check of set 0 against the oracle (not timed)."""
+    w1, w3, w2 = s0["hw"]
+    ow = [oracle_mod.Weight(h.data, h.scale, h.colsum) for h in (w1, w3, w2)]
+    rows = 64
+    want = oracle_mod.swiglu(s0["x"][:rows], *ow, *s0["b"])
+    got = s0["out"].get()[:rows]
+    return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import iro_b200 as iro
+
+    world, rank, local = dist_setup(args.gpus)
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    iro.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
+    rng = np.random.default_rng(1000 + rank)
+
+    import oracle as oracle_mod
+    sets = make_sets(rng, iro, oracle_mod)
+    ws = iro.DevBuf(iro.swiglu_workspace_bytes(M, D, H, False), np.uint8)
+
+    def step(i):
+        s = sets[i % NSETS]
+        iro.swiglu_dev(s["xd"], M, s["w13"], s["w2"], None, s["out"], workspace=ws)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident throughput --------------------------------------
+    for i in range(args.warmup):
+        step(i)
+    iro.synchronize()
+    rel_err = check_parity(iro, oracle_mod, sets[0]) if rank == 0 else 0.0
+
+    sampler = ClockSampler(physical_gpu(local)) if local == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    iro.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    ev1.synchronize()
+    iro.synchronize()
+    dev_ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop() if sampler else None
+    torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(dev_ms)
+    ms_per_step = dev_ms / args.steps
+    value = world * OPS_STEP * args.steps / (dev_ms * 1e-3) / 1e12
+
+    # ---- dominant kernel alone: fused W1|W3 GEMM + gate ------------------
+    kreps = max(50, min(args.steps, 2000))
+    for i in range(5):
+        s = sets[i % NSETS]
+        iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
+    iro.synchronize()
+    barrier()
+    k0 = torch.cuda.Event(enable_timing=True)
+    k1 = torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for i in range(kreps):
+        s = sets[i % NSETS]
+        iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
+    k1.record(stream)
+    k1.synchronize()
+    iro.synchronize()
+    k_ms = max_over_ranks(k0.elapsed_time(k1) / kreps)
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]
+    k_tops = OPS_W13 / (k_ms * 1e-3) / 1e12
+
+    # ---- end to end through the host-pointer C ABI ------------------------
+    xs_pinned = []
+    outs_pinned = []
+    for s in sets[:4]:
+        xp = torch.empty((M, D), dtype=torch.float32, pin_memory=True)
+        xp.numpy()[:] = s["x"]
+        xs_pinned.append(xp)
+        outs_pinned.append(torch.empty((M, D), dtype=torch.float32, pin_memory=True))
+    e2e_steps = max(10, min(args.steps, 500))
+    for i in range(3):
+        s = sets[i % NSETS]
+        iro.swiglu_host(xs_pinned[i % 4].numpy(), s["w13"], s["w2"], out=outs_pinned[i % 4].numpy())
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        s = sets[i % NSETS]
+        j = i % 4
+        iro.swiglu_host(xs_pinned[j].numpy(), s["w13"], s["w2"], out=outs_pinned[j].numpy())
+    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(e2e_s)
+    e2e_tops = world * OPS_STEP * e2e_steps / e2e_s / 1e12
+
+    # ---- CPU baseline: the reference's own int8 path on the host cores ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_sample(seconds=args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8 (u8 x s8 -> s32, fp32 dequant epilogue)",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) biases)",
+        "config": {"workload": WORKLOAD, "M": M, "D": D, "H": H, "ops_per_step": OPS_STEP,
+                   "global_batch_rows": M * world, "parallelism": f"replicas x{world}",
+                   "l2": f"rotating {NSETS} input+weight sets ({NSETS * 25} MB) > 126 MB L2",
+                   "pct_int8_peak": round(100.0 * value / world / int8_peak, 2),
+                   "parity_rel_err_vs_oracle": rel_err},
+        "e2e": {"value": round(e2e_tops, 3), "unit": "TOPS",
+                "h2d_bytes_per_step": M * D * 4, "d2h_bytes_per_step": M * D * 4,
+                "api": "iro_int8_swiglu (host pointers, pinned)"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel<256,EPI_GATED> (W1|W3 + silu)",
+                     "achieved": round(k_tops, 2), "peak": round(int8_peak, 1),
+                     "unit": "TFLOP/s",
+                     "peak_note": (f"int8 dense = 2 x {pk['source']} cuBLAS bf16 burst "
+                                   f"{pk['bf16_tflops']} TF/s (of {pk['source']})"),
+                     "frac": round(k_tops / int8_peak, 4), "traffic": profile_traffic(),
+                     "ms_per_launch": round(k_ms, 5), "ops_per_launch": OPS_W13},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": 4 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# The reference's CPU path (oracle/_ref: ops.c built with the reference's
+# product flags -O3 -ffast-math for this host's ISA level), row slices over
+# all host threads (rows are independent: tests/test_int8_ops.c:87-97).
+
+
+def _ref_block(oracle_mod, L, x, ws, bs, threads):
+    import ctypes as C
+    from concurrent.futures import ThreadPoolExecutor
+
+    rows = x.shape[0]
+    out = np.empty((rows, D), np.float32)
+    wst = [oracle_mod._ref_struct(w) for w in ws]
+    p = oracle_mod._ptr
+
+    def part(lo, hi):
+        m = hi - lo
+        if m <= 0:
+            return
+        xs = np.ascontiguousarray(x[lo:hi])
+        q = np.empty((m, D), np.uint8); s = np.empty(m, np.float32); z = np.empty(m, np.int32)
+        h1 = np.empty((m, H), np.float32); h3 = np.empty((m, H), np.float32)
+        work = np.empty((m, H), np.int32)
+        qh = np.empty((m, H), np.uint8); sh = np.empty(m, np.float32); zh = np.empty(m, np.int32)
+        o = np.empty((m, D), np.float32)
+        L.iro_int8_quantize_rows(p(xs), m, D, p(q), p(s), p(z))
+        L.iro_int8_linear_ex(p(q), p(s), p(z), C.byref(wst[0]), p(bs[0]), p(h1), m, p(work), 0)
+        L.iro_int8_linear_ex(p(q), p(s), p(z), C.byref(wst[1]), p(bs[1]), p(h3), m, p(work), 0)
+        L.iro_silu_mul_inplace(p(h1), p(h3), m * H)
+        L.iro_int8_quantize_rows(p(h1), m, H, p(qh), p(sh), p(zh))
+        L.iro_int8_linear_ex(p(qh), p(sh), p(zh), C.byref(wst[2]), p(bs[2]), p(o), m, p(work), 0)
+        out[lo:hi] = o
+
+    bounds = [(rows * t // threads, rows * (t + 1) // threads) for t in range(threads)]
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda b: part(*b), bounds))
+    return out
+
+
+def _ref_inputs(rows):
+    import oracle as oracle_mod
+
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((rows, D), dtype=np.float32)
+    ws = [oracle_mod.weight_quantize(rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02))
+          for sh in ((H, D), (H, D), (D, H))]
+    bs = [rng.standard_normal(n, dtype=np.float32) * np.float32(0.01) for n in (H, H, D)]
+    return oracle_mod, x, ws, bs
+
+
+def _ref_lib():
+    import oracle as oracle_mod
+    if oracle_mod.ref_available("fast_" + oracle_mod._host_isa_variant()):
+        return oracle_mod.ref_lib("fast"), "reference", "fast_" + oracle_mod._host_isa_variant()
+    return None, "port", None
+
+
+def cpu_reference_sample(seconds=10.0, rows=256):
+    L, kind, variant = _ref_lib()
+    threads = os.cpu_count() or 1
+    oracle_mod, x, ws, bs = _ref_inputs(rows)
+    if L is None:
+        # The C restatement (same algorithm, IEEE build), when the reference
+        # could not be compiled where the build ran.
+        def run():
+            oracle_mod.swiglu(x, *ws, *bs)
+    else:
+        def run():
+            _ref_block(oracle_mod, L, x, ws, bs, threads)
+    run()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 1000:
+            break
+    ops = OPS_STEP * rows / M * reps
+    return {"value": round(ops / el / 1e12, 5), "unit": "TOPS", "cores": threads, "kind": kind,
+            "build": variant or "oracle port (-O2 IEEE)",
+            "sample": f"{rows} of {M} rows of the cfg2 block x {reps} repetitions in {el:.1f} s"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    L, kind, variant = _ref_lib()
+    threads = os.cpu_count() or 1
+    rows = 256
+    oracle_mod, x, ws, bs = _ref_inputs(rows)
+
+    def run():
+        if L is None:
+            oracle_mod.swiglu(x, *ws, *bs)
+        else:
+            _ref_block(oracle_mod, L, x, ws, bs, threads)
+
+    for _ in range(args.warmup):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = OPS_STEP * rows / M * args.steps / total / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 5), "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 (u8 x s8 -> s32, fp32 dequant epilogue)",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) biases)",
+        "config": {"workload": WORKLOAD, "M": M, "D": D, "H": H, "sample_rows": rows,
+                   "parallelism": f"{threads} host threads (row slices)"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": threads, "kind": kind,
+                         "build": variant or "oracle port (-O2 IEEE)",
+                         "sample": f"{rows} of {M} rows of the cfg2 block per step"},
+        "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_profile_case(args):
+    """A short, fixed launch sequence for ncu captures (no timing, no JSON):
+    one input set, `--warmup` + `--steps` launches of the selected op."""
+    import iro_b200 as iro
+    import oracle as oracle_mod
+
+    global NSETS
+    NSETS = 1
+    iro.init(0)
+    s = make_sets(np.random.default_rng(5), iro, oracle_mod)[0]
+    ws = iro.DevBuf(iro.swiglu_workspace_bytes(M, D, H, False), np.uint8)
+    qh = iro.DevBuf((M, H), np.uint8)
+    sh = iro.DevBuf(M, np.float32)
+    zh = iro.DevBuf(M, np.int32)
+    iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
+    iro.quantize_rows_dev(s["hid"], M, H, qh, sh, zh)
+    iro.synchronize()
+    for _ in range(args.warmup + args.steps):
+        if args.profile == "gated":
+            iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
+        elif args.profile == "w2":
+            iro.linear_dev(qh, sh, zh, s["w2"], None, s["out"], M)
+        elif args.profile == "quant":
+            iro.quantize_rows_dev(s["hid"], M, H, qh, sh, zh)
+        else:
+            iro.swiglu_dev(s["xd"], M, s["w13"], s["w2"], None, s["out"], workspace=ws)
+    iro.synchronize()
+    print(f"profile case {args.profile}: {args.warmup + args.steps} launches ok")
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block"],
+                    help="run a short fixed launch sequence for ncu instead of the benchmark")
+    args = ap.parse_args()
+    if args.warmup < 3 and not args.profile:
+        raise SystemExit("--warmup must be >= 3")
+    if args.profile:
+        run_profile_case(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -16,14 +16,23 @@
 // Parity: the integer sums are exact.  The epilogue uses explicitly rounded
 // intrinsics in the reference's order, so fp32 outputs are bit-identical to
 // the IEEE build of ops.c.
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
 #include "gemm_i8.cuh"
 
 namespace iro {
 
 constexpr int BM = 128;
 constexpr int BKB = 128;  // K bytes per pipeline stage (one swizzle row)
-constexpr int kThreads = 192;
-constexpr int kStageBudget = 196 * 1024;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kSmemMax = 232448;  // 227 KB opt-in per CTA
+constexpr int kStgBytes = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 fp32
 
 template <int BN, int EPI>
 struct Cfg {
@@ -31,18 +40,23 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BKB;
   static constexpr int B_BYTES = BN * BKB;
   static constexpr int STAGE = NA * A_BYTES + B_BYTES;
-  static constexpr int STAGES = (kStageBudget / STAGE) > 8 ? 8 : (kStageBudget / STAGE);
+  static constexpr int STG = kEpiWarps * kStgBytes;
+  static constexpr int PARAMS = 2 * 3 * BN * 4;  // double-buffered colsum/scale/bias
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int FIXED = STG + PARAMS + BAR_BYTES + 1024;
+  static constexpr int STAGES_RAW = (kSmemMax - FIXED) / STAGE;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int ACC_COLS = (EPI == EPI_DUAL) ? 2 * BN : BN;
   static constexpr int TMEM_COLS = (2 * ACC_COLS) <= 32    ? 32
                                    : (2 * ACC_COLS) <= 64  ? 64
                                    : (2 * ACC_COLS) <= 128 ? 128
                                    : (2 * ACC_COLS) <= 256 ? 256
                                                            : 512;
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;
+  static constexpr int SMEM = STAGES * STAGE + FIXED;
   static constexpr uint32_t IDESC = idesc_i8(BM, BN, 0);
   static_assert(2 * ACC_COLS <= 512, "TMEM holds 512 columns");
   static_assert(STAGES >= 2, "pipeline needs two stages");
+  static_assert(SMEM <= kSmemMax, "shared memory budget");
 };
 
 struct GemmParams {
@@ -54,12 +68,12 @@ struct GemmParams {
   const float* wscale;
   const int32_t* wcolsum;
   const float* bias;
-  int bias_vec;  // bias 16-byte aligned
   float* y;
   int ldy;
   int32_t* work;
   int ldw;
   int accumulate;
+  int tma_out;  // outputs written by TMA tile stores (else direct stores)
   float* outs[4];
   int seg;
   float* hidden;
@@ -67,88 +81,55 @@ struct GemmParams {
   int H;
   DevError* err;
   uint64_t limit_ns;
+  unsigned long long* trace;  // optional per-CTA timestamps (IRO_GEMM_TRACE)
 };
 
-// Per-column parameters of 4 consecutive weight rows n..n+3 (colsum, weight
-// scale, bias), guarded against n >= N.  `vec` = the 4 rows are in range and
-// 16-byte aligned in every array.
-struct Col4 {
-  int4 cs;
-  float4 sw;
-  float4 b;
+// Trace slots per CTA (globaltimer ns): entry, first TMA issue, first stage
+// landed at the MMA warp, last MMA commit of the first tile, first
+// accumulator handed to the epilogue, end of the first tile's epilogue,
+// exit, tiles processed.
+enum { TR_ENTRY = 0, TR_TMA0, TR_FULL0, TR_MMA_END0, TR_EPI0, TR_EPI_END0, TR_EXIT, TR_TILES,
+       TR_SLOTS = 8 };
+
+__device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
+  if (p.trace) p.trace[blockIdx.x * TR_SLOTS + slot] = globaltimer_ns();
+}
+
+// Output tensor maps (row-major fp32, box 32 x 32, 128-byte swizzle).
+struct OutMaps {
+  CUtensorMap m[4];
 };
 
-__device__ __forceinline__ Col4 load_col4(const int32_t* __restrict__ colsum,
-                                          const float* __restrict__ wscale,
-                                          const float* __restrict__ bias, int bias_vec, int n,
-                                          int N) {
-  Col4 c;
-  if (n + 4 <= N) {
-    c.cs = __ldg(reinterpret_cast<const int4*>(colsum + n));
-    c.sw = __ldg(reinterpret_cast<const float4*>(wscale + n));
-    if (bias && bias_vec) {
-      c.b = __ldg(reinterpret_cast<const float4*>(bias + n));
-    } else if (bias) {
-      c.b = make_float4(__ldg(bias + n), __ldg(bias + n + 1), __ldg(bias + n + 2),
-                        __ldg(bias + n + 3));
-    } else {
-      c.b = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  } else {
-    int cs[4];
-    float sw[4], b[4];
+// Staging layout for one warp's 32 x 32 fp32 tile in the 128-byte swizzle
+// the TMA store expects: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
+__device__ __forceinline__ void stage_row32(uint8_t* stg, int r, const float (&v)[32]) {
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const bool ok = n + j < N;
-      cs[j] = ok ? __ldg(colsum + n + j) : 0;
-      sw[j] = ok ? __ldg(wscale + n + j) : 0.0f;
-      b[j] = (ok && bias) ? __ldg(bias + n + j) : 0.0f;
-    }
-    c.cs = make_int4(cs[0], cs[1], cs[2], cs[3]);
-    c.sw = make_float4(sw[0], sw[1], sw[2], sw[3]);
-    c.b = make_float4(b[0], b[1], b[2], b[3]);
-  }
-  return c;
-}
-
-__device__ __forceinline__ float get4(const float4& v, int j) {
-  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
-}
-__device__ __forceinline__ int get4(const int4& v, int j) {
-  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
-}
-
-// Store 4 floats at dst (valid of them in range; vec = 16-byte aligned).
-__device__ __forceinline__ void store4(float* dst, const float (&v)[4], int valid, bool vec) {
-  if (valid >= 4 && vec) {
-    *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 4; j++)
-      if (j < valid) dst[j] = v[j];
+  for (int c = 0; c < 8; c++) {
+    float4* d = reinterpret_cast<float4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+    *d = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   }
 }
 
-__device__ __forceinline__ void load4(const float* src, float (&v)[4], int valid, bool vec) {
-  if (valid >= 4 && vec) {
-    const float4 t = *reinterpret_cast<const float4*>(src);
-    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-  } else {
+// Direct stores of 32 floats of one row (fallback for unaligned outputs).
+__device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], int valid) {
 #pragma unroll
-    for (int j = 0; j < 4; j++) v[j] = j < valid ? src[j] : 0.0f;
-  }
+  for (int j = 0; j < 32; j++)
+    if (j < valid) dst[j] = v[j];
 }
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmA2, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ OutMaps tmO, const GemmParams p) {
   using C = Cfg<BN, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+  uint8_t* stg_base = smem + C::STAGES * C::STAGE;             // 1024-aligned
+  float* prm = reinterpret_cast<float*>(stg_base + C::STG);    // [2][3][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg_base + C::STG + C::PARAMS);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -165,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -183,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_mark(p, TR_ENTRY);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -203,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sa, &tmA, &full[s], kb * BKB, mb * BM);
           if (EPI == EPI_DUAL) tma_load_2d(sa + C::A_BYTES, &tmA2, &full[s], kb * BKB, mb * BM);
           tma_load_2d(sb, &tmB, &full[s], kb * BKB, nb * BN);
+          if (tile == (int)blockIdx.x && kb == 0) trace_mark(p, TR_TMA0);
           if (++s == C::STAGES) {
             s = 0;
             ph ^= 1u;
@@ -229,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (tile == (int)blockIdx.x && kb == 0) trace_mark(p, TR_FULL0);
           const uint32_t a_addr = smem_u32(smem + s * C::STAGE);
           const uint32_t b_addr = a_addr + C::NA * C::A_BYTES;
 #pragma unroll
@@ -247,65 +231,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         mma_commit(&tfull[acc]);
+        if (tile == (int)blockIdx.x) trace_mark(p, TR_MMA_END0);
         acc ^= 1;
         if (acc == 0) aph ^= 1u;
       }
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+    // ---------------- epilogue (8 warps) ----------------
+    const int e = warp - 2;          // 0..7
+    const int quad = warp & 3;       // TMEM lanes 32*quad .. 32*quad+31
+    const int half = e >> 2;         // which half of the tile's columns
+    const int et = threadIdx.x - 64; // 0..255
+    uint8_t* stg = stg_base + e * kStgBytes;
     int acc = 0;
     uint32_t aph = 0;
-    const bool y_vec = ((p.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.y) & 15u) == 0);
+    int pbuf = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
-      bool got = mbar_wait_bounded(&tfull[acc], aph, p.err, 4, abort_flag, p.limit_ns);
-      got = __all_sync(0xffffffffu, got);
-      if (!got) break;
-      tc_fence_after();
-      const int row = mb * BM + quad * 32 + lane;
+      // Stage this tile's per-column parameters (overlaps the MMA).
+      float* pc = prm + pbuf * 3 * BN;
+      int* p_cs = reinterpret_cast<int*>(pc);
+      float* p_sw = pc + BN;
+      float* p_b = pc + 2 * BN;
+      for (int j = et; j < BN; j += 32 * kEpiWarps) {
+        const int n = nb * BN + j;
+        const bool ok = n < p.N;
+        p_cs[j] = ok ? __ldg(p.wcolsum + n) : 0;
+        p_sw[j] = ok ? __ldg(p.wscale + n) : 0.0f;
+        p_b[j] = (ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      }
+      const int row0 = mb * BM + quad * 32;
+      const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const float sx = row_ok ? __ldg(p.sx + row) : 0.0f;
       const int zp = row_ok ? __ldg(p.zp + row) : 0;
+      float sx2 = 0.0f;
+      int zp2 = 0;
+      if (EPI == EPI_DUAL && row_ok) {
+        sx2 = __ldg(p.sx2 + row);
+        zp2 = __ldg(p.zp2 + row);
+      }
+      // The vote doubles as the barrier that publishes the staged parameters;
+      // if any warp's bounded wait gave up, all epilogue warps stop together.
+      const bool got = mbar_wait_bounded(&tfull[acc], aph, p.err, 4, abort_flag, p.limit_ns);
+      if (named_bar_or(1, 32 * kEpiWarps, !got)) break;
+      tc_fence_after();
+      if (e == 0 && lane == 0 && tile == (int)blockIdx.x) trace_mark(p, TR_EPI0);
       const uint32_t tbase =
           tmem_base + (uint32_t)(acc * C::ACC_COLS) + ((uint32_t)(quad * 32) << 16);
+
+      // One 32-column chunk: values v for (row, out_col0 .. +31) of output
+      // map `om` / pointer base `dst_row` (when direct).
+      auto emit = [&](const float (&v)[32], const CUtensorMap* om, int out_col0, int out_cols,
+                      float* dst_row) {
+        if (p.tma_out) {
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+          stage_row32(stg, lane, v);
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0 && row0 < p.M && out_col0 < out_cols) {
+            tma_store_2d(om, stg, out_col0, row0);
+            bulk_commit();
+          }
+        } else if (row_ok) {
+          store_row32(dst_row, v, out_cols - out_col0);
+        }
+      };
 
       if (EPI == EPI_GATED) {
         // Columns [0, BN/2) hold W1 rows, [BN/2, BN) the matching W3 rows.
         constexpr int HALF = BN / 2;
-        const bool hv = ((p.ldh & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.hidden) & 15u) == 0);
-        for (int c0 = 0; c0 < HALF; c0 += 32) {
+        constexpr int PER = HALF / 2;  // hidden columns per epilogue half
+        for (int c0 = half * PER; c0 < (half + 1) * PER; c0 += 32) {
           const int h0 = nb * HALF + c0;
           if (h0 >= p.H) break;  // warp-uniform
           uint32_t r1[32], r3[32];
           tmem_ld_32x32b_x32(tbase + c0, r1);
           tmem_ld_32x32b_x32(tbase + HALF + c0, r3);
           tmem_ld_wait();
-          float* hrow = p.hidden + (size_t)row * p.ldh + h0;
+          float v[32];
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const int n1 = nb * BN + c0 + 4 * i;
-            const Col4 k1 = load_col4(p.wcolsum, p.wscale, p.bias, 1, n1, p.N);
-            const Col4 k3 = load_col4(p.wcolsum, p.wscale, p.bias, 1, n1 + HALF, p.N);
-            float v[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              float a1 = dequant((int)r1[4 * i + j], zp, get4(k1.cs, j), sx, get4(k1.sw, j));
-              float a3 = dequant((int)r3[4 * i + j], zp, get4(k3.cs, j), sx, get4(k3.sw, j));
-              if (p.bias) {
-                a1 = __fadd_rn(a1, get4(k1.b, j));
-                a3 = __fadd_rn(a3, get4(k3.b, j));
-              }
-              // ops.c:781-784: (x / (1 + expf(-x))) * g
-              v[j] = __fmul_rn(__fdiv_rn(a1, __fadd_rn(1.0f, expf(-a1))), a3);
+          for (int j = 0; j < 32; j++) {
+            const int c1 = c0 + j, c3 = HALF + c0 + j;
+            float a1 = dequant((int)r1[j], zp, p_cs[c1], sx, p_sw[c1]);
+            float a3 = dequant((int)r3[j], zp, p_cs[c3], sx, p_sw[c3]);
+            if (p.bias) {
+              a1 = __fadd_rn(a1, p_b[c1]);
+              a3 = __fadd_rn(a3, p_b[c3]);
             }
-            if (row_ok) store4(hrow + 4 * i, v, p.H - h0 - 4 * i, hv);
+            // ops.c:781-784: (x / (1 + expf(-x))) * g
+            v[j] = __fmul_rn(__fdiv_rn(a1, __fadd_rn(1.0f, expf(-a1))), a3);
           }
+          emit(v, &tmO.m[0], h0, p.H, p.hidden + (size_t)row * p.ldh + h0);
         }
       } else {
-        const bool vec_out = (EPI == EPI_SPLIT) ? ((p.seg & 3) == 0) : y_vec;
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
           const int n0 = nb * BN + c0;
           if (n0 >= p.N) break;  // warp-uniform
           uint32_t r[32];
@@ -313,73 +335,101 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r2[32];
           if (EPI == EPI_DUAL) tmem_ld_32x32b_x32(tbase + BN + c0, r2);
           tmem_ld_wait();
-          float sx2 = 0.0f;
-          int zp2 = 0;
-          if (EPI == EPI_DUAL && row_ok) {
-            sx2 = __ldg(p.sx2 + row);
-            zp2 = __ldg(p.zp2 + row);
-          }
-          float* dst;
-          int ld;
+          int g = 0, col0 = n0, ncols = p.N, ld = p.ldy;
+          float* base = p.y;
           if (EPI == EPI_SPLIT) {
-            const int g = n0 / p.seg;
-            float* base = g == 0 ? p.outs[0] : g == 1 ? p.outs[1] : g == 2 ? p.outs[2] : p.outs[3];
-            dst = base + (n0 - g * p.seg);
+            g = n0 / p.seg;
+            col0 = n0 - g * p.seg;
+            ncols = p.seg;
             ld = p.seg;
-          } else {
-            dst = p.y + n0;
-            ld = p.ldy;
+            base = g == 0 ? p.outs[0] : g == 1 ? p.outs[1] : g == 2 ? p.outs[2] : p.outs[3];
           }
-          float* drow = dst + (size_t)row * ld;
-          int32_t* wrow = (EPI == EPI_LINEAR && p.work) ? p.work + (size_t)row * p.ldw + n0 : nullptr;
-          const bool w_vec = (p.ldw & 3) == 0;
+          float* drow = base + (size_t)row * ld + col0;
+          const int valid = ncols - col0;
+          float v[32];
+          if (EPI == EPI_LINEAR && p.accumulate) {
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const int n = n0 + 4 * i;
-            const int valid = p.N - n;
-            const Col4 k = load_col4(p.wcolsum, p.wscale, p.bias, p.bias_vec, n, p.N);
-            float old[4] = {0.f, 0.f, 0.f, 0.f};
-            if (EPI == EPI_LINEAR && p.accumulate && row_ok && valid > 0)
-              load4(drow + 4 * i, old, valid, vec_out);
-            float v[4];
+            for (int j = 0; j < 32; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
+          }
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              float t = dequant((int)r[4 * i + j], zp, get4(k.cs, j), sx, get4(k.sw, j));
-              if (p.bias) t = __fadd_rn(t, get4(k.b, j));
-              if (EPI == EPI_DUAL)
-                t = __fadd_rn(t, dequant((int)r2[4 * i + j], zp2, get4(k.cs, j), sx2, get4(k.sw, j)));
-              if (EPI == EPI_LINEAR && p.accumulate) t = __fadd_rn(old[j], t);
-              v[j] = t;
-            }
-            if (row_ok && valid > 0) {
-              store4(drow + 4 * i, v, valid, vec_out);
-              if (wrow) {
-                if (valid >= 4 && w_vec) {
-                  *reinterpret_cast<int4*>(wrow + 4 * i) =
-                      make_int4((int)r[4 * i], (int)r[4 * i + 1], (int)r[4 * i + 2], (int)r[4 * i + 3]);
-                } else {
+          for (int j = 0; j < 32; j++) {
+            const int c = c0 + j;
+            float t = dequant((int)r[j], zp, p_cs[c], sx, p_sw[c]);
+            if (p.bias) t = __fadd_rn(t, p_b[c]);
+            if (EPI == EPI_DUAL) t = __fadd_rn(t, dequant((int)r2[j], zp2, p_cs[c], sx2, p_sw[c]));
+            if (EPI == EPI_LINEAR && p.accumulate) t = __fadd_rn(v[j], t);
+            v[j] = t;
+          }
+          emit(v, &tmO.m[g], col0, ncols, drow);
+          if (EPI == EPI_LINEAR && p.work != nullptr && row_ok) {
+            int32_t* wrow = p.work + (size_t)row * p.ldw + n0;
 #pragma unroll
-                  for (int j = 0; j < 4; j++)
-                    if (j < valid) wrow[4 * i + j] = (int)r[4 * i + j];
-                }
-              }
-            }
+            for (int j = 0; j < 32; j++)
+              if (j < valid) wrow[j] = (int)r[j];
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (e == 0 && lane == 0 && tile == (int)blockIdx.x) trace_mark(p, TR_EPI_END0);
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
+      pbuf ^= 1;
     }
+    if (lane == 0) bulk_wait_all<0>();
+    __syncwarp();
   }
 
   __syncthreads();
+  if (threadIdx.x == 0 && p.trace) {
+    trace_mark(p, TR_EXIT);
+    p.trace[blockIdx.x * TR_SLOTS + TR_TILES] =
+        (unsigned long long)((p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+}
+
+// IRO_GEMM_TRACE=1: print a per-role timeline of each GEMM launch (median and
+// max over CTAs, microseconds from the earliest CTA entry).  Diagnostic only;
+// synchronises the stream after every launch.
+static int trace_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("IRO_GEMM_TRACE");
+    on = (e && *e && *e != '0') ? 1 : 0;
+  }
+  return on;
+}
+
+static void trace_report(const char* name, int M, int N, int K, const unsigned long long* dev,
+                         int grid, cudaStream_t s) {
+  std::vector<unsigned long long> h((size_t)grid * TR_SLOTS);
+  cudaStreamSynchronize(s);
+  cudaMemcpy(h.data(), dev, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  unsigned long long t0 = ~0ull;
+  for (int b = 0; b < grid; b++) t0 = std::min(t0, h[(size_t)b * TR_SLOTS + TR_ENTRY]);
+  const char* names[7] = {"entry", "tma0", "full0", "mma_end0", "epi0", "epi_end0", "exit"};
+  fprintf(stderr, "[gemm trace] %s M=%d N=%d K=%d grid=%d tiles/cta=%llu..%llu\n", name, M, N, K,
+          grid, h[(size_t)(grid - 1) * TR_SLOTS + TR_TILES], h[TR_TILES]);
+  for (int k = 0; k < 7; k++) {
+    std::vector<double> v;
+    for (int b = 0; b < grid; b++) {
+      unsigned long long t = h[(size_t)b * TR_SLOTS + k];
+      if (t >= t0) v.push_back((t - t0) * 1e-3);
+    }
+    std::sort(v.begin(), v.end());
+    if (v.empty()) continue;
+    fprintf(stderr, "  %-9s min %8.2f  med %8.2f  max %8.2f us\n", names[k], v.front(),
+            v[v.size() / 2], v.back());
+  }
+}
+
+static bool out_tma_ok(const float* base, int ld) {
+  return base != nullptr && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (ld & 3) == 0;
 }
 
 template <int BN, int EPI>
@@ -405,12 +455,48 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
     ta2 = ta;
   }
   GemmParams p = p0;
+  OutMaps om;
+  memset(&om, 0, sizeof(om));
+  // Output tiles go out through TMA stores when every output is 16-byte
+  // aligned with a 16-byte multiple pitch; otherwise direct stores.
+  bool tma = true;
+  if (EPI == EPI_GATED) {
+    tma = out_tma_ok(r.hidden, r.ldh);
+    if (tma)
+      st = make_tmap_f32_sw128(&om.m[0], r.hidden, (uint64_t)w->hidden, (uint64_t)r.M,
+                               (uint64_t)r.ldh * 4);
+  } else if (EPI == EPI_SPLIT) {
+    for (int i = 0; i < r.nout && tma; i++) tma = out_tma_ok(r.outs[i], r.seg);
+    for (int i = 0; tma && i < r.nout && st == IRO_OK; i++)
+      st = make_tmap_f32_sw128(&om.m[i], r.outs[i], (uint64_t)r.seg, (uint64_t)r.M,
+                               (uint64_t)r.seg * 4);
+  } else {
+    tma = out_tma_ok(r.y, r.ldy);
+    if (tma)
+      st = make_tmap_f32_sw128(&om.m[0], r.y, (uint64_t)w->N, (uint64_t)r.M,
+                               (uint64_t)r.ldy * 4);
+  }
+  if (st) return st;
+  p.tma_out = tma ? 1 : 0;
   p.tiles_m = cdiv(r.M, BM);
   p.tiles_n = cdiv(w->N, BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   const int grid = p.num_tiles < c->num_sms ? p.num_tiles : c->num_sms;
-  gemm_i8_kernel<BN, EPI><<<grid, kThreads, C::SMEM, s>>>(ta, tb, ta2, p);
-  return check_launch();
+  unsigned long long* tr = nullptr;
+  if (trace_enabled()) {
+    cudaMalloc(&tr, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid);
+    cudaMemsetAsync(tr, 0, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid, s);
+    p.trace = tr;
+  }
+  gemm_i8_kernel<BN, EPI><<<grid, kThreads, C::SMEM, s>>>(ta, tb, ta2, om, p);
+  st = check_launch();
+  if (tr) {
+    char name[48];
+    snprintf(name, sizeof(name), "bn%d/epi%d", BN, EPI);
+    trace_report(name, r.M, w->N, w->K, tr, grid, s);
+    cudaFree(tr);
+  }
+  return st;
 }
 
 // Tile width: the fewest waves of the persistent grid, with a per-tile cost
@@ -449,7 +535,6 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   p.wscale = w->scale;
   p.wcolsum = w->colsum;
   p.bias = (r.epi == EPI_GATED) ? w->bias : r.bias;
-  p.bias_vec = p.bias ? ((reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0) : 0;
   p.y = r.y;
   p.ldy = r.ldy;
   p.work = r.work;

@@ -140,39 +140,43 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One bounded poll of the phase with the given parity.  The suspend-time
+// hint lets the hardware park the thread until the phase completes (or the
+// hint expires) instead of spinning on shared memory, which would compete
+// with the tensor cores' operand reads.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
 
 // Wait for the phase with the given parity to complete, giving up after
-// `limit_ns` of wall time (or when `abort` is raised by another role).
-// Returns false on give-up, after recording the error.
+// about `limit_ns` (or when `abort` is raised by another role).  The bound
+// uses the SM cycle counter, converted at 2 cycles per ns, so a slower clock
+// only lengthens the wait.  Returns false on give-up, after recording the
+// error.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   DevError* err, int where,
                                                   volatile int* abort_flag,
                                                   uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
-      if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
-        report_error(err, IRO_ERR_DEVICE_TIMEOUT, where);
-        if (abort_flag != nullptr) *abort_flag = 1;
-        return false;
-      }
+  const long long t0 = clock64();
+  const long long limit_cycles = (long long)(limit_ns * 2ull);
+  while (!mbar_try_wait(bar, parity)) {
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (clock64() - t0 > limit_cycles) {
+      report_error(err, IRO_ERR_DEVICE_TIMEOUT, where);
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
     }
   }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -189,6 +193,56 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// TMA tile store from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x,
+                                             int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(smem_u32(smem_src))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Make generic-proxy shared-memory writes visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier over `count` threads (id 0 is __syncthreads).
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier over `count` threads that also ORs a predicate across them:
+// every participant learns whether any of them passed `pred` = true.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
 }
 
 // ---------------------------------------------------------------------------

@@ -176,6 +176,12 @@ int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ro
                    box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+int make_tmap_f32_sw128(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                        uint64_t pitch_bytes) {
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, inner, rows, pitch_bytes, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 int make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                   uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_rows) {
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, inner, rows, pitch_bytes,
