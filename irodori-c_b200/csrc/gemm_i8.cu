@@ -313,16 +313,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int c1 = c0 + j, c3 = HALF + c0 + j;
-            float a1 = dequant((int)r1[j], zp, p_cs[c1], sx, p_sw[c1]);
-            float a3 = dequant((int)r3[j], zp, p_cs[c3], sx, p_sw[c3]);
+          for (int i = 0; i < 8; i++) {
+            const int c1 = c0 + 4 * i, c3 = HALF + c0 + 4 * i;
+            const int4 cs1 = *reinterpret_cast<const int4*>(p_cs + c1);
+            const float4 sw1 = *reinterpret_cast<const float4*>(p_sw + c1);
+            const int4 cs3 = *reinterpret_cast<const int4*>(p_cs + c3);
+            const float4 sw3 = *reinterpret_cast<const float4*>(p_sw + c3);
+            float2 a1lo = dequant2(r1[4 * i], r1[4 * i + 1], zp, cs1.x, cs1.y, sx, sw1.x, sw1.y);
+            float2 a1hi = dequant2(r1[4 * i + 2], r1[4 * i + 3], zp, cs1.z, cs1.w, sx, sw1.z, sw1.w);
+            float2 a3lo = dequant2(r3[4 * i], r3[4 * i + 1], zp, cs3.x, cs3.y, sx, sw3.x, sw3.y);
+            float2 a3hi = dequant2(r3[4 * i + 2], r3[4 * i + 3], zp, cs3.z, cs3.w, sx, sw3.z, sw3.w);
             if (p.bias) {
-              a1 = __fadd_rn(a1, p_b[c1]);
-              a3 = __fadd_rn(a3, p_b[c3]);
+              const float4 b1 = *reinterpret_cast<const float4*>(p_b + c1);
+              const float4 b3 = *reinterpret_cast<const float4*>(p_b + c3);
+              a1lo = add2_rn(a1lo, make_float2(b1.x, b1.y));
+              a1hi = add2_rn(a1hi, make_float2(b1.z, b1.w));
+              a3lo = add2_rn(a3lo, make_float2(b3.x, b3.y));
+              a3hi = add2_rn(a3hi, make_float2(b3.z, b3.w));
             }
-            // ops.c:781-784: (x / (1 + expf(-x))) * g
-            v[j] = __fmul_rn(__fdiv_rn(a1, __fadd_rn(1.0f, expf(-a1))), a3);
+            v[4 * i] = silu_gate(a1lo.x, a3lo.x);
+            v[4 * i + 1] = silu_gate(a1lo.y, a3lo.y);
+            v[4 * i + 2] = silu_gate(a1hi.x, a3hi.x);
+            v[4 * i + 3] = silu_gate(a1hi.y, a3hi.y);
           }
           emit(v, &tmO.m[0], h0, p.H, p.hidden + (size_t)row * p.ldh + h0);
         }
@@ -352,13 +364,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
           }
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int c = c0 + j;
-            float t = dequant((int)r[j], zp, p_cs[c], sx, p_sw[c]);
-            if (p.bias) t = __fadd_rn(t, p_b[c]);
-            if (EPI == EPI_DUAL) t = __fadd_rn(t, dequant((int)r2[j], zp2, p_cs[c], sx2, p_sw[c]));
-            if (EPI == EPI_LINEAR && p.accumulate) t = __fadd_rn(v[j], t);
-            v[j] = t;
+          for (int i = 0; i < 8; i++) {
+            const int c = c0 + 4 * i;
+            const int4 cs = *reinterpret_cast<const int4*>(p_cs + c);
+            const float4 sw = *reinterpret_cast<const float4*>(p_sw + c);
+            float2 lo = dequant2(r[4 * i], r[4 * i + 1], zp, cs.x, cs.y, sx, sw.x, sw.y);
+            float2 hi = dequant2(r[4 * i + 2], r[4 * i + 3], zp, cs.z, cs.w, sx, sw.z, sw.w);
+            if (p.bias) {
+              const float4 b = *reinterpret_cast<const float4*>(p_b + c);
+              lo = add2_rn(lo, make_float2(b.x, b.y));
+              hi = add2_rn(hi, make_float2(b.z, b.w));
+            }
+            if (EPI == EPI_DUAL) {
+              lo = add2_rn(lo, dequant2(r2[4 * i], r2[4 * i + 1], zp2, cs.x, cs.y, sx2, sw.x, sw.y));
+              hi = add2_rn(hi, dequant2(r2[4 * i + 2], r2[4 * i + 3], zp2, cs.z, cs.w, sx2, sw.z, sw.w));
+            }
+            if (EPI == EPI_LINEAR && p.accumulate) {
+              lo = add2_rn(make_float2(v[4 * i], v[4 * i + 1]), lo);
+              hi = add2_rn(make_float2(v[4 * i + 2], v[4 * i + 3]), hi);
+            }
+            v[4 * i] = lo.x;
+            v[4 * i + 1] = lo.y;
+            v[4 * i + 2] = hi.x;
+            v[4 * i + 3] = hi.y;
           }
           emit(v, &tmO.m[g], col0, ncols, drow);
           if (EPI == EPI_LINEAR && p.work != nullptr && row_ok) {

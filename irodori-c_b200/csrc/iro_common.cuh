@@ -114,6 +114,39 @@ __device__ __forceinline__ float dequant(int acc, int zp, int colsum, float sx,
   return __fmul_rn(__int2float_rn(acc - zp * colsum), __fmul_rn(sx, sw));
 }
 
+// Two dequantised outputs (the reference's scalar formula twice).  Packed
+// f32x2 arithmetic is not used here: ptxas may contract a packed product
+// and a packed sum into one FFMA2 even with explicit .rn, which changes the
+// rounding; the scalar __fmul_rn / __fadd_rn are never contracted.
+__device__ __forceinline__ float2 dequant2(uint32_t acc0, uint32_t acc1, int zp, int cs0,
+                                           int cs1, float sx, float sw0, float sw1) {
+  return make_float2(dequant((int)acc0, zp, cs0, sx, sw0), dequant((int)acc1, zp, cs1, sx, sw1));
+}
+
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+}
+
+// a / d for d >= 1 (d may be +inf), the silu denominator.  Markstein's
+// method: an approximate reciprocal r, the quotient q0 = a*r, the exact
+// residual a - q0*d from one FMA, and one correction q0 + residual*r; this
+// lands within half an ulp of a/d except when a/d lies within ~2^-23 ulp of a
+// rounding boundary.  a/inf is the signed zero a*0.
+__device__ __forceinline__ float div_ge1(float a, float d) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+  const float q0 = __fmul_rn(a, r);
+  const float e = __fmaf_rn(-q0, d, a);
+  const float q1 = __fmaf_rn(e, r, q0);
+  return d == __int_as_float(0x7f800000) ? __fmul_rn(a, 0.0f) : q1;
+}
+
+// silu(a) * g as the reference writes it, (a / (1 + expf(-a))) * g
+// (ops.c:781-784), with expf from the CUDA math library.
+__device__ __forceinline__ float silu_gate(float a, float g) {
+  return __fmul_rn(div_ge1(a, __fadd_rn(1.0f, expf(-a))), g);
+}
+
 // ---------------------------------------------------------------------------
 // Shared-memory addresses and mbarriers.
 
