@@ -140,6 +140,24 @@ def dist_setup(n_gpus):
     return world, rank, local
 
 
+def shard_requests(n_requests, world, rank):
+    """Contiguous block of whole requests for `rank` (every CFG row of a
+    request stays on one GPU: attention and the CFG combine mix rows only
+    within a request, SURVEY rows 8e / sampler.c:285-297)."""
+    base, extra = divmod(n_requests, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def max_over_ranks_cpu(value, dist):
+    """Max of a host float over the process group (gloo or nccl)."""
+    import torch
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def physical_gpu(local):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:

@@ -270,7 +270,7 @@ def _bind_ops(L):
 
 
 def ref_lib(kind="ieee"):
-    """kind: 'ieee' (parity build), 'codec', 'dit', or 'fast' (product flags,
+    """kind: "ieee" (parity build), "codec", "dit", "vnni", or "fast" (product flags,
     variant chosen for this host's ISA)."""
     if kind == "fast":
         kind = "fast_" + _host_isa_variant()
@@ -278,7 +278,7 @@ def ref_lib(kind="ieee"):
         path = os.path.join(REF_DIR, f"libiro_ref_{kind}.so")
         if not os.path.exists(path):
             raise RuntimeError(f"reference build {path} is missing")
-        L = _bind_ops(C.CDLL(path))
+        L = C.CDLL(path) if kind == "vnni" else _bind_ops(C.CDLL(path))
         if kind == "codec":
             L.ref_conv1d_int8_forward.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int,
                                                   C.c_int, C.c_int, C.c_int, C.c_int, _vp,

@@ -1,0 +1,93 @@
+"""Seeded inputs behind the golden fixtures (shared by make_golden.py and the
+tests).  The test_int8_ops.c cases use that test's own xorshift generator
+(tests/test_int8_ops.c:12-16, 49-53, 122-125); the others use numpy PCG64."""
+import hashlib
+
+import numpy as np
+
+CONV_KEYS = ("T", "C", "N", "kernel", "stride", "dilation", "padding", "residual", "bias")
+
+
+def sha(*arrays):
+    h = hashlib.sha256()
+    for a in arrays:
+        if a is not None:
+            h.update(np.ascontiguousarray(a).tobytes())
+    return h.digest()
+
+
+def _xorshift():
+    import oracle
+    return oracle.XorShift()
+
+
+def int8_ops_cases():
+    """The four cases of tests/test_int8_ops.c, in its order, drawing from one
+    generator: w = rnd()*0.08, x = rnd()*3, outliers x[m,17] = 20 + rnd(),
+    bias = rnd()."""
+    g = _xorshift()
+    out = []
+    for (M, N, K, outlier) in [(7, 32, 64, 0), (23, 96, 128, 1), (112, 160, 1280, 0),
+                               (37, 184, 1280, 1)]:
+        w = g.rnd(N * K).reshape(N, K) * np.float32(0.08)
+        x = g.rnd(M * K).reshape(M, K) * np.float32(3.0)
+        if outlier:
+            for m in range(M):
+                x[m, 17] = np.float32(20.0) + g.rnd(1)[0]
+        bias = g.rnd(N)
+        out.append((M, N, K, outlier, w.astype(np.float32), x.astype(np.float32),
+                    bias.astype(np.float32)))
+    return out
+
+
+def degenerate_rows():
+    """tests/test_int8_ops.c:126-134."""
+    x = np.zeros((2, 16), np.float32)
+    x[1] = 2.5
+    return x
+
+
+def residual_input():
+    rng = np.random.default_rng(2024)
+    x = (rng.standard_normal((33, 257)) * np.exp(rng.standard_normal((33, 1)))).astype(np.float32)
+    x[3] = 0.0
+    x[4, 7] = 40.0
+    return x
+
+
+def residual_weight():
+    rng = np.random.default_rng(2025)
+    return (rng.standard_normal((48, 257)) * 0.02).astype(np.float32)
+
+
+def conv_cases():
+    cases = [dict(T=40, C=32, N=24, kernel=7, stride=1, dilation=1, padding=3, residual=0, bias=1),
+             dict(T=40, C=32, N=24, kernel=7, stride=1, dilation=3, padding=9, residual=1, bias=0),
+             dict(T=37, C=16, N=8, kernel=7, stride=2, dilation=1, padding=3, residual=0, bias=1),
+             dict(T=12, C=32, N=24, kernel=7, stride=1, dilation=9, padding=27, residual=1, bias=1)]
+    out = []
+    for i, c in enumerate(cases):
+        rng = np.random.default_rng(100 + i)
+        inp = (rng.standard_normal((c["T"], c["C"])) * 0.5).astype(np.float32)
+        inp[min(5, c["T"] - 1)] = 0.0
+        w = (rng.standard_normal((c["N"], c["kernel"] * c["C"])) * 0.02).astype(np.float32)
+        bias = (rng.standard_normal(c["N"]) * 0.01).astype(np.float32) if c["bias"] else None
+        out.append((c, inp, w, bias))
+    return out
+
+
+def sym_input():
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((40, 96)).astype(np.float32)
+    x[2] = 0.0
+    x[5, 3] = 55.0
+    return x
+
+
+def dit_swiglu_inputs(D, H, rows=3):
+    rng = np.random.default_rng(4242)
+    x = rng.standard_normal((rows, D)).astype(np.float32)
+    w1 = (rng.standard_normal((H, D)) * 0.02).astype(np.float32)
+    w3 = (rng.standard_normal((H, D)) * 0.02).astype(np.float32)
+    w2 = (rng.standard_normal((D, H)) * 0.02).astype(np.float32)
+    return x, w1, w3, w2

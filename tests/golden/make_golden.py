@@ -1,0 +1,128 @@
+"""Generate the committed golden fixtures in tests/golden/ from the REFERENCE
+itself: oracle/_ref holds irodori-c's ops.c (IEEE build), dacvae.c, dit.c and
+the VNNI prototype compiled from their sources (oracle/Makefile `ref`).
+
+    make -C oracle ref REF_DIR=<reference tree>
+    python tests/golden/make_golden.py
+
+Inputs are regenerated from seeds by tests/golden/inputs.py (the reference
+test's xorshift for the test_int8_ops.c cases, numpy PCG64 elsewhere); each
+fixture also records a SHA-256 of its inputs so a generator drift is caught.
+Outputs are exactly what the reference code returned.
+"""
+import ctypes as C
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+sys.path.insert(0, HERE)
+
+import oracle  # noqa: E402
+import inputs  # noqa: E402
+
+
+def int8_ops():
+    out = {}
+    for idx, (M, N, K, outlier, w, x, bias) in enumerate(inputs.int8_ops_cases()):
+        W = oracle.ref_weight_quantize(w)
+        q, s, z = oracle.ref_quantize_rows(x)
+        y, work = oracle.ref_linear_ex(q, s, z, W, bias)
+        sub = min(M, 5)
+        y_sub, work_sub = oracle.ref_linear_ex(q[M - sub:], s[M - sub:], z[M - sub:], W, bias)
+        pre = f"c{idx}_"
+        out.update({pre + "shape": np.array([M, N, K, outlier], np.int32),
+                    pre + "inputs_sha": np.frombuffer(inputs.sha(w, x, bias), np.uint8),
+                    pre + "wdata": W.data, pre + "wscale": W.scale, pre + "wcolsum": W.colsum,
+                    pre + "q": q, pre + "s": s, pre + "z": z, pre + "work": work, pre + "y": y,
+                    pre + "work_sub": work_sub})
+    x = inputs.degenerate_rows()
+    q, s, z = oracle.ref_quantize_rows(x)
+    out.update({"degen_q": q, "degen_s": s, "degen_z": z})
+    L = oracle.ref_lib("ieee")
+    out["selfcheck_rc"] = np.array([L.iro_int8_selfcheck()], np.int32)
+    return out
+
+
+def residual():
+    x = inputs.residual_input()
+    (q1, s1, z1), r, (q2, s2, z2) = oracle.ref_quantize_rows_residual(x)
+    acc = {}
+    W = oracle.ref_weight_quantize(inputs.residual_weight())
+    y1, _ = oracle.ref_linear_ex(q1, s1, z1, W, None)
+    y2, _ = oracle.ref_linear_ex(q2, s2, z2, W, None, y=y1, accumulate=True)
+    acc.update({"inputs_sha": np.frombuffer(inputs.sha(x), np.uint8), "q1": q1, "s1": s1,
+                "z1": z1, "r": r, "q2": q2, "s2": s2, "z2": z2, "y_two_term": y2})
+    return acc
+
+
+def conv7():
+    out = {}
+    for idx, (case, inp, w, bias) in enumerate(inputs.conv_cases()):
+        W = oracle.ref_weight_quantize(w)
+        o = oracle.ref_conv1d_int8(inp, W, case["kernel"], case["stride"], case["dilation"],
+                                   case["padding"], bias, case["residual"])
+        pre = f"c{idx}_"
+        out.update({pre + "params": np.array([case[k] for k in inputs.CONV_KEYS], np.int32),
+                    pre + "inputs_sha": np.frombuffer(inputs.sha(inp, w, bias), np.uint8),
+                    pre + "wdata": W.data, pre + "wscale": W.scale, pre + "wcolsum": W.colsum,
+                    pre + "out": o})
+    return out
+
+
+def sym():
+    x = inputs.sym_input()
+    L = oracle.ref_lib("vnni")
+    L.ref_quantize_activation_sym.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]
+    L.ref_quantize_activation_sym.restype = None
+    M, K = x.shape
+    q = np.empty((M, K), np.uint8)
+    s = np.empty(M, np.float32)
+    L.ref_quantize_activation_sym(oracle._ptr(x), oracle._ptr(q), oracle._ptr(s), M, K)
+    return {"inputs_sha": np.frombuffer(inputs.sha(x), np.uint8), "q": q, "s": s}
+
+
+def dit_swiglu_child(mode):
+    """Runs in a child process so IRO_INT8_RESIDUAL is read fresh (the
+    reference caches it in a function-static)."""
+    D, H = oracle.ref_dit_dims()
+    x, w1, w3, w2 = inputs.dit_swiglu_inputs(D, H)
+    W = [oracle.ref_weight_quantize(w) for w in (w1, w3, w2)]
+    o = oracle.ref_dit_swiglu(x, *W)
+    np.save(os.path.join(HERE, f"_tmp_swiglu_{mode}.npy"), o)
+
+
+def dit_swiglu():
+    out = {}
+    for mode, env in (("residual_default", None), ("single_term", "0")):
+        e = dict(os.environ)
+        e.pop("IRO_INT8_RESIDUAL", None)
+        if env is not None:
+            e["IRO_INT8_RESIDUAL"] = env
+        subprocess.run([sys.executable, __file__, "--swiglu-child", mode], check=True, env=e)
+        path = os.path.join(HERE, f"_tmp_swiglu_{mode}.npy")
+        out[mode] = np.load(path)
+        os.remove(path)
+    D, H = oracle.ref_dit_dims()
+    x, w1, w3, w2 = inputs.dit_swiglu_inputs(D, H)
+    out["dims"] = np.array([D, H], np.int32)
+    out["inputs_sha"] = np.frombuffer(inputs.sha(x, w1, w3, w2), np.uint8)
+    return out
+
+
+def main():
+    if len(sys.argv) > 2 and sys.argv[1] == "--swiglu-child":
+        dit_swiglu_child(sys.argv[2])
+        return
+    for name, fn in (("int8_ops", int8_ops), ("residual", residual), ("conv7", conv7),
+                     ("sym_quant", sym), ("dit_swiglu", dit_swiglu)):
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    main()
