@@ -237,6 +237,24 @@ int iro_int8_swiglu(const float *x, int M, const IroInt8DevWeight *w13,
                     const IroInt8DevWeight *w2, const float *b2, float *out,
                     int residual_w2);
 
+/* The SwiGLU block without allocation.  No counterpart in the reference.
+   For callers that cannot allocate device memory where they run the block:
+   code recording it into a CUDA graph under global-mode stream capture,
+   engines that reserve all device memory at start-up, and latency-critical
+   loops (growing the library arena calls cudaFree, which waits for the
+   device).  Same arguments and results as iro_int8_swiglu_dev without the
+   workspace: the scratch is a 64 MiB array inside the library, reserved on
+   every GPU where the library's device code is loaded until the process
+   exits.  Calls whose scratch (iro_int8_swiglu_workspace_bytes) exceeds
+   64 MiB are rejected with IRO_ERR_UNSUPPORTED and a message on stderr; split
+   the rows.  It calls no cudaMalloc/cudaFree and does not touch the library
+   context.  The first call on a device resolves the scratch address, so make
+   it before any stream capture.  Calls share the scratch: calls that can
+   overlap on the GPU race.  `stream` NULL is the default stream. */
+int iro_int8_swiglu_noalloc_dev(const float *x, int M, const IroInt8DevWeight *w13,
+                                const IroInt8DevWeight *w2, const float *b2, float *out,
+                                int residual_w2, void *stream);
+
 /* Codec convolution ------------------------------------------------------------ */
 
 /* dacvae.c:543-688 (no snake): W8A8 conv1d over time-major input [T_in, C]

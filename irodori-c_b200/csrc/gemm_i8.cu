@@ -511,7 +511,7 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
   p.num_tiles = p.tiles_m * p.tiles_n;
   const int grid = p.num_tiles < c->num_sms ? p.num_tiles : c->num_sms;
   unsigned long long* tr = nullptr;
-  if (trace_enabled()) {
+  if (trace_enabled() && !r.no_alloc) {
     cudaMalloc(&tr, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid);
     cudaMemsetAsync(tr, 0, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid, s);
     p.trace = tr;

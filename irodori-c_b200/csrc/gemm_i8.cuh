@@ -36,6 +36,7 @@ struct GemmRequest {
   float* hidden = nullptr;  // GATED: [M, w->hidden], row pitch ldh
   int ldh = 0;
   int force_bn = 0;         // 0 = heuristic
+  int no_alloc = 0;         // never allocate (skips the IRO_GEMM_TRACE buffer)
 };
 
 int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);

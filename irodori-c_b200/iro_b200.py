@@ -95,6 +95,7 @@ SIGNATURES = {
     "iro_int8_swiglu_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "iro_int8_swiglu_dev": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i, _vp, _vp]),
     "iro_int8_swiglu": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i]),
+    "iro_int8_swiglu_noalloc_dev": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i, _vp]),
     "iro_conv1d_out_len": (_i, [_i, _i, _i, _i, _i]),
     "iro_int8_conv1d_dev": (_i, [_vp, _i, _i, _DW, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
@@ -440,6 +441,13 @@ def swiglu_host(x, w13: DevWeight, w2: DevWeight, out=None, residual_w2=False, b
     check(lib().iro_int8_swiglu(_p(x), M, C.byref(w13.st), C.byref(w2.st), _p(b2_dev), _p(out),
                                 int(bool(residual_w2))), "iro_int8_swiglu")
     return out
+
+
+def swiglu_noalloc_dev(x, M, w13: DevWeight, w2: DevWeight, b2, out, residual_w2=False,
+                      stream=None):
+    """The SwiGLU block on the library's built-in scratch (no allocation)."""
+    return lib().iro_int8_swiglu_noalloc_dev(_p(x), M, C.byref(w13.st), C.byref(w2.st), _p(b2),
+                                             _p(out), int(bool(residual_w2)), stream)
 
 
 def conv1d_out_len(T_in, kernel, stride=1, dilation=1, padding=0):
