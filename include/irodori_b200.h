@@ -257,13 +257,14 @@ int iro_int8_swiglu_noalloc_dev(const float *x, int M, const IroInt8DevWeight *w
 
 /* Codec convolution ------------------------------------------------------------ */
 
-/* dacvae.c:543-688 (no snake): W8A8 conv1d over time-major input [T_in, C]
-   with per-output-row quantisation over the union of the kernel taps'
-   rows (padding taps = zero point), weight [N, kernel*C] tap-major, output
-   [T_out, N] (+ bias); residual adds the s/255, zero-point-128 second term.
-   Returns T_out (> 0) or IRO_ERR_*. */
+/* dacvae.c:543-688 (no snake): W8A8 conv1d over `batch` independent
+   time-major inputs [T_in, C] (contiguous, [batch, T_in, C]) with
+   per-output-row quantisation over the union of the kernel taps' rows
+   (padding taps = zero point), weight [N, kernel*C] tap-major (dacvae.h:11-12),
+   output [batch, T_out, N] (+ bias); residual adds the s/255, zero-point-128
+   second term.  Returns T_out (> 0) or IRO_ERR_*. */
 int iro_conv1d_out_len(int T_in, int kernel, int stride, int dilation, int padding);
-int iro_int8_conv1d_dev(const float *input, int T_in, int C,
+int iro_int8_conv1d_dev(const float *input, int batch, int T_in, int C,
                         const IroInt8DevWeight *w, int kernel, int stride,
                         int dilation, int padding, const float *bias,
                         int residual, float *output, void *stream);

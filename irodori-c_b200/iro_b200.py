@@ -97,7 +97,7 @@ SIGNATURES = {
     "iro_int8_swiglu": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i]),
     "iro_int8_swiglu_noalloc_dev": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i, _vp]),
     "iro_conv1d_out_len": (_i, [_i, _i, _i, _i, _i]),
-    "iro_int8_conv1d_dev": (_i, [_vp, _i, _i, _DW, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
+    "iro_int8_conv1d_dev": (_i, [_vp, _i, _i, _i, _DW, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
 }
 
@@ -454,10 +454,10 @@ def conv1d_out_len(T_in, kernel, stride=1, dilation=1, padding=0):
     return lib().iro_conv1d_out_len(T_in, kernel, stride, dilation, padding)
 
 
-def conv1d_dev(inp, T_in, Cin, w: DevWeight, kernel, stride, dilation, padding, bias, residual,
-               out, stream=None):
-    rc = lib().iro_int8_conv1d_dev(_p(inp), T_in, Cin, C.byref(w.st), kernel, stride, dilation,
-                                   padding, _p(bias), int(bool(residual)), _p(out), stream)
+def conv1d_dev(inp, batch, T_in, Cin, w: DevWeight, kernel, stride, dilation, padding, bias,
+               residual, out, stream=None):
+    rc = lib().iro_int8_conv1d_dev(_p(inp), batch, T_in, Cin, C.byref(w.st), kernel, stride,
+                                   dilation, padding, _p(bias), int(bool(residual)), _p(out), stream)
     if rc < 0:
         raise IroError(rc, "conv1d_dev")
     return rc
