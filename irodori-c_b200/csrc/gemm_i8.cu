@@ -29,10 +29,13 @@ namespace iro {
 
 constexpr int BM = 128;
 constexpr int BKB = 128;  // K bytes per pipeline stage (one swizzle row)
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;      // 4 per TMEM lane quadrant / per scheduler
+constexpr int kParts = kEpiWarps / 4;  // column parts per quadrant
+constexpr int kChunk = 16;         // columns per tcgen05.ld / staging tile
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemMax = 232448;  // 227 KB opt-in per CTA
-constexpr int kStgBytes = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 fp32
+constexpr int kStgBytes = 32 * kChunk * 4;  // one staging tile: 32 rows x 16 fp32
+constexpr int kStgBufs = 2;                 // staging tiles per epilogue warp
 
 template <int BN, int EPI>
 struct Cfg {
@@ -40,7 +43,7 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BKB;
   static constexpr int B_BYTES = BN * BKB;
   static constexpr int STAGE = NA * A_BYTES + B_BYTES;
-  static constexpr int STG = kEpiWarps * kStgBytes;
+  static constexpr int STG = kEpiWarps * kStgBufs * kStgBytes;
   static constexpr int PARAMS = 2 * 3 * BN * 4;  // double-buffered colsum/scale/bias
   static constexpr int BAR_BYTES = 256;
   static constexpr int FIXED = STG + PARAMS + BAR_BYTES + 1024;
@@ -95,25 +98,25 @@ __device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
   if (p.trace) p.trace[blockIdx.x * TR_SLOTS + slot] = globaltimer_ns();
 }
 
-// Output tensor maps (row-major fp32, box 32 x 32, 128-byte swizzle).
+// Output tensor maps (row-major fp32, box 32 rows x 16 columns, 64-byte swizzle).
 struct OutMaps {
   CUtensorMap m[4];
 };
 
-// Staging layout for one warp's 32 x 32 fp32 tile in the 128-byte swizzle
-// the TMA store expects: 16-byte chunk c of row r lives at chunk c ^ (r & 7).
-__device__ __forceinline__ void stage_row32(uint8_t* stg, int r, const float (&v)[32]) {
+// Staging layout for one warp's 32 x 16 fp32 tile in the 64-byte swizzle the
+// TMA store expects: 16-byte chunk c of row r lives at chunk c ^ ((r >> 1) & 3).
+__device__ __forceinline__ void stage_row16(uint8_t* stg, int r, const float (&v)[kChunk]) {
 #pragma unroll
-  for (int c = 0; c < 8; c++) {
-    float4* d = reinterpret_cast<float4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+  for (int c = 0; c < 4; c++) {
+    float4* d = reinterpret_cast<float4*>(stg + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
     *d = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   }
 }
 
-// Direct stores of 32 floats of one row (fallback for unaligned outputs).
-__device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], int valid) {
+// Direct stores of one row's chunk (fallback for unaligned outputs).
+__device__ __forceinline__ void store_row16(float* dst, const float (&v)[kChunk], int valid) {
 #pragma unroll
-  for (int j = 0; j < 32; j++)
+  for (int j = 0; j < kChunk; j++)
     if (j < valid) dst[j] = v[j];
 }
 
@@ -238,12 +241,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue (8 warps) ----------------
-    const int e = warp - 2;          // 0..7
+    // ---------------- epilogue (16 warps) ----------------
+    const int e = warp - 2;          // 0..15
     const int quad = warp & 3;       // TMEM lanes 32*quad .. 32*quad+31
-    const int half = e >> 2;         // which half of the tile's columns
-    const int et = threadIdx.x - 64; // 0..255
-    uint8_t* stg = stg_base + e * kStgBytes;
+    const int part = e >> 2;         // which quarter of the tile's columns
+    const int et = threadIdx.x - 64; // 0..511
+    uint8_t* stg_mine = stg_base + e * kStgBufs * kStgBytes;
+    int sbuf = 0;  // next staging tile of this warp
     int acc = 0;
     uint32_t aph = 0;
     int pbuf = 0;
@@ -281,14 +285,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tbase =
           tmem_base + (uint32_t)(acc * C::ACC_COLS) + ((uint32_t)(quad * 32) << 16);
 
-      // One 32-column chunk: values v for (row, out_col0 .. +31) of output
-      // map `om` / pointer base `dst_row` (when direct).
-      auto emit = [&](const float (&v)[32], const CUtensorMap* om, int out_col0, int out_cols,
+      // One 16-column chunk: values v for (row, out_col0 .. +15) of output
+      // map `om` / pointer `dst_row` (direct fallback).
+      auto emit = [&](const float (&v)[kChunk], const CUtensorMap* om, int out_col0, int out_cols,
                       float* dst_row) {
         if (p.tma_out) {
-          if (lane == 0) bulk_wait_read<0>();
+          // The store issued kStgBufs chunks ago read this tile; wait only
+          // for that one (at most kStgBufs - 1 stores stay in flight).
+          uint8_t* stg = stg_mine + sbuf * kStgBytes;
+          sbuf = sbuf + 1 == kStgBufs ? 0 : sbuf + 1;
+          if (lane == 0) bulk_wait_read<kStgBufs - 1>();
           __syncwarp();
-          stage_row32(stg, lane, v);
+          stage_row16(stg, lane, v);
           fence_async_shared();
           __syncwarp();
           if (lane == 0 && row0 < p.M && out_col0 < out_cols) {
@@ -296,24 +304,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_commit();
           }
         } else if (row_ok) {
-          store_row32(dst_row, v, out_cols - out_col0);
+          store_row16(dst_row, v, out_cols - out_col0);
         }
       };
 
       if (EPI == EPI_GATED) {
         // Columns [0, BN/2) hold W1 rows, [BN/2, BN) the matching W3 rows.
         constexpr int HALF = BN / 2;
-        constexpr int PER = HALF / 2;  // hidden columns per epilogue half
-        for (int c0 = half * PER; c0 < (half + 1) * PER; c0 += 32) {
+        constexpr int PER = HALF / kParts;  // hidden columns per epilogue warp
+        for (int c0 = part * PER; c0 < (part + 1) * PER; c0 += kChunk) {
           const int h0 = nb * HALF + c0;
           if (h0 >= p.H) break;  // warp-uniform
-          uint32_t r1[32], r3[32];
-          tmem_ld_32x32b_x32(tbase + c0, r1);
-          tmem_ld_32x32b_x32(tbase + HALF + c0, r3);
+          uint32_t r1[kChunk], r3[kChunk];
+          tmem_ld_32x32b_x16(tbase + c0, r1);
+          tmem_ld_32x32b_x16(tbase + HALF + c0, r3);
           tmem_ld_wait();
-          float v[32];
+          float v[kChunk];
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
+          for (int i = 0; i < kChunk / 4; i++) {
             const int c1 = c0 + 4 * i, c3 = HALF + c0 + 4 * i;
             const int4 cs1 = *reinterpret_cast<const int4*>(p_cs + c1);
             const float4 sw1 = *reinterpret_cast<const float4*>(p_sw + c1);
@@ -339,13 +347,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           emit(v, &tmO.m[0], h0, p.H, p.hidden + (size_t)row * p.ldh + h0);
         }
       } else {
-        for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+        constexpr int PER = BN / kParts;
+        for (int c0 = part * PER; c0 < (part + 1) * PER; c0 += kChunk) {
           const int n0 = nb * BN + c0;
           if (n0 >= p.N) break;  // warp-uniform
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c0, r);
-          uint32_t r2[32];
-          if (EPI == EPI_DUAL) tmem_ld_32x32b_x32(tbase + BN + c0, r2);
+          uint32_t r[kChunk];
+          tmem_ld_32x32b_x16(tbase + c0, r);
+          uint32_t r2[kChunk];
+          if (EPI == EPI_DUAL) tmem_ld_32x32b_x16(tbase + BN + c0, r2);
           tmem_ld_wait();
           int g = 0, col0 = n0, ncols = p.N, ld = p.ldy;
           float* base = p.y;
@@ -358,13 +367,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           float* drow = base + (size_t)row * ld + col0;
           const int valid = ncols - col0;
-          float v[32];
+          float v[kChunk];
           if (EPI == EPI_LINEAR && p.accumulate) {
 #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
+            for (int j = 0; j < kChunk; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
           }
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
+          for (int i = 0; i < kChunk / 4; i++) {
             const int c = c0 + 4 * i;
             const int4 cs = *reinterpret_cast<const int4*>(p_cs + c);
             const float4 sw = *reinterpret_cast<const float4*>(p_sw + c);
@@ -392,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (EPI == EPI_LINEAR && p.work != nullptr && row_ok) {
             int32_t* wrow = p.work + (size_t)row * p.ldw + n0;
 #pragma unroll
-            for (int j = 0; j < 32; j++)
+            for (int j = 0; j < kChunk; j++)
               if (j < valid) wrow[j] = (int)r[j];
           }
         }

@@ -178,8 +178,8 @@ int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ro
 
 int make_tmap_f32_sw128(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                         uint64_t pitch_bytes) {
-  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, inner, rows, pitch_bytes, 32, 32,
-                   CU_TENSOR_MAP_SWIZZLE_128B);
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, inner, rows, pitch_bytes, 16, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 int make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,

@@ -63,8 +63,8 @@ int take_device_error(Ctx* c);
 int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                  uint64_t pitch, uint32_t box_inner, uint32_t box_rows);
 
-// 2-D f32 tensor map for TMA tile stores of 32 x 32 boxes with the 128-byte
-// swizzle (rows x inner floats, pitch in bytes, multiple of 16).
+// 2-D f32 tensor map for TMA tile stores of 32-row x 16-column boxes with the
+// 64-byte swizzle (rows x inner floats, pitch in bytes, multiple of 16).
 int make_tmap_f32_sw128(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                         uint64_t pitch_bytes);
 
