@@ -131,18 +131,21 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
 // method: an approximate reciprocal r, the quotient q0 = a*r, the exact
 // residual a - q0*d from one FMA, and one correction q0 + residual*r; this
 // lands within half an ulp of a/d except when a/d lies within ~2^-23 ulp of a
-// rounding boundary.  a/inf is the signed zero a*0.
+// rounding boundary.  For d >= 2^126 (including +inf) the flushed reciprocal
+// is unusable and the rarely taken branch divides exactly.
 __device__ __forceinline__ float div_ge1(float a, float d) {
+  if (d >= 8.5070592e37f) return __fdiv_rn(a, d);  // 2^126
   float r;
-  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
   const float q0 = __fmul_rn(a, r);
   const float e = __fmaf_rn(-q0, d, a);
-  const float q1 = __fmaf_rn(e, r, q0);
-  return d == __int_as_float(0x7f800000) ? __fmul_rn(a, 0.0f) : q1;
+  return __fmaf_rn(e, r, q0);
 }
 
 // silu(a) * g as the reference writes it, (a / (1 + expf(-a))) * g
-// (ops.c:781-784), with expf from the CUDA math library.
+// (ops.c:781-784), with expf from the CUDA math library (a faster
+// hardware-ex2 exponential was tried and moved the hidden up to 5 ulp from
+// the host libm, enough to flip requantisation codes).
 __device__ __forceinline__ float silu_gate(float a, float g) {
   return __fmul_rn(div_ge1(a, __fadd_rn(1.0f, expf(-a))), g);
 }

@@ -36,9 +36,9 @@ def ulp_diff(a, b):
     return np.abs(ai - bi)
 
 
-def make_block(seed, M, D, H, bias=True):
+def make_block(seed, M, D, H, bias=True, x_scale=1.0):
     rng = np.random.default_rng(seed)
-    x = rng.standard_normal((M, D)).astype(np.float32)
+    x = (rng.standard_normal((M, D)) * x_scale).astype(np.float32)
     ws = [oracle.weight_quantize((rng.standard_normal(sh) * 0.02).astype(np.float32))
           for sh in ((H, D), (H, D), (D, H))]
     bs = [(rng.standard_normal(n) * 0.01).astype(np.float32) if bias else None
@@ -55,10 +55,13 @@ def upload(ws, bs):
     return w13, dw2
 
 
-@pytest.mark.parametrize("M,D,H", [(64, 1024, 2816), (300, 1280, 3680), (2048, 1024, 2816),
-                                   (5, 256, 200)])
-def test_gated_hidden(M, D, H):
-    x, ws, bs = make_block(M + H, M, D, H)
+@pytest.mark.parametrize("M,D,H,x_scale", [(64, 1024, 2816, 1.0), (300, 1280, 3680, 1.0),
+                                           (2048, 1024, 2816, 1.0), (5, 256, 200, 1.0),
+                                           (256, 1024, 2816, 60.0)])
+def test_gated_hidden(M, D, H, x_scale):
+    """x_scale 60 spreads the gate inputs over roughly +-100, through the
+    overflow of e^-a (a < -88.7) and the flush of e^-a to 0 (a > 87)."""
+    x, ws, bs = make_block(M + H, M, D, H, x_scale=x_scale)
     w13, _ = upload(ws, bs)
     q, s, z = oracle.quantize_rows(x)
     qd, sd, zd = iro.DevBuf.from_host(q), iro.DevBuf.from_host(s), iro.DevBuf.from_host(z)
