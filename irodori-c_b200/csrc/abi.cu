@@ -800,6 +800,16 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
   return gemm_launch(c, r, s);
 }
 
+// True when `p` is page-locked host memory (async copies can overlap).
+static bool is_pinned(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
+
 int iro_int8_swiglu(const float* x, int M, const IroInt8DevWeight* w13,
                     const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2) {
   if (!x || !out || !w13 || !w2 || M < 0) return IRO_ERR_INVALID;
@@ -808,19 +818,55 @@ int iro_int8_swiglu(const float* x, int M, const IroInt8DevWeight* w13,
   if (!hc.c) return hc.status;
   Ctx* c = hc.c;
   const int D = w13->K;
-  const size_t xb = (sizeof(float) * (size_t)M * D + 255) / 256 * 256;
-  const size_t wsb = iro_int8_swiglu_workspace_bytes(M, D, w13->hidden, residual_w2);
+  const size_t row_bytes = sizeof(float) * (size_t)D;
+  // Rows are independent, so the block can run in row chunks: with page-locked
+  // host buffers the copy in of chunk i+1, the compute of chunk i and the copy
+  // out of chunk i-1 run at once on three streams.  Pageable buffers take one
+  // synchronous pass.
+  // A chunk must stay large enough that its compute (four kernel launches)
+  // is shorter than its copies: ~512 rows, at most 8 chunks.
+  const char* env = getenv("IRO_SWIGLU_CHUNK_ROWS");
+  const int target = env && *env ? std::max(128, atoi(env)) : 512;
+  const bool overlap = M >= 2 * target && is_pinned(x) && is_pinned(out);
+  const int nchunk = overlap ? std::min(8, M / target) : 1;
+  const int chunk = round_up(cdiv(M, nchunk), 128);
+  const size_t xb = (row_bytes * (size_t)M + 255) / 256 * 256;
+  const size_t wsb = iro_int8_swiglu_workspace_bytes(std::min(chunk, M), D, w13->hidden, residual_w2);
   int st = IRO_OK;
   uint8_t* base = static_cast<uint8_t*>(arena_get(c, 2 * xb + wsb, &st));
   if (!base) return st;
   float* x_d = reinterpret_cast<float*>(base);
   float* o_d = reinterpret_cast<float*>(base + xb);
+  uint8_t* ws = base + 2 * xb;
   cudaStream_t s = c->stream;
-  st = cuda_st(cudaMemcpyAsync(x_d, x, sizeof(float) * (size_t)M * D, cudaMemcpyHostToDevice, s));
-  if (st == IRO_OK)
-    st = iro_int8_swiglu_dev(x_d, M, w13, w2, b2, o_d, residual_w2, base + 2 * xb, s);
-  if (st == IRO_OK)
-    st = cuda_st(cudaMemcpyAsync(out, o_d, sizeof(float) * (size_t)M * D, cudaMemcpyDeviceToHost, s));
+  if (!overlap) {
+    st = cuda_st(cudaMemcpyAsync(x_d, x, row_bytes * M, cudaMemcpyHostToDevice, s));
+    if (st == IRO_OK) st = iro_int8_swiglu_dev(x_d, M, w13, w2, b2, o_d, residual_w2, ws, s);
+    if (st == IRO_OK)
+      st = cuda_st(cudaMemcpyAsync(out, o_d, row_bytes * M, cudaMemcpyDeviceToHost, s));
+    return finish(c, st);
+  }
+  st = ctx_copy_resources(c, 2 * nchunk + 1);
+  if (st) return st;
+  cudaEvent_t* ev = c->events.data();
+  for (int i = 0, r0 = 0; st == IRO_OK && r0 < M; i++, r0 += chunk) {
+    const int rows = std::min(chunk, M - r0);
+    const size_t off = (size_t)r0 * D;
+    st = cuda_st(cudaMemcpyAsync(x_d + off, x + off, row_bytes * rows, cudaMemcpyHostToDevice,
+                                 c->copy_in));
+    if (st == IRO_OK) st = cuda_st(cudaEventRecord(ev[2 * i], c->copy_in));
+    if (st == IRO_OK) st = cuda_st(cudaStreamWaitEvent(s, ev[2 * i], 0));
+    if (st == IRO_OK)
+      st = iro_int8_swiglu_dev(x_d + off, rows, w13, w2, b2, o_d + off, residual_w2, ws, s);
+    if (st == IRO_OK) st = cuda_st(cudaEventRecord(ev[2 * i + 1], s));
+    if (st == IRO_OK) st = cuda_st(cudaStreamWaitEvent(c->copy_out, ev[2 * i + 1], 0));
+    if (st == IRO_OK)
+      st = cuda_st(cudaMemcpyAsync(out + off, o_d + off, row_bytes * rows, cudaMemcpyDeviceToHost,
+                                   c->copy_out));
+  }
+  cudaError_t e = cudaStreamSynchronize(c->copy_out);
+  if (st == IRO_OK && e != cudaSuccess) st = map_cuda(e);
+  cudaStreamSynchronize(c->copy_in);
   return finish(c, st);
 }
 

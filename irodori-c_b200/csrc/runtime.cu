@@ -137,6 +137,23 @@ void* arena_get(Ctx* c, size_t bytes, int* status) {
   return c->arena;
 }
 
+int ctx_copy_resources(Ctx* c, int n) {
+  cudaError_t e = cudaSuccess;
+  if (!c->copy_in) e = cudaStreamCreateWithFlags(&c->copy_in, cudaStreamNonBlocking);
+  if (e == cudaSuccess && !c->copy_out)
+    e = cudaStreamCreateWithFlags(&c->copy_out, cudaStreamNonBlocking);
+  while (e == cudaSuccess && (int)c->events.size() < n) {
+    cudaEvent_t ev;
+    e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) c->events.push_back(ev);
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return map_cuda(e);
+  }
+  return IRO_OK;
+}
+
 int take_device_error(Ctx* c) {
   if (cudaMemcpy(c->err_host, c->err, sizeof(DevError), cudaMemcpyDeviceToHost) != cudaSuccess)
     return IRO_ERR_CUDA;

@@ -31,7 +31,15 @@ struct Ctx {
   size_t arena_bytes = 0;
   std::mutex mu;
   std::unordered_map<const void*, CachedWeight> wcache;
+  // Copy streams and events for host-pointer calls that overlap their
+  // host<->device copies with compute (created on first use).
+  cudaStream_t copy_in = nullptr;
+  cudaStream_t copy_out = nullptr;
+  std::vector<cudaEvent_t> events;
 };
+
+// The copy streams and at least `n` events of the context (created lazily).
+int ctx_copy_resources(Ctx* c, int n);
 
 // Context of device `dev` if it was already created (no side effects).
 Ctx* ctx_existing(int dev);

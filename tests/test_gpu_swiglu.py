@@ -132,3 +132,29 @@ def test_swiglu_caller_workspace_matches_arena():
     iro.swiglu_dev(xd, M, w13, dw2, None, o2, residual_w2=True, workspace=wsb)
     iro.synchronize()
     assert (o1.get().view(np.uint32) == o2.get().view(np.uint32)).all()
+
+
+def test_swiglu_host_pinned_pipelined_matches_device():
+    """With page-locked host buffers iro_int8_swiglu runs the block in row
+    chunks with the copies overlapped; rows are independent, so the result is
+    bit-identical to one device-pointer call."""
+    import ctypes as C
+    M, D, H = 2048, 1024, 2816
+    x, ws, bs = make_block(123, M, D, H)
+    w13, dw2 = upload(ws, bs)
+    L = iro.lib()
+    px, po = L.iro_host_alloc_pinned(M * D * 4), L.iro_host_alloc_pinned(M * D * 4)
+    try:
+        xp = np.ctypeslib.as_array((C.c_float * (M * D)).from_address(px)).reshape(M, D)
+        op = np.ctypeslib.as_array((C.c_float * (M * D)).from_address(po)).reshape(M, D)
+        xp[:] = x
+        iro.check(L.iro_int8_swiglu(iro._p(xp), M, C.byref(w13.st), C.byref(dw2.st), None,
+                                    iro._p(op), 0), "iro_int8_swiglu")
+        xd = iro.DevBuf.from_host(x)
+        out = iro.DevBuf((M, D), np.float32)
+        iro.swiglu_dev(xd, M, w13, dw2, None, out)
+        iro.synchronize()
+        assert (op.view(np.uint32) == out.get().view(np.uint32)).all()
+    finally:
+        L.iro_host_free_pinned(px)
+        L.iro_host_free_pinned(po)
