@@ -237,6 +237,17 @@ int iro_int8_swiglu(const float *x, int M, const IroInt8DevWeight *w13,
                     const IroInt8DevWeight *w2, const float *b2, float *out,
                     int residual_w2);
 
+/* Recorded plans.  A plan records one block's kernel launches, with fixed
+   device pointers, as a CUDA graph; iro_plan_launch replays it on `stream`
+   with one call.  The plan owns its workspace.  Inputs are read and outputs
+   written at launch time, so the caller refills x between launches. */
+typedef struct IroPlan IroPlan;
+int iro_int8_swiglu_plan(IroPlan **plan, const float *x, int M, const IroInt8DevWeight *w13,
+                         const IroInt8DevWeight *w2, const float *b2, float *out,
+                         int residual_w2);
+int iro_plan_launch(const IroPlan *plan, void *stream);
+void iro_plan_free(IroPlan *plan);
+
 /* The SwiGLU block without allocation.  No counterpart in the reference.
    For callers that cannot allocate device memory where they run the block:
    code recording it into a CUDA graph under global-mode stream capture,

@@ -96,6 +96,9 @@ SIGNATURES = {
     "iro_int8_swiglu_dev": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i, _vp, _vp]),
     "iro_int8_swiglu": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i]),
     "iro_int8_swiglu_noalloc_dev": (_i, [_vp, _i, _DW, _DW, _vp, _vp, _i, _vp]),
+    "iro_int8_swiglu_plan": (_i, [C.POINTER(_vp), _vp, _i, _DW, _DW, _vp, _vp, _i]),
+    "iro_plan_launch": (_i, [_vp, _vp]),
+    "iro_plan_free": (None, [_vp]),
     "iro_conv1d_out_len": (_i, [_i, _i, _i, _i, _i]),
     "iro_int8_conv1d_dev": (_i, [_vp, _i, _i, _i, _DW, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
@@ -448,6 +451,31 @@ def swiglu_noalloc_dev(x, M, w13: DevWeight, w2: DevWeight, b2, out, residual_w2
     """The SwiGLU block on the library's built-in scratch (no allocation)."""
     return lib().iro_int8_swiglu_noalloc_dev(_p(x), M, C.byref(w13.st), C.byref(w2.st), _p(b2),
                                              _p(out), int(bool(residual_w2)), stream)
+
+
+class Plan:
+    """A recorded SwiGLU block (CUDA graph) with fixed device buffers."""
+
+    def __init__(self, x, M, w13: DevWeight, w2: DevWeight, b2, out, residual_w2=False):
+        self.h = C.c_void_p()
+        check(lib().iro_int8_swiglu_plan(C.byref(self.h), _p(x), M, C.byref(w13.st),
+                                         C.byref(w2.st), _p(b2), _p(out),
+                                         int(bool(residual_w2))), "iro_int8_swiglu_plan")
+        self._keep = (x, w13, w2, b2, out)
+
+    def launch(self, stream=None):
+        check(lib().iro_plan_launch(self.h, stream), "iro_plan_launch")
+
+    def free(self):
+        if self.h:
+            lib().iro_plan_free(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def conv1d_out_len(T_in, kernel, stride=1, dilation=1, padding=0):

@@ -158,3 +158,25 @@ def test_swiglu_host_pinned_pipelined_matches_device():
     finally:
         L.iro_host_free_pinned(px)
         L.iro_host_free_pinned(po)
+
+
+@pytest.mark.parametrize("residual", [False, True])
+def test_swiglu_plan_replays_the_block(residual):
+    """A recorded plan (CUDA graph) gives the block's result bit-for-bit, and
+    reads the input buffer afresh at every launch."""
+    M, D, H = 1024, 1024, 2816
+    x, ws, bs = make_block(55, M, D, H)
+    w13, dw2 = upload(ws, bs)
+    xd = iro.DevBuf.from_host(x)
+    out = iro.DevBuf((M, D), np.float32)
+    plan = iro.Plan(xd, M, w13, dw2, None, out, residual_w2=residual)
+    ref = iro.DevBuf((M, D), np.float32)
+    for step in range(2):
+        xs = (x * (1.0 + step)).astype(np.float32)
+        xd.upload(xs)
+        plan.launch()
+        iro.synchronize()
+        iro.swiglu_dev(xd, M, w13, dw2, None, ref, residual_w2=residual)
+        iro.synchronize()
+        assert (out.get().view(np.uint32) == ref.get().view(np.uint32)).all(), f"step {step}"
+    plan.free()
