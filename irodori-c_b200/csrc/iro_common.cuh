@@ -64,29 +64,30 @@ __device__ __forceinline__ void row_params(float lo, float hi, float& s,
 }
 
 // One asymmetric code: clamp(rint(x*inv + zp), 0, 255); NaN -> 0 as the
-// reference's (uint8_t) cast gives on x86-64.
+// reference's (uint8_t) cast gives on x86-64.  The clamp is fmaxf/fminf,
+// whose NaN rule (the non-NaN operand wins) sends a NaN to 0 as well.
 __device__ __forceinline__ uint32_t quant_code(float x, float inv, float zpf) {
-  float v = rintf(__fadd_rn(__fmul_rn(x, inv), zpf));
-  v = v < 0.0f ? 0.0f : v;
-  v = v > 255.0f ? 255.0f : v;
-  return (v == v) ? (uint32_t)__float2int_rz(v) : 0u;
+  const float v = fminf(fmaxf(rintf(__fadd_rn(__fmul_rn(x, inv), zpf)), 0.0f), 255.0f);
+  return (uint32_t)__float2int_rz(v);
 }
 
-// The same code, also returning the clamped float value (needed by the
-// remainder of the two-term residual quantiser).
+// The same code, also returning the clamped float value (the conv's
+// remainder term uses it).  For a NaN input the reference keeps v = NaN while
+// this gives 0; the remainder is NaN either way (it subtracts from x).
 __device__ __forceinline__ uint32_t quant_code_v(float x, float inv, float zpf,
                                                  float& vout) {
-  float v = rintf(__fadd_rn(__fmul_rn(x, inv), zpf));
-  v = v < 0.0f ? 0.0f : v;
-  v = v > 255.0f ? 255.0f : v;
+  const float v = fminf(fmaxf(rintf(__fadd_rn(__fmul_rn(x, inv), zpf)), 0.0f), 255.0f);
   vout = v;
-  return (v == v) ? (uint32_t)__float2int_rz(v) : 0u;
+  return (uint32_t)__float2int_rz(v);
 }
 
-// Running min/max with the reference's strict comparisons: a NaN never
-// replaces the running value, -0.0 never replaces +0.0.
-__device__ __forceinline__ float run_lo(float v, float lo) { return v < lo ? v : lo; }
-__device__ __forceinline__ float run_hi(float v, float hi) { return v > hi ? v : hi; }
+// Running min/max of a row.  The reference updates with strict comparisons
+// (a NaN never replaces the running value, -0.0 never replaces +0.0).
+// fminf/fmaxf agree on NaN; they may keep -0.0 where the reference keeps
+// +0.0, which changes no output: the range enters only as hi - lo (equal for
+// either zero) and rint(-lo * inv) (a zero either way).
+__device__ __forceinline__ float run_lo(float v, float lo) { return fminf(v, lo); }
+__device__ __forceinline__ float run_hi(float v, float hi) { return fmaxf(v, hi); }
 
 __device__ __forceinline__ void warp_minmax(float& lo, float& hi) {
 #pragma unroll
