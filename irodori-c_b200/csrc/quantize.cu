@@ -1,11 +1,11 @@
 // quantize.cu — per-row activation quantisers and the weight quantiser.
 //
 // Activation rows (ops.c:321-348, ops.c:427-442, tests/bench_vnni_linear.c:
-// 82-101) are HBM-bound: one warp per row, the row held in registers as
-// float4 (coalesced 512-byte loads per warp instruction), a shuffle min/max,
-// then codes packed four per 32-bit store.  Rows that do not fit the
-// register path (K > 4096, K % 4 != 0 or unaligned pointers) take a generic
-// warp-per-row path that re-reads the row.
+// 82-101) are memory-bound: one 128-thread block per row, the row held in
+// registers as float4 (coalesced loads), a block min/max, then codes packed
+// four per 32-bit store.  Rows that do not fit the register path (K > 4096,
+// K % 4 != 0 or unaligned pointers) take a generic warp-per-row path that
+// re-reads the row.
 #include "quantize.cuh"
 
 namespace iro {
@@ -34,24 +34,51 @@ __device__ __forceinline__ uint32_t sym_code(float x, float s) {
   return (uint32_t)(v + 128);
 }
 
+// One 128-thread block per row: thread t holds float4 elements t, t+128, ...
+// (at most V of them) in registers.  The row range is reduced across the
+// block (warp shuffles, then four partials in shared memory).
+constexpr int kQThreads = 128;
+
+__device__ __forceinline__ void block_minmax(float& lo, float& hi, float* sm) {
+  warp_minmax(lo, hi);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // sm may still be read from a previous reduction
+  if (lane == 0) {
+    sm[2 * w] = lo;
+    sm[2 * w + 1] = hi;
+  }
+  __syncthreads();
+  lo = fminf(fminf(sm[0], sm[2]), fminf(sm[4], sm[6]));
+  hi = fmaxf(fmaxf(sm[1], sm[3]), fmaxf(sm[5], sm[7]));
+}
+
+__device__ __forceinline__ float block_max(float a, float* sm) {
+  a = warp_max(a);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) sm[w] = a;
+  __syncthreads();
+  return fmaxf(fmaxf(sm[0], sm[1]), fmaxf(sm[2], sm[3]));
+}
+
 template <int V, int MODE>
-__global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= a.M) return;
+__global__ void __launch_bounds__(kQThreads) quant_rows_vec(QuantArgs a) {
+  __shared__ float sm[8];
+  const int tid = threadIdx.x;
+  const int row = blockIdx.x;
   const int K4 = a.K >> 2;
   const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)row * a.K);
   float4 v[V];
 #pragma unroll
   for (int i = 0; i < V; i++) {
-    const int j = i * 32 + lane;
+    const int j = i * kQThreads + tid;
     v[i] = j < K4 ? __ldg(src + j) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (MODE == QM_SYM) {
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < V; i++) {
-      if (i * 32 + lane < K4) {
+      if (i * kQThreads + tid < K4) {
         float t;
         t = fabsf(v[i].x); amax = t > amax ? t : amax;
         t = fabsf(v[i].y); amax = t > amax ? t : amax;
@@ -59,17 +86,17 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
         t = fabsf(v[i].w); amax = t > amax ? t : amax;
       }
     }
-    amax = warp_max(amax);
+    amax = block_max(amax, sm);
     const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     uint32_t* dst = reinterpret_cast<uint32_t*>(a.q + (size_t)row * a.K);
 #pragma unroll
     for (int i = 0; i < V; i++) {
-      const int j = i * 32 + lane;
+      const int j = i * kQThreads + tid;
       if (j < K4)
         dst[j] = sym_code(v[i].x, s) | (sym_code(v[i].y, s) << 8) |
                  (sym_code(v[i].z, s) << 16) | (sym_code(v[i].w, s) << 24);
     }
-    if (lane == 0) {
+    if (tid == 0) {
       a.scale[row] = s;
       a.zero[row] = 128;
     }
@@ -78,14 +105,14 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
   float lo = 0.0f, hi = 0.0f;
 #pragma unroll
   for (int i = 0; i < V; i++) {
-    if (i * 32 + lane < K4) {
+    if (i * kQThreads + tid < K4) {
       lo = run_lo(v[i].x, lo); hi = run_hi(v[i].x, hi);
       lo = run_lo(v[i].y, lo); hi = run_hi(v[i].y, hi);
       lo = run_lo(v[i].z, lo); hi = run_hi(v[i].z, hi);
       lo = run_lo(v[i].w, lo); hi = run_hi(v[i].w, hi);
     }
   }
-  warp_minmax(lo, hi);
+  block_minmax(lo, hi, sm);
   float s, inv;
   int zp;
   row_params(lo, hi, s, inv, zp);
@@ -93,7 +120,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
   uint32_t* dst = reinterpret_cast<uint32_t*>(a.q + (size_t)row * a.K);
 #pragma unroll
   for (int i = 0; i < V; i++) {
-    const int j = i * 32 + lane;
+    const int j = i * kQThreads + tid;
     if (j < K4) {
       const uint32_t c0 = quant_code(v[i].x, inv, zpf), c1 = quant_code(v[i].y, inv, zpf);
       const uint32_t c2 = quant_code(v[i].z, inv, zpf), c3 = quant_code(v[i].w, inv, zpf);
@@ -107,7 +134,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
       }
     }
   }
-  if (lane == 0) {
+  if (tid == 0) {
     a.scale[row] = s;
     a.zero[row] = zp;
   }
@@ -116,7 +143,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
   float lo2 = 0.0f, hi2 = 0.0f;
 #pragma unroll
   for (int i = 0; i < V; i++) {
-    const int j = i * 32 + lane;
+    const int j = i * kQThreads + tid;
     if (j < K4) {
       if (rdst) rdst[j] = v[i];
       lo2 = run_lo(v[i].x, lo2); hi2 = run_hi(v[i].x, hi2);
@@ -125,7 +152,7 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
       lo2 = run_lo(v[i].w, lo2); hi2 = run_hi(v[i].w, hi2);
     }
   }
-  warp_minmax(lo2, hi2);
+  block_minmax(lo2, hi2, sm);
   float s2, inv2;
   int zp2;
   row_params(lo2, hi2, s2, inv2, zp2);
@@ -133,12 +160,12 @@ __global__ void __launch_bounds__(256) quant_rows_vec(QuantArgs a) {
   uint32_t* dst2 = reinterpret_cast<uint32_t*>(a.q2 + (size_t)row * a.K);
 #pragma unroll
   for (int i = 0; i < V; i++) {
-    const int j = i * 32 + lane;
+    const int j = i * kQThreads + tid;
     if (j < K4)
       dst2[j] = quant_code(v[i].x, inv2, zpf2) | (quant_code(v[i].y, inv2, zpf2) << 8) |
                 (quant_code(v[i].z, inv2, zpf2) << 16) | (quant_code(v[i].w, inv2, zpf2) << 24);
   }
-  if (lane == 0) {
+  if (tid == 0) {
     a.scale2[row] = s2;
     a.zero2[row] = zp2;
   }
@@ -220,14 +247,13 @@ static int launch_mode(const QuantArgs& a, cudaStream_t s) {
                         (((reinterpret_cast<uintptr_t>(a.q2) & 3u) == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.residual) & 15u) == 0)));
   const int K4 = a.K / 4;
-  if (aligned && K4 <= 32 * 32) {
-    if (K4 <= 32) quant_rows_vec<1, MODE><<<grid, block, 0, s>>>(a);
-    else if (K4 <= 64) quant_rows_vec<2, MODE><<<grid, block, 0, s>>>(a);
-    else if (K4 <= 128) quant_rows_vec<4, MODE><<<grid, block, 0, s>>>(a);
-    else if (K4 <= 256) quant_rows_vec<8, MODE><<<grid, block, 0, s>>>(a);
-    else if (K4 <= 512) quant_rows_vec<16, MODE><<<grid, block, 0, s>>>(a);
-    else if (K4 <= 768) quant_rows_vec<24, MODE><<<grid, block, 0, s>>>(a);
-    else quant_rows_vec<32, MODE><<<grid, block, 0, s>>>(a);
+  if (aligned && K4 <= 8 * kQThreads) {
+    const dim3 rg((unsigned)a.M), rb(kQThreads);
+    if (K4 <= 1 * kQThreads) quant_rows_vec<1, MODE><<<rg, rb, 0, s>>>(a);
+    else if (K4 <= 2 * kQThreads) quant_rows_vec<2, MODE><<<rg, rb, 0, s>>>(a);
+    else if (K4 <= 4 * kQThreads) quant_rows_vec<4, MODE><<<rg, rb, 0, s>>>(a);
+    else if (K4 <= 6 * kQThreads) quant_rows_vec<6, MODE><<<rg, rb, 0, s>>>(a);
+    else quant_rows_vec<8, MODE><<<rg, rb, 0, s>>>(a);
   } else {
     quant_rows_generic<MODE><<<grid, block, 0, s>>>(a);
   }
