@@ -521,6 +521,44 @@ def run_profile_case(args):
     print(f"profile case {args.profile}: {args.warmup + args.steps} launches ok")
 
 
+def run_conv7(args):
+    """the codec's int8 kernel-7 conv over 4 x 48000 frames,
+    512 -> 512 channels (device-resident; one JSON line)."""
+    import torch
+    import iro_b200 as iro
+    import oracle as oracle_mod
+
+    B, T, C, N, KW = 4, 48000, 512, 512, 7
+    iro.init(0)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
+    rng = np.random.default_rng(44)
+    inp = rng.standard_normal((B, T, C), dtype=np.float32) * np.float32(0.5)
+    w = rng.standard_normal((N, KW * C), dtype=np.float32) * np.float32(0.02)
+    bias = rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)
+    hw = iro.HostWeight(w)
+    dw = iro.DevWeight.upload(hw)
+    xd = iro.DevBuf.from_host(inp)
+    bd = iro.DevBuf.from_host(bias)
+    out = iro.DevBuf((B, T, N), np.float32)
+    for _ in range(args.warmup):
+        iro.conv1d_dev(xd, B, T, C, dw, KW, 1, 1, 3, bd, False, out)
+    iro.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        iro.conv1d_dev(xd, B, T, C, dw, KW, 1, 1, 3, bd, False, out)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ops = 2.0 * B * T * N * KW * C
+    print(json.dumps({"metric": "int8 conv7 TOPS", "value": round(ops / ms / 1e9, 2),
+                      "unit": "TOPS", "ms_per_step": round(ms, 4), "steps": args.steps,
+                      "config": {"workload": "cfg4 DACVAE int8 conv1d k7 [4,48000,512]->[4,48000,512]",
+                                 "ops_per_step": ops}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -529,6 +567,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", choices=["swiglu", "conv7"], default="swiglu",
+                    help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
     ap.add_argument("--profile", choices=["gated", "w2", "quant", "block"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
     args = ap.parse_args()
@@ -536,6 +576,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.profile:
         run_profile_case(args)
+    elif args.workload == "conv7" and args.impl == "ours":
+        run_conv7(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -14,6 +14,7 @@
 // codes [t, tap*C + c]) -> the tcgen05 GEMM against the [N, kernel*C] weight
 // (EPI_LINEAR, or EPI_DUAL for the two-term form).  Rows are processed in
 // chunks so the code buffer stays bounded.
+#include "conv_igemm.cuh"
 #include "gemm_i8.cuh"
 #include "quantize.cuh"
 
@@ -48,6 +49,32 @@ __global__ void __launch_bounds__(256) conv_row_range_kernel(const float* __rest
     lo_out[r] = lo;
     hi_out[r] = hi;
   }
+}
+
+// Per output row: the window range over its taps' input rows (dacvae.c:
+// 618-627) and the row parameters s, 1/s, zero point (ops.c:329-339 form).
+__global__ void __launch_bounds__(256) conv_row_params_kernel(
+    const float* __restrict__ rlo, const float* __restrict__ rhi, int batch, int T_in,
+    int T_out, int kernel, int stride, int dilation, int padding, float* __restrict__ scale,
+    int32_t* __restrict__ zero, float* __restrict__ inv_out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= batch * T_out) return;
+  const int b = i / T_out;
+  const int t = i - b * T_out;
+  const size_t base = (size_t)b * T_in;
+  float lo = 0.0f, hi = 0.0f;
+  for (int tap = 0; tap < kernel; tap++) {
+    const long long it = (long long)t * stride - padding + (long long)tap * dilation;
+    if (it < 0 || it >= T_in) continue;
+    lo = run_lo(rlo[base + it], lo);
+    hi = run_hi(rhi[base + it], hi);
+  }
+  float s, inv;
+  int zp;
+  row_params(lo, hi, s, inv, zp);
+  scale[i] = s;
+  zero[i] = zp;
+  inv_out[i] = inv;
 }
 
 struct PackArgs {
@@ -183,6 +210,21 @@ extern "C" int iro_int8_conv1d_dev(const float* input, int batch, int T_in, int 
   conv_row_range_kernel<<<cdiv((int)in_rows, 8), 256, 0, s>>>(input, (int)in_rows, C, rlo, rhi);
   st = check_launch();
   if (st) return st;
+  if (conv7_igemm_supported(C, w->N, kernel, stride, dilation, padding, residual, input, output)) {
+    // Implicit GEMM: row parameters for all output rows, then one launch.
+    float* sc_all = reinterpret_cast<float*>(cols);  // reuse the code buffer area
+    int32_t* zr_all = reinterpret_cast<int32_t*>(sc_all + total);
+    float* inv_all = reinterpret_cast<float*>(zr_all + total);
+    if ((size_t)3 * total * 4 > (size_t)chunk * ld) return IRO_ERR_UNSUPPORTED;
+    conv_row_params_kernel<<<cdiv(total, 256), 256, 0, s>>>(rlo, rhi, batch, T_in, T_out, kernel,
+                                                             stride, dilation, padding, sc_all,
+                                                             zr_all, inv_all);
+    st = check_launch();
+    if (st) return st;
+    st = conv7_igemm_launch(c, input, batch, T_in, C, w, kernel, dilation, padding, bias, sc_all,
+                            zr_all, inv_all, output, T_out, s);
+    return st ? st : T_out;
+  }
   for (int row0 = 0; row0 < total; row0 += chunk) {
     const int rows = total - row0 < chunk ? total - row0 : chunk;
     PackArgs a{input, rlo, rhi, T_in, C, T_out, kernel, stride, dilation, padding, row0, rows,

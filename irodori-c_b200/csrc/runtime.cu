@@ -187,6 +187,25 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
   return IRO_OK;
 }
 
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                CUtensorMapSwizzle swz) {
+  std::call_once(g_encode_once, load_encode);
+  if (!g_encode) return IRO_ERR_NO_DEVICE;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return IRO_ERR_UNSUPPORTED;
+  for (int i = 0; i + 1 < rank; i++)
+    if ((strides[i] & 15u) != 0) return IRO_ERR_UNSUPPORTED;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(map, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    fprintf(stderr, "irodori_b200: cuTensorMapEncodeTiled (rank %d) failed (%d)\n", rank, (int)r);
+    return IRO_ERR_UNSUPPORTED;
+  }
+  return IRO_OK;
+}
+
 int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                  uint64_t pitch, uint32_t box_inner, uint32_t box_rows) {
   return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, inner, rows, pitch, box_inner,

@@ -76,6 +76,12 @@ int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t ro
 int make_tmap_f32_sw128(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                         uint64_t pitch_bytes);
 
+// Generic tiled tensor map of rank 1..5: dims and box innermost first,
+// strides in bytes for dims 1..rank-1.
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                CUtensorMapSwizzle swz);
+
 // 2-D f32 tensor map without swizzle (for staging fp32 tiles).
 int make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                   uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_rows);

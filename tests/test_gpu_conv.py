@@ -63,7 +63,10 @@ def test_conv_matches_reference_fixture(idx):
 @pytest.mark.parametrize("B,T,C,N,d,stride,res", [
     (2, 300, 96, 64, 1, 1, False), (1, 250, 96, 40, 3, 1, True), (3, 90, 32, 24, 9, 1, True),
     (1, 200, 20, 16, 1, 2, False), (2, 500, 512, 512, 1, 1, False), (1, 160, 512, 512, 3, 1, True),
-    (1, 5, 64, 32, 1, 1, True)])
+    (1, 5, 64, 32, 1, 1, True),
+    # implicit-GEMM path (stride 1, 512 output channels, C a multiple of 64)
+    (1, 300, 64, 512, 1, 1, False), (3, 200, 128, 512, 9, 1, False), (2, 130, 64, 512, 3, 1, False),
+    (1, 7, 192, 512, 1, 1, False), (1, 1000, 256, 512, 1, 1, False)])
 def test_conv_matches_oracle(B, T, C, N, d, stride, res):
     rng = np.random.default_rng(B * 1000 + T + C + d)
     inp = (rng.standard_normal((B, T, C)) * 0.5).astype(np.float32)
