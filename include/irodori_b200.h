@@ -248,6 +248,21 @@ int iro_int8_swiglu_plan(IroPlan **plan, const float *x, int M, const IroInt8Dev
 int iro_plan_launch(const IroPlan *plan, void *stream);
 void iro_plan_free(IroPlan *plan);
 
+/* Host-buffer serving pipeline for the SwiGLU block.  A ring of `depth`
+   device slots (input, output, recorded block each); submit() copies x_host
+   in, runs the block and copies the result to out_host, all asynchronously,
+   so consecutive submissions overlap their host->device copy, compute and
+   device->host copy on three streams.  The host buffers must stay valid and
+   untouched until wait() returns; they should be page-locked for the copies
+   to overlap.  Same numerics as iro_int8_swiglu_dev. */
+typedef struct IroSwigluPipe IroSwigluPipe;
+int iro_int8_swiglu_pipe_create(IroSwigluPipe **pipe, int M, const IroInt8DevWeight *w13,
+                                const IroInt8DevWeight *w2, const float *b2, int residual_w2,
+                                int depth);
+int iro_int8_swiglu_pipe_submit(IroSwigluPipe *pipe, const float *x_host, float *out_host);
+int iro_int8_swiglu_pipe_wait(IroSwigluPipe *pipe);
+void iro_int8_swiglu_pipe_free(IroSwigluPipe *pipe);
+
 /* The SwiGLU block without allocation.  No counterpart in the reference.
    For callers that cannot allocate device memory where they run the block:
    code recording it into a CUDA graph under global-mode stream capture,

@@ -99,6 +99,10 @@ SIGNATURES = {
     "iro_int8_swiglu_plan": (_i, [C.POINTER(_vp), _vp, _i, _DW, _DW, _vp, _vp, _i]),
     "iro_plan_launch": (_i, [_vp, _vp]),
     "iro_plan_free": (None, [_vp]),
+    "iro_int8_swiglu_pipe_create": (_i, [C.POINTER(_vp), _i, _DW, _DW, _vp, _i, _i]),
+    "iro_int8_swiglu_pipe_submit": (_i, [_vp, _vp, _vp]),
+    "iro_int8_swiglu_pipe_wait": (_i, [_vp]),
+    "iro_int8_swiglu_pipe_free": (None, [_vp]),
     "iro_conv1d_out_len": (_i, [_i, _i, _i, _i, _i]),
     "iro_int8_conv1d_dev": (_i, [_vp, _i, _i, _i, _DW, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
@@ -469,6 +473,35 @@ class Plan:
     def free(self):
         if self.h:
             lib().iro_plan_free(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class SwigluPipe:
+    """Asynchronous host-buffer pipeline of the SwiGLU block."""
+
+    def __init__(self, M, w13: DevWeight, w2: DevWeight, b2=None, residual_w2=False, depth=3):
+        self.h = C.c_void_p()
+        check(lib().iro_int8_swiglu_pipe_create(C.byref(self.h), M, C.byref(w13.st),
+                                                C.byref(w2.st), _p(b2), int(bool(residual_w2)),
+                                                depth), "iro_int8_swiglu_pipe_create")
+        self._keep = (w13, w2, b2)
+
+    def submit(self, x_host, out_host):
+        check(lib().iro_int8_swiglu_pipe_submit(self.h, _p(x_host), _p(out_host)),
+              "iro_int8_swiglu_pipe_submit")
+
+    def wait(self):
+        check(lib().iro_int8_swiglu_pipe_wait(self.h), "iro_int8_swiglu_pipe_wait")
+
+    def free(self):
+        if self.h:
+            lib().iro_int8_swiglu_pipe_free(self.h)
             self.h = C.c_void_p()
 
     def __del__(self):
