@@ -251,31 +251,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t aph = 0;
     int pbuf = 0;
+    // Per-tile parameters: one output column per thread (colsum, scale,
+    // bias) and one row per lane (scale, zero point).  They are fetched into
+    // registers one tile ahead, so their global-load latency overlaps the
+    // previous tile's epilogue instead of delaying this one.
+    static_assert(BN <= 32 * kEpiWarps, "one staged column per epilogue thread");
+    struct Prefetch {
+      int cs;
+      float sw, b, sx, sx2;
+      int zp, zp2;
+    } pf;
+    auto fetch = [&](int t) {
+      const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+      const int n = nb * BN + et;
+      const bool ok = et < BN && n < p.N;
+      pf.cs = ok ? __ldg(p.wcolsum + n) : 0;
+      pf.sw = ok ? __ldg(p.wscale + n) : 0.0f;
+      pf.b = (ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      const int r = mb * BM + quad * 32 + lane;
+      const bool rok = r < p.M;
+      pf.sx = rok ? __ldg(p.sx + r) : 0.0f;
+      pf.zp = rok ? __ldg(p.zp + r) : 0;
+      pf.sx2 = (EPI == EPI_DUAL && rok) ? __ldg(p.sx2 + r) : 0.0f;
+      pf.zp2 = (EPI == EPI_DUAL && rok) ? __ldg(p.zp2 + r) : 0;
+    };
+    if ((int)blockIdx.x < p.num_tiles) fetch(blockIdx.x);
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
-      // Stage this tile's per-column parameters (overlaps the MMA).
+      // Stage this tile's per-column parameters (the buffer was last read by
+      // the tile before the previous one, which every warp has finished).
       float* pc = prm + pbuf * 3 * BN;
       int* p_cs = reinterpret_cast<int*>(pc);
       float* p_sw = pc + BN;
       float* p_b = pc + 2 * BN;
-      for (int j = et; j < BN; j += 32 * kEpiWarps) {
-        const int n = nb * BN + j;
-        const bool ok = n < p.N;
-        p_cs[j] = ok ? __ldg(p.wcolsum + n) : 0;
-        p_sw[j] = ok ? __ldg(p.wscale + n) : 0.0f;
-        p_b[j] = (ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      if (et < BN) {
+        p_cs[et] = pf.cs;
+        p_sw[et] = pf.sw;
+        p_b[et] = pf.b;
       }
       const int row0 = mb * BM + quad * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
-      const float sx = row_ok ? __ldg(p.sx + row) : 0.0f;
-      const int zp = row_ok ? __ldg(p.zp + row) : 0;
-      float sx2 = 0.0f;
-      int zp2 = 0;
-      if (EPI == EPI_DUAL && row_ok) {
-        sx2 = __ldg(p.sx2 + row);
-        zp2 = __ldg(p.zp2 + row);
-      }
+      const float sx = pf.sx;
+      const int zp = pf.zp;
+      const float sx2 = pf.sx2;
+      const int zp2 = pf.zp2;
+      if (tile + (int)gridDim.x < p.num_tiles) fetch(tile + (int)gridDim.x);
       // The vote doubles as the barrier that publishes the staged parameters;
       // if any warp's bounded wait gave up, all epilogue warps stop together.
       const bool got = mbar_wait_bounded(&tfull[acc], aph, p.err, 4, abort_flag, p.limit_ns);
@@ -319,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x16(tbase + c0, r1);
           tmem_ld_32x32b_x16(tbase + HALF + c0, r3);
           tmem_ld_wait();
-          float v[kChunk];
+          float a1[kChunk], a3[kChunk];
 #pragma unroll
           for (int i = 0; i < kChunk / 4; i++) {
             const int c1 = c0 + 4 * i, c3 = HALF + c0 + 4 * i;
@@ -331,19 +352,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             float2 a1hi = dequant2(r1[4 * i + 2], r1[4 * i + 3], zp, cs1.z, cs1.w, sx, sw1.z, sw1.w);
             float2 a3lo = dequant2(r3[4 * i], r3[4 * i + 1], zp, cs3.x, cs3.y, sx, sw3.x, sw3.y);
             float2 a3hi = dequant2(r3[4 * i + 2], r3[4 * i + 3], zp, cs3.z, cs3.w, sx, sw3.z, sw3.w);
-            if (p.bias) {
-              const float4 b1 = *reinterpret_cast<const float4*>(p_b + c1);
-              const float4 b3 = *reinterpret_cast<const float4*>(p_b + c3);
-              a1lo = add2_rn(a1lo, make_float2(b1.x, b1.y));
-              a1hi = add2_rn(a1hi, make_float2(b1.z, b1.w));
-              a3lo = add2_rn(a3lo, make_float2(b3.x, b3.y));
-              a3hi = add2_rn(a3hi, make_float2(b3.z, b3.w));
-            }
-            v[4 * i] = silu_gate(a1lo.x, a3lo.x);
-            v[4 * i + 1] = silu_gate(a1lo.y, a3lo.y);
-            v[4 * i + 2] = silu_gate(a1hi.x, a3hi.x);
-            v[4 * i + 3] = silu_gate(a1hi.y, a3hi.y);
+            // Without a bias the staged bias is +0, and x + 0 == x here: a
+            // dequantised value is never -0 (an int converts to +0 and the
+            // scales are positive), so no branch is needed.
+            const float4 b1 = *reinterpret_cast<const float4*>(p_b + c1);
+            const float4 b3 = *reinterpret_cast<const float4*>(p_b + c3);
+            a1lo = add2_rn(a1lo, make_float2(b1.x, b1.y));
+            a1hi = add2_rn(a1hi, make_float2(b1.z, b1.w));
+            a3lo = add2_rn(a3lo, make_float2(b3.x, b3.y));
+            a3hi = add2_rn(a3hi, make_float2(b3.z, b3.w));
+            a1[4 * i] = a1lo.x;
+            a1[4 * i + 1] = a1lo.y;
+            a1[4 * i + 2] = a1hi.x;
+            a1[4 * i + 3] = a1hi.y;
+            a3[4 * i] = a3lo.x;
+            a3[4 * i + 1] = a3lo.y;
+            a3[4 * i + 2] = a3hi.x;
+            a3[4 * i + 3] = a3hi.y;
           }
+          float v[kChunk];
+          silu_gate_chunk(a1, a3, v);
           emit(v, &tmO.m[0], h0, p.H, p.hidden + (size_t)row * p.ldh + h0);
         }
       } else {

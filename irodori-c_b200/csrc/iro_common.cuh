@@ -128,27 +128,44 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
   return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
 }
 
-// a / d for d >= 1 (d may be +inf), the silu denominator.  Markstein's
-// method: an approximate reciprocal r, the quotient q0 = a*r, the exact
-// residual a - q0*d from one FMA, and one correction q0 + residual*r; this
-// lands within half an ulp of a/d except when a/d lies within ~2^-23 ulp of a
-// rounding boundary.  For d >= 2^126 (including +inf) the flushed reciprocal
-// is unusable and the rarely taken branch divides exactly.
-__device__ __forceinline__ float div_ge1(float a, float d) {
-  if (d >= 8.5070592e37f) return __fdiv_rn(a, d);  // 2^126
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
-  const float q0 = __fmul_rn(a, r);
-  const float e = __fmaf_rn(-q0, d, a);
-  return __fmaf_rn(e, r, q0);
-}
-
 // silu(a) * g as the reference writes it, (a / (1 + expf(-a))) * g
-// (ops.c:781-784), with expf from the CUDA math library (a faster
-// hardware-ex2 exponential was tried and moved the hidden up to 5 ulp from
-// the host libm, enough to flip requantisation codes).
-__device__ __forceinline__ float silu_gate(float a, float g) {
-  return __fmul_rn(div_ge1(a, __fadd_rn(1.0f, expf(-a))), g);
+// (ops.c:781-784), for the N outputs one lane holds in an epilogue chunk.
+// expf is the CUDA math library's (a faster hardware-ex2 exponential was
+// tried and moved the hidden up to 5 ulp from the host libm, enough to flip
+// requantisation codes).
+//
+// The quotient a / d (d = 1 + expf(-a) >= 1) uses Markstein's method: an
+// approximate reciprocal r, q0 = a*r, the exact residual a - q0*d from one
+// FMA, and one correction q0 + residual*r.  That lands within half an ulp of
+// a/d except when a/d lies within ~2^-23 ulp of a rounding boundary, and it
+// needs d < 2^126 (the flushed reciprocal vanishes above) and a != +inf.
+// One warp vote per chunk sends the rare chunks outside that range
+// (a <= -87 or a = +inf) to the exactly rounded division, so the common path
+// has no per-output branch or select and the chunk's outputs schedule
+// together.  NaN inputs take the fast path and stay NaN.
+template <int N>
+__device__ __forceinline__ void silu_gate_chunk(const float (&a)[N], const float (&g)[N],
+                                                float (&out)[N]) {
+  float d[N];
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < N; j++) {
+    d[j] = __fadd_rn(1.0f, expf(-a[j]));
+    m = fmaxf(m, fmaxf(d[j], a[j]));
+  }
+  if (__any_sync(0xffffffffu, m >= 8.5070592e37f)) {  // 2^126
+#pragma unroll
+    for (int j = 0; j < N; j++) out[j] = __fmul_rn(__fdiv_rn(a[j], d[j]), g[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+      float r;
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d[j]));
+      const float q0 = __fmul_rn(a[j], r);
+      const float e = __fmaf_rn(-q0, d[j], a[j]);
+      out[j] = __fmul_rn(__fmaf_rn(e, r, q0), g[j]);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -490,6 +490,110 @@ int oracle_swiglu(const float *x, int M, int D, int H,
     return ok ? 0 : -1;
 }
 
+/* dacvae.c:350-358. */
+int oracle_convtranspose1d_out_len(int T_in, int kernel, int stride,
+                                   int padding, int output_padding) {
+    if (T_in <= 0 || stride <= 0 || kernel <= 0) return -1;
+    long long out = (long long)(T_in - 1) * stride - 2LL * padding + kernel +
+                    output_padding;
+    return out <= 0 || out > 0x7fffffff ? -1 : (int)out;
+}
+
+/* The codec's W8A8 transposed convolution, dacvae.c:696-790 with the int8
+   weight and no snake (alpha = NULL):
+   - every output row starts as the bias (dacvae.c:707-709);
+   - the input rows [T_in, C_in] are quantised per row (asymmetric, or the
+     two-term residual form when `residual`, dacvae.c:748-772);
+   - expanded[r, tap*C_out + c] = linear(q, W) without bias, plus the second
+     term accumulated (dacvae.c:766-767);
+   - expanded row r, tap t is added onto output row r*stride - padding + t
+     when that row exists (dacvae.c:776-787).
+   The reference walks the input in blocks of rows_cap rows; each output
+   element receives its additions in increasing input-row order either way,
+   so the unblocked loop below gives identical sums.  W is [kernel*C_out,
+   C_in] (dacvae.h:47-52).  Returns T_out or -1. */
+int oracle_convtranspose1d_int8(const float *input, int T_in, int C_in,
+                                int C_out, const int8_t *wdata,
+                                const float *wscale, const int32_t *wcolsum,
+                                int kernel, int stride, int padding,
+                                int output_padding, const float *bias,
+                                int residual, float *output) {
+    int T_out = oracle_convtranspose1d_out_len(T_in, kernel, stride, padding,
+                                               output_padding);
+    if (T_out <= 0 || C_in <= 0 || C_out <= 0) return -1;
+    const int N = kernel * C_out;
+    for (int t = 0; t < T_out; t++)
+        for (int c = 0; c < C_out; c++)
+            output[(size_t)t * C_out + c] = bias ? bias[c] : 0.0f;
+    size_t mk = (size_t)T_in * C_in, mn = (size_t)T_in * N;
+    uint8_t *q = (uint8_t *)malloc(mk), *q2 = (uint8_t *)malloc(mk);
+    float *s = (float *)malloc(sizeof(float) * T_in);
+    float *s2 = (float *)malloc(sizeof(float) * T_in);
+    int32_t *z = (int32_t *)malloc(sizeof(int32_t) * T_in);
+    int32_t *z2 = (int32_t *)malloc(sizeof(int32_t) * T_in);
+    float *rem = residual ? (float *)malloc(sizeof(float) * mk) : NULL;
+    float *e = (float *)malloc(sizeof(float) * mn);
+    int32_t *work = (int32_t *)malloc(sizeof(int32_t) * mn);
+    int ok = q && q2 && s && s2 && z && z2 && e && work && (!residual || rem);
+    if (ok) {
+        if (residual) {
+            oracle_quantize_rows_residual(input, T_in, C_in, q, s, z, rem, q2, s2, z2);
+            oracle_linear_ex(q, s, z, wdata, wscale, wcolsum, N, C_in, NULL, e, T_in, work, 0);
+            oracle_linear_ex(q2, s2, z2, wdata, wscale, wcolsum, N, C_in, NULL, e, T_in, work, 1);
+        } else {
+            oracle_quantize_rows(input, T_in, C_in, q, s, z);
+            oracle_linear_ex(q, s, z, wdata, wscale, wcolsum, N, C_in, NULL, e, T_in, work, 0);
+        }
+        for (int r = 0; r < T_in; r++) {
+            long long base = (long long)r * stride - padding;
+            for (int tap = 0; tap < kernel; tap++) {
+                long long ot = base + tap;
+                if (ot < 0 || ot >= T_out) continue;
+                const float *src = e + (size_t)r * N + (size_t)tap * C_out;
+                float *dst = output + (size_t)ot * C_out;
+                for (int c = 0; c < C_out; c++) dst[c] += src[c];
+            }
+        }
+    }
+    free(q); free(q2); free(s); free(s2); free(z); free(z2); free(rem);
+    free(e); free(work);
+    return ok ? T_out : -1;
+}
+
+/* The residual unit's skip + 1x1 projection, dacvae.c:979-1009: output
+   starts as the skip input (dacvae.c:983); the hidden rows are quantised
+   (two-term residual form when `residual`) and the projection is
+   accumulated onto it, the first term with the bias, the second without
+   (dacvae.c:1002-1008). */
+int oracle_codec_conv1(const float *hidden, int rows, int C,
+                       const int8_t *wdata, const float *wscale,
+                       const int32_t *wcolsum, const float *bias,
+                       const float *skip, int residual, float *output) {
+    if (rows <= 0 || C <= 0) return -1;
+    size_t n = (size_t)rows * C;
+    memcpy(output, skip, sizeof(float) * n);
+    uint8_t *q = (uint8_t *)malloc(n), *q2 = (uint8_t *)malloc(n);
+    float *s = (float *)malloc(sizeof(float) * rows);
+    float *s2 = (float *)malloc(sizeof(float) * rows);
+    int32_t *z = (int32_t *)malloc(sizeof(int32_t) * rows);
+    int32_t *z2 = (int32_t *)malloc(sizeof(int32_t) * rows);
+    float *rem = residual ? (float *)malloc(sizeof(float) * n) : NULL;
+    int32_t *work = (int32_t *)malloc(sizeof(int32_t) * n);
+    int ok = q && q2 && s && s2 && z && z2 && work && (!residual || rem);
+    if (ok) {
+        if (residual) {
+            oracle_quantize_rows_residual(hidden, rows, C, q, s, z, rem, q2, s2, z2);
+            oracle_linear_ex(q, s, z, wdata, wscale, wcolsum, C, C, bias, output, rows, work, 1);
+            oracle_linear_ex(q2, s2, z2, wdata, wscale, wcolsum, C, C, NULL, output, rows, work, 1);
+        } else {
+            oracle_quantize_rows(hidden, rows, C, q, s, z);
+            oracle_linear_ex(q, s, z, wdata, wscale, wcolsum, C, C, bias, output, rows, work, 1);
+        }
+    }
+    free(q); free(q2); free(s); free(s2); free(z); free(z2); free(rem); free(work);
+    return ok ? 0 : -1;
+}
+
 /* ops.c:375-398 — operands whose 255*127 products overflow int16. */
 void oracle_selfcheck_case(uint8_t a[3 * 64], int8_t b[5 * 64],
                            int32_t want[3 * 5]) {

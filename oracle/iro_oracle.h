@@ -89,6 +89,26 @@ int oracle_swiglu(const float *x, int M, int D, int H,
                   const float *b2,
                   int residual_w2, float *out, float *hidden_out);
 
+/* The codec's W8A8 transposed convolution (dacvae.c:696-790, no snake):
+   input [T_in, C_in], W [kernel*C_out, C_in] (tap-major rows), output
+   [T_out, C_out] = bias + scatter-add of the per-row linear outputs.
+   Returns T_out or -1. */
+int oracle_convtranspose1d_out_len(int T_in, int kernel, int stride,
+                                   int padding, int output_padding);
+int oracle_convtranspose1d_int8(const float *input, int T_in, int C_in,
+                                int C_out, const int8_t *wdata,
+                                const float *wscale, const int32_t *wcolsum,
+                                int kernel, int stride, int padding,
+                                int output_padding, const float *bias,
+                                int residual, float *output);
+
+/* The residual unit's skip + int8 1x1 projection (dacvae.c:979-1009):
+   output = skip + linear(quant(hidden)) [+ second residual term]. */
+int oracle_codec_conv1(const float *hidden, int rows, int C,
+                       const int8_t *wdata, const float *wscale,
+                       const int32_t *wcolsum, const float *bias,
+                       const float *skip, int residual, float *output);
+
 /* iro_int8_selfcheck's extreme-value probe (ops.c:375-398): fills the fixed
    3x5x64 operands and the expected sums. */
 void oracle_selfcheck_case(uint8_t a[3 * 64], int8_t b[5 * 64],

@@ -73,6 +73,15 @@ def lib():
         L.oracle_swiglu.restype = C.c_int
         L.oracle_selfcheck_case.argtypes = [_vp, _vp, _vp]
         L.oracle_selfcheck_case.restype = None
+        L.oracle_convtranspose1d_out_len.argtypes = [C.c_int] * 5
+        L.oracle_convtranspose1d_out_len.restype = C.c_int
+        L.oracle_convtranspose1d_int8.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp,
+                                                  C.c_int, C.c_int, C.c_int, C.c_int, _vp,
+                                                  C.c_int, _vp]
+        L.oracle_convtranspose1d_int8.restype = C.c_int
+        L.oracle_codec_conv1.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp,
+                                         C.c_int, _vp]
+        L.oracle_codec_conv1.restype = C.c_int
         _lib = L
     return _lib
 
@@ -269,6 +278,46 @@ def _bind_ops(L):
     return L
 
 
+def convtranspose1d_out_len(T_in, kernel, stride, padding, output_padding=0):
+    return lib().oracle_convtranspose1d_out_len(T_in, kernel, stride, padding, output_padding)
+
+
+def convtranspose1d_int8(inp, w: Weight, C_out, kernel, stride, padding, output_padding=0,
+                         bias=None, residual=False):
+    """inp: time-major [T_in, C_in]; w: [kernel*C_out, C_in].  Returns [T_out, C_out]."""
+    inp = _c(inp, np.float32)
+    T_in, Cin = inp.shape
+    T_out = convtranspose1d_out_len(T_in, kernel, stride, padding, output_padding)
+    if T_out <= 0 or w.N != kernel * C_out or w.K != Cin:
+        raise ValueError("bad transposed-convolution shape")
+    out = np.empty((T_out, C_out), np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    rc = lib().oracle_convtranspose1d_int8(_ptr(inp), T_in, Cin, C_out, _ptr(w.data),
+                                           _ptr(w.scale), _ptr(w.colsum), kernel, stride,
+                                           padding, output_padding, _ptr(b),
+                                           int(bool(residual)), _ptr(out))
+    if rc != T_out:
+        raise RuntimeError("oracle transposed conv failed")
+    return out
+
+
+def codec_conv1(hidden, w: Weight, bias, skip, residual=False):
+    """Residual unit's skip + 1x1 projection: skip + linear(quant(hidden))."""
+    hidden = _c(hidden, np.float32)
+    skip = _c(skip, np.float32)
+    rows, Cc = hidden.shape
+    if w.N != Cc or w.K != Cc or skip.shape != hidden.shape:
+        raise ValueError("bad conv1 shape")
+    out = np.empty_like(hidden)
+    b = None if bias is None else _c(bias, np.float32)
+    rc = lib().oracle_codec_conv1(_ptr(hidden), rows, Cc, _ptr(w.data), _ptr(w.scale),
+                                  _ptr(w.colsum), _ptr(b), _ptr(skip), int(bool(residual)),
+                                  _ptr(out))
+    if rc != 0:
+        raise RuntimeError("oracle conv1 failed")
+    return out
+
+
 def ref_lib(kind="ieee"):
     """kind: "ieee" (parity build), "codec", "dit", "vnni", or "fast" (product flags,
     variant chosen for this host's ISA)."""
@@ -286,6 +335,14 @@ def ref_lib(kind="ieee"):
             L.ref_conv1d_int8_forward.restype = C.c_int
             L.ref_conv1d_output_length.argtypes = [C.c_int] * 5
             L.ref_conv1d_output_length.restype = C.c_int
+            L.ref_convtranspose1d_int8_forward.argtypes = [_vp, C.c_int, C.c_int, C.c_int, _vp,
+                                                           _vp, _vp, C.c_int, C.c_int, C.c_int,
+                                                           C.c_int, _vp, _vp]
+            L.ref_convtranspose1d_int8_forward.restype = C.c_int
+            L.ref_convtranspose1d_output_length.argtypes = [C.c_int] * 5
+            L.ref_convtranspose1d_output_length.restype = C.c_int
+            L.ref_codec_upsample_residual.argtypes = []
+            L.ref_codec_upsample_residual.restype = C.c_int
         if kind == "dit":
             L.ref_dit_swiglu_int8.argtypes = [_vp, C.c_int] + [_vp] * 10
             L.ref_dit_swiglu_int8.restype = C.c_int
@@ -405,6 +462,29 @@ def ref_conv1d_int8(inp, w: Weight, kernel, stride=1, dilation=1, padding=0, bia
     if rc != 0:
         raise RuntimeError("reference conv failed")
     return out
+
+
+def ref_convtranspose1d_int8(inp, w: Weight, C_out, kernel, stride, padding, output_padding=0,
+                             bias=None):
+    """The reference's own transposed conv (dacvae.c:696-790).  Whether it adds
+    the second term is the reference's process-wide policy: see
+    ref_codec_upsample_residual()."""
+    L = ref_lib("codec")
+    inp = _c(inp, np.float32)
+    T_in, Cin = inp.shape
+    T_out = L.ref_convtranspose1d_output_length(T_in, kernel, stride, padding, output_padding)
+    out = np.empty((T_out, C_out), np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    rc = L.ref_convtranspose1d_int8_forward(_ptr(inp), T_in, Cin, C_out, _ptr(w.data),
+                                            _ptr(w.scale), _ptr(w.colsum), kernel, stride,
+                                            padding, output_padding, _ptr(b), _ptr(out))
+    if rc != 0:
+        raise RuntimeError("reference transposed conv failed")
+    return out
+
+
+def ref_codec_upsample_residual():
+    return bool(ref_lib("codec").ref_codec_upsample_residual())
 
 
 def ref_dit_dims():
