@@ -295,6 +295,34 @@ int iro_int8_conv1d_dev(const float *input, int batch, int T_in, int C,
                         int dilation, int padding, const float *bias,
                         int residual, float *output, void *stream);
 
+/* dacvae.c:696-790 (int8 weight, no snake): W8A8 transposed (upsampling)
+   convolution over `batch` independent time-major inputs [batch, T_in, C_in].
+   W is [kernel*C_out, C_in] with row tap*C_out + c (dacvae.h:47-52); output
+   [batch, T_out, C_out] = bias (or 0) plus, for every input row r and tap t,
+   linear(quant(x_r))[t*C_out .. +C_out] added onto output row
+   r*stride - padding + t, each output element's additions in increasing r
+   (the reference's order).  residual adds the two-term quantisation's second
+   linear (dacvae.c:748-767).  The decoder uses kernel = 2*stride, padding =
+   (stride+1)/2, output_padding = stride&1 (dacvae.c:150-160).  C_in must be a
+   multiple of 16.  Returns T_out (> 0) or IRO_ERR_*.  The length follows
+   iro_convtranspose1d_output_length (dacvae.c:350-358). */
+int iro_convtranspose1d_out_len(int T_in, int kernel, int stride, int padding,
+                                int output_padding);
+int iro_int8_convtranspose1d_dev(const float *input, int batch, int T_in, int C_in,
+                                 const IroInt8DevWeight *w, int C_out, int kernel,
+                                 int stride, int padding, int output_padding,
+                                 const float *bias, int residual, float *output,
+                                 void *stream);
+
+/* dacvae.c:979-1009: the residual unit's skip connection plus int8 1x1
+   projection, output[rows, C] = skip + (linear(quant(hidden)) + bias)
+   [+ linear of the residual term, without bias], each addition rounded in
+   the reference's order.  W is [C, C] (w->N == w->K == C, a multiple of 16).
+   skip may equal output (in place).  Returns IRO_OK or IRO_ERR_*. */
+int iro_int8_codec_conv1_dev(const float *hidden, int rows, const IroInt8DevWeight *w,
+                             const float *bias, const float *skip, int residual,
+                             float *output, void *stream);
+
 /* Failure detection ------------------------------------------------------------- */
 
 /* Launches one block that waits on a device barrier nothing ever completes,

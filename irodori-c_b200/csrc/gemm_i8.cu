@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* drow = base + (size_t)row * ld + col0;
           const int valid = ncols - col0;
           float v[kChunk];
-          if (EPI == EPI_LINEAR && p.accumulate) {
+          if ((EPI == EPI_LINEAR || EPI == EPI_DUAL) && p.accumulate) {
 #pragma unroll
             for (int j = 0; j < kChunk; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
           }
@@ -413,6 +413,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               hi = add2_rn(hi, make_float2(b.z, b.w));
             }
             if (EPI == EPI_DUAL) {
+              // Two accumulating linears in the reference's order:
+              // y = (y + (d1 + bias)) + d2 (ops.c:473-481 applied twice).
+              if (p.accumulate) {
+                lo = add2_rn(make_float2(v[4 * i], v[4 * i + 1]), lo);
+                hi = add2_rn(make_float2(v[4 * i + 2], v[4 * i + 3]), hi);
+              }
               lo = add2_rn(lo, dequant2(r2[4 * i], r2[4 * i + 1], zp2, cs.x, cs.y, sx2, sw.x, sw.y));
               hi = add2_rn(hi, dequant2(r2[4 * i + 2], r2[4 * i + 3], zp2, cs.z, cs.w, sx2, sw.z, sw.w));
             }

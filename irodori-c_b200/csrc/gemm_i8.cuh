@@ -9,7 +9,8 @@ enum EpiKind {
   EPI_LINEAR = 0,  // y (=|+=) dequant (+bias); optional raw s32 sums
   EPI_SPLIT = 1,   // as LINEAR, column block g written to outs[g]
   EPI_GATED = 2,   // hidden = silu(dequant W1 + b1) * (dequant W3 + b3)
-  EPI_DUAL = 3     // y = (dequant(q1) + bias) + dequant(q2)
+  EPI_DUAL = 3     // y = (dequant(q1) + bias) + dequant(q2); with accumulate
+                   // y = (y + (dequant(q1) + bias)) + dequant(q2)
 };
 
 // One GEMM request: A (u8 codes, rows of `lda` bytes, K valid) against the

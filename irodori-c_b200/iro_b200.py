@@ -105,6 +105,10 @@ SIGNATURES = {
     "iro_int8_swiglu_pipe_free": (None, [_vp]),
     "iro_conv1d_out_len": (_i, [_i, _i, _i, _i, _i]),
     "iro_int8_conv1d_dev": (_i, [_vp, _i, _i, _i, _DW, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
+    "iro_convtranspose1d_out_len": (_i, [_i, _i, _i, _i, _i]),
+    "iro_int8_convtranspose1d_dev": (_i, [_vp, _i, _i, _i, _DW, _i, _i, _i, _i, _i, _vp, _i,
+                                          _vp, _vp]),
+    "iro_int8_codec_conv1_dev": (_i, [_vp, _i, _DW, _vp, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
 }
 
@@ -522,6 +526,26 @@ def conv1d_dev(inp, batch, T_in, Cin, w: DevWeight, kernel, stride, dilation, pa
     if rc < 0:
         raise IroError(rc, "conv1d_dev")
     return rc
+
+
+def convtranspose1d_out_len(T_in, kernel, stride, padding, output_padding=0):
+    return lib().iro_convtranspose1d_out_len(T_in, kernel, stride, padding, output_padding)
+
+
+def convtranspose1d_dev(inp, batch, T_in, Cin, w: DevWeight, C_out, kernel, stride, padding,
+                        output_padding, bias, residual, out, stream=None):
+    rc = lib().iro_int8_convtranspose1d_dev(_p(inp), batch, T_in, Cin, C.byref(w.st), C_out,
+                                            kernel, stride, padding, output_padding, _p(bias),
+                                            int(bool(residual)), _p(out), stream)
+    if rc < 0:
+        raise IroError(rc, "convtranspose1d_dev")
+    return rc
+
+
+def codec_conv1_dev(hidden, rows, w: DevWeight, bias, skip, residual, out, stream=None):
+    check(lib().iro_int8_codec_conv1_dev(_p(hidden), rows, C.byref(w.st), _p(bias), _p(skip),
+                                          int(bool(residual)), _p(out), stream),
+           "codec_conv1_dev")
 
 
 def header_symbols(path=HEADER_PATH):

@@ -76,6 +76,43 @@ def conv_cases():
     return out
 
 
+CONVT_KEYS = ("T", "C_in", "C_out", "kernel", "stride", "padding", "output_padding", "bias")
+
+
+def convt_cases():
+    """Transposed-conv cases: the decoder's geometry (kernel 2*stride,
+    padding (stride+1)/2, output_padding stride&1, dacvae.c:150-160) at
+    strides 2, 3, 8 and 12, plus one free geometry.  The reference always
+    has a bias here (it copies conv->bias into every output row)."""
+    cases = []
+    for (T, ci, co, s, b) in ((40, 32, 16, 2, 1), (25, 48, 24, 3, 1), (30, 64, 8, 8, 1),
+                              (9, 32, 16, 12, 1)):
+        cases.append(dict(T=T, C_in=ci, C_out=co, kernel=2 * s, stride=s, padding=(s + 1) // 2,
+                          output_padding=s & 1, bias=b))
+    cases.append(dict(T=21, C_in=16, C_out=12, kernel=5, stride=2, padding=0, output_padding=2,
+                      bias=1))
+    out = []
+    for i, c in enumerate(cases):
+        rng = np.random.default_rng(300 + i)
+        inp = (rng.standard_normal((c["T"], c["C_in"])) * 0.5).astype(np.float32)
+        inp[min(4, c["T"] - 1)] = 0.0
+        w = (rng.standard_normal((c["kernel"] * c["C_out"], c["C_in"])) * 0.05).astype(np.float32)
+        bias = (rng.standard_normal(c["C_out"]) * 0.01).astype(np.float32) if c["bias"] else None
+        out.append((c, inp, w, bias))
+    return out
+
+
+def conv1_case():
+    rng = np.random.default_rng(400)
+    rows, C = 70, 48
+    hidden = rng.standard_normal((rows, C)).astype(np.float32)
+    hidden[3] = 0.0
+    skip = (rng.standard_normal((rows, C)) * 0.3).astype(np.float32)
+    w = (rng.standard_normal((C, C)) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    return hidden, skip, w, bias
+
+
 def sym_input():
     rng = np.random.default_rng(77)
     x = rng.standard_normal((40, 96)).astype(np.float32)

@@ -114,12 +114,67 @@ def dit_swiglu():
     return out
 
 
+def convt_child(mode):
+    """Child process: the reference's upsample residual policy is read once
+    per process from IRO_CODEC_INT8_RESIDUAL (dacvae.c:54-61)."""
+    want = mode == "two_term"
+    assert oracle.ref_codec_upsample_residual() == want
+    res = {}
+    for idx, (case, inp, w, bias) in enumerate(inputs.convt_cases()):
+        W = oracle.ref_weight_quantize(w)
+        res[f"c{idx}"] = oracle.ref_convtranspose1d_int8(
+            inp, W, case["C_out"], case["kernel"], case["stride"], case["padding"],
+            case["output_padding"], bias)
+    np.savez(os.path.join(HERE, f"_tmp_convt_{mode}.npz"), **res)
+
+
+def convt():
+    out = {}
+    for mode, env in (("single", "0"), ("two_term", "2")):
+        e = dict(os.environ)
+        e["IRO_CODEC_INT8_RESIDUAL"] = env
+        subprocess.run([sys.executable, __file__, "--convt-child", mode], check=True, env=e)
+        path = os.path.join(HERE, f"_tmp_convt_{mode}.npz")
+        got = np.load(path)
+        for k in got.files:
+            out[f"{k}_{mode}"] = got[k]
+        os.remove(path)
+    for idx, (case, inp, w, bias) in enumerate(inputs.convt_cases()):
+        W = oracle.ref_weight_quantize(w)
+        pre = f"c{idx}_"
+        out.update({pre + "params": np.array([case[k] for k in inputs.CONVT_KEYS], np.int32),
+                    pre + "inputs_sha": np.frombuffer(inputs.sha(inp, w, bias), np.uint8),
+                    pre + "wdata": W.data, pre + "wscale": W.scale, pre + "wcolsum": W.colsum})
+    return out
+
+
+def conv1():
+    """dacvae.c:983-1008 is the skip copy plus these ops.c calls."""
+    hidden, skip, w, bias = inputs.conv1_case()
+    W = oracle.ref_weight_quantize(w)
+    q, s, z = oracle.ref_quantize_rows(hidden)
+    y1, _ = oracle.ref_linear_ex(q, s, z, W, bias, y=skip.copy(), accumulate=True)
+    (q1, s1, z1), _, (q2, s2, z2) = oracle.ref_quantize_rows_residual(hidden)
+    y2, _ = oracle.ref_linear_ex(q1, s1, z1, W, bias, y=skip.copy(), accumulate=True)
+    y2, _ = oracle.ref_linear_ex(q2, s2, z2, W, None, y=y2, accumulate=True)
+    return {"inputs_sha": np.frombuffer(inputs.sha(hidden, skip, w, bias), np.uint8),
+            "wdata": W.data, "wscale": W.scale, "wcolsum": W.colsum,
+            "out_single": y1, "out_two_term": y2}
+
+
 def main():
     if len(sys.argv) > 2 and sys.argv[1] == "--swiglu-child":
         dit_swiglu_child(sys.argv[2])
         return
+    if len(sys.argv) > 2 and sys.argv[1] == "--convt-child":
+        convt_child(sys.argv[2])
+        return
+    only = set(sys.argv[1:])
     for name, fn in (("int8_ops", int8_ops), ("residual", residual), ("conv7", conv7),
-                     ("sym_quant", sym), ("dit_swiglu", dit_swiglu)):
+                     ("sym_quant", sym), ("dit_swiglu", dit_swiglu), ("convt", convt),
+                     ("conv1", conv1)):
+        if only and name not in only:
+            continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())
         print("wrote", name)
 

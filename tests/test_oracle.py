@@ -90,6 +90,30 @@ def test_golden_conv7(idx):
     assert same(out, g[f"c{idx}_out"])
 
 
+@pytest.mark.parametrize("idx", range(5))
+@pytest.mark.parametrize("mode", ["single", "two_term"])
+def test_golden_convtranspose(idx, mode):
+    g = load("convt")
+    case, inp, w, bias = inputs.convt_cases()[idx]
+    assert bytes(g[f"c{idx}_inputs_sha"]) == inputs.sha(inp, w, bias)
+    W = oracle.weight_quantize(w)
+    assert same(W.data, g[f"c{idx}_wdata"])
+    out = oracle.convtranspose1d_int8(inp, W, case["C_out"], case["kernel"], case["stride"],
+                                      case["padding"], case["output_padding"], bias,
+                                      mode == "two_term")
+    assert same(out, g[f"c{idx}_{mode}"])
+
+
+@pytest.mark.parametrize("mode", ["single", "two_term"])
+def test_golden_codec_conv1(mode):
+    g = load("conv1")
+    hidden, skip, w, bias = inputs.conv1_case()
+    assert bytes(g["inputs_sha"]) == inputs.sha(hidden, skip, w, bias)
+    W = oracle.weight_quantize(w)
+    out = oracle.codec_conv1(hidden, W, bias, skip, mode == "two_term")
+    assert same(out, g[f"out_{mode}"])
+
+
 def test_golden_symmetric_quantiser():
     g = load("sym_quant")
     x = inputs.sym_input()
