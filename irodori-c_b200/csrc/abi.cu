@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "gemm_i8.cuh"
+#include "swiglu_fused.cuh"
 #include "quantize.cuh"
 
 using namespace iro;
@@ -715,7 +716,7 @@ size_t iro_int8_swiglu_workspace_bytes(int M, int D, int H, int residual_w2) {
              al(sizeof(float) * (size_t)M * H) +                           // hidden
              al((size_t)M * round_up(H, 16)) + 2 * al(sizeof(float) * M);   // qh, sh, zh
   if (residual_w2) t += al((size_t)M * round_up(H, 16)) + 2 * al(sizeof(float) * M);
-  return t;
+  return t + swiglu_fused_extra_bytes(M);
 }
 
 int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
@@ -759,6 +760,20 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
     qh2 = take((size_t)M * H);
     sh2 = reinterpret_cast<float*>(take(sizeof(float) * M));
     zh2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
+  }
+  if (swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
+    SwigluBuffers b;
+    b.qx = qx;
+    b.sx = sx;
+    b.zx = zx;
+    b.hidden = hid;
+    b.qh = qh;
+    b.sh = sh;
+    b.zh = zh;
+    b.hlo = reinterpret_cast<int*>(take(sizeof(int) * M));
+    b.hhi = reinterpret_cast<int*>(take(sizeof(int) * M));
+    b.ctr = reinterpret_cast<int*>(ws + off);
+    return swiglu_fused_launch(c, x, M, w13, w2, b2 ? b2 : w2->bias, out, b, s);
   }
   st = quantize_rows_launch(x, M, D, qx, sx, zx, 0, s);
   if (st) return st;

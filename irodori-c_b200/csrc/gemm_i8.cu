@@ -3,15 +3,17 @@
 // TMA through a shared-memory ring, with the dequantisation epilogues of the
 // reference's int8 linear fused in.
 //
-// Roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: A tile [128 x 128 B] (+ second A for the dual
-//               term) and B tile [BN x 128 B] per stage, 128-byte swizzle.
-//   warp 1      TMEM allocator + MMA issuer: 4 MMAs of K=32 per stage into
-//               one of two TMEM accumulator buffers; commits release the
-//               stage and, after the last K block, hand the buffer over.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, the exact
-//               reference float arithmetic (ops.c:468-490), global stores;
-//               runs while the MMA warp fills the other accumulator.
+// Roles (576 threads, one CTA per SM):
+//   warp 0       TMA producer: A tile [128 x 128 B] (+ second A for the dual
+//                term) and B tile [BN x 128 B] per stage, 128-byte swizzle.
+//   warp 1       TMEM allocator + MMA issuer: 4 MMAs of K=32 per stage into
+//                one of two TMEM accumulator buffers; commits release the
+//                stage and, after the last K block, hand the buffer over.
+//   warps 2..17  epilogue, four warps per TMEM lane quadrant, each a quarter
+//                of the tile's columns: tcgen05.ld 16 columns at a time, the
+//                exact reference float arithmetic (ops.c:468-490), 64-byte
+//                swizzled staging and TMA tile stores; runs while the MMA
+//                warp fills the other accumulator.
 //
 // Parity: the integer sums are exact.  The epilogue uses explicitly rounded
 // intrinsics in the reference's order, so fp32 outputs are bit-identical to
@@ -23,6 +25,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "epi_math.cuh"
 #include "gemm_i8.cuh"
 
 namespace iro {
@@ -31,7 +34,6 @@ constexpr int BM = 128;
 constexpr int BKB = 128;  // K bytes per pipeline stage (one swizzle row)
 constexpr int kEpiWarps = 16;      // 4 per TMEM lane quadrant / per scheduler
 constexpr int kParts = kEpiWarps / 4;  // column parts per quadrant
-constexpr int kChunk = 16;         // columns per tcgen05.ld / staging tile
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemMax = 232448;  // 227 KB opt-in per CTA
 constexpr int kStgBytes = 32 * kChunk * 4;  // one staging tile: 32 rows x 16 fp32
@@ -102,23 +104,6 @@ __device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
 struct OutMaps {
   CUtensorMap m[4];
 };
-
-// Staging layout for one warp's 32 x 16 fp32 tile in the 64-byte swizzle the
-// TMA store expects: 16-byte chunk c of row r lives at chunk c ^ ((r >> 1) & 3).
-__device__ __forceinline__ void stage_row16(uint8_t* stg, int r, const float (&v)[kChunk]) {
-#pragma unroll
-  for (int c = 0; c < 4; c++) {
-    float4* d = reinterpret_cast<float4*>(stg + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-    *d = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-  }
-}
-
-// Direct stores of one row's chunk (fallback for unaligned outputs).
-__device__ __forceinline__ void store_row16(float* dst, const float (&v)[kChunk], int valid) {
-#pragma unroll
-  for (int j = 0; j < kChunk; j++)
-    if (j < valid) dst[j] = v[j];
-}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -340,38 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x16(tbase + c0, r1);
           tmem_ld_32x32b_x16(tbase + HALF + c0, r3);
           tmem_ld_wait();
-          float a1[kChunk], a3[kChunk];
-#pragma unroll
-          for (int i = 0; i < kChunk / 4; i++) {
-            const int c1 = c0 + 4 * i, c3 = HALF + c0 + 4 * i;
-            const int4 cs1 = *reinterpret_cast<const int4*>(p_cs + c1);
-            const float4 sw1 = *reinterpret_cast<const float4*>(p_sw + c1);
-            const int4 cs3 = *reinterpret_cast<const int4*>(p_cs + c3);
-            const float4 sw3 = *reinterpret_cast<const float4*>(p_sw + c3);
-            float2 a1lo = dequant2(r1[4 * i], r1[4 * i + 1], zp, cs1.x, cs1.y, sx, sw1.x, sw1.y);
-            float2 a1hi = dequant2(r1[4 * i + 2], r1[4 * i + 3], zp, cs1.z, cs1.w, sx, sw1.z, sw1.w);
-            float2 a3lo = dequant2(r3[4 * i], r3[4 * i + 1], zp, cs3.x, cs3.y, sx, sw3.x, sw3.y);
-            float2 a3hi = dequant2(r3[4 * i + 2], r3[4 * i + 3], zp, cs3.z, cs3.w, sx, sw3.z, sw3.w);
-            // Without a bias the staged bias is +0, and x + 0 == x here: a
-            // dequantised value is never -0 (an int converts to +0 and the
-            // scales are positive), so no branch is needed.
-            const float4 b1 = *reinterpret_cast<const float4*>(p_b + c1);
-            const float4 b3 = *reinterpret_cast<const float4*>(p_b + c3);
-            a1lo = add2_rn(a1lo, make_float2(b1.x, b1.y));
-            a1hi = add2_rn(a1hi, make_float2(b1.z, b1.w));
-            a3lo = add2_rn(a3lo, make_float2(b3.x, b3.y));
-            a3hi = add2_rn(a3hi, make_float2(b3.z, b3.w));
-            a1[4 * i] = a1lo.x;
-            a1[4 * i + 1] = a1lo.y;
-            a1[4 * i + 2] = a1hi.x;
-            a1[4 * i + 3] = a1hi.y;
-            a3[4 * i] = a3lo.x;
-            a3[4 * i + 1] = a3lo.y;
-            a3[4 * i + 2] = a3hi.x;
-            a3[4 * i + 3] = a3hi.y;
-          }
           float v[kChunk];
-          silu_gate_chunk(a1, a3, v);
+          gated_chunk(r1, r3, c0, HALF + c0, p_cs, p_sw, p_b, zp, sx, v);
           emit(v, &tmO.m[0], h0, p.H, p.hidden + (size_t)row * p.ldh + h0);
         }
       } else {
@@ -638,9 +593,11 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       return launch_t<64, EPI_SPLIT>(c, r, p, s);
     }
     case EPI_GATED:
-      if (w->layout != IRO_LAYOUT_GATED_PAIR || w->pair != 128 || !r.hidden)
-        return IRO_ERR_UNSUPPORTED;
-      return launch_t<256, EPI_GATED>(c, r, p, s);
+      // The tile holds one pair block: `pair` W1 rows then the matching W3 rows.
+      if (w->layout != IRO_LAYOUT_GATED_PAIR || !r.hidden) return IRO_ERR_UNSUPPORTED;
+      if (w->pair == 128) return launch_t<256, EPI_GATED>(c, r, p, s);
+      if (w->pair == 64) return launch_t<128, EPI_GATED>(c, r, p, s);
+      return IRO_ERR_UNSUPPORTED;
     case EPI_DUAL: {
       if (!r.a2 || !r.sx2 || !r.zp2 || !r.y) return IRO_ERR_INVALID;
       const int bn = r.force_bn ? r.force_bn : pick_bn(r.M, w->N, c->num_sms, 1);
