@@ -152,6 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above overlaps the previous kernel's tail under a
+  // programmatic launch; everything below may read its outputs.
+  grid_dep_wait();
   if (threadIdx.x == 0) trace_mark(p, TR_ENTRY);
 
   if (warp == 0) {
@@ -514,8 +517,9 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
     cudaMemsetAsync(tr, 0, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid, s);
     p.trace = tr;
   }
-  gemm_i8_kernel<BN, EPI><<<grid, kThreads, C::SMEM, s>>>(ta, tb, ta2, om, p);
-  st = check_launch();
+  cudaError_t le = launch_pdl(gemm_i8_kernel<BN, EPI>, dim3(grid), dim3(kThreads),
+                              (size_t)C::SMEM, s, ta, tb, ta2, om, p);
+  st = le == cudaSuccess ? check_launch() : (cudaGetLastError(), map_cuda(le));
   if (tr) {
     char name[48];
     snprintf(name, sizeof(name), "bn%d/epi%d", BN, EPI);

@@ -168,6 +168,14 @@ __device__ __forceinline__ void silu_gate_chunk(const float (&a)[N], const float
   }
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream drains.
+// It must call grid_dep_wait() before it reads or writes global memory that
+// kernel touches; without that launch attribute the call returns at once.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Shared-memory addresses and mbarriers.
 

@@ -64,6 +64,7 @@ __device__ __forceinline__ float block_max(float a, float* sm) {
 template <int V, int MODE>
 __global__ void __launch_bounds__(kQThreads) quant_rows_vec(QuantArgs a) {
   __shared__ float sm[8];
+  grid_dep_wait();
   const int tid = threadIdx.x;
   const int row = blockIdx.x;
   const int K4 = a.K >> 2;
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec(QuantArgs a) {
 // Any K / alignment: one warp per row, scalar loads, the row read per pass.
 template <int MODE>
 __global__ void __launch_bounds__(256) quant_rows_generic(QuantArgs a) {
+  grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= a.M) return;
@@ -249,13 +251,22 @@ static int launch_mode(const QuantArgs& a, cudaStream_t s) {
   const int K4 = a.K / 4;
   if (aligned && K4 <= 8 * kQThreads) {
     const dim3 rg((unsigned)a.M), rb(kQThreads);
-    if (K4 <= 1 * kQThreads) quant_rows_vec<1, MODE><<<rg, rb, 0, s>>>(a);
-    else if (K4 <= 2 * kQThreads) quant_rows_vec<2, MODE><<<rg, rb, 0, s>>>(a);
-    else if (K4 <= 4 * kQThreads) quant_rows_vec<4, MODE><<<rg, rb, 0, s>>>(a);
-    else if (K4 <= 6 * kQThreads) quant_rows_vec<6, MODE><<<rg, rb, 0, s>>>(a);
-    else quant_rows_vec<8, MODE><<<rg, rb, 0, s>>>(a);
+    cudaError_t e;
+    if (K4 <= 1 * kQThreads) e = launch_pdl(quant_rows_vec<1, MODE>, rg, rb, 0, s, a);
+    else if (K4 <= 2 * kQThreads) e = launch_pdl(quant_rows_vec<2, MODE>, rg, rb, 0, s, a);
+    else if (K4 <= 4 * kQThreads) e = launch_pdl(quant_rows_vec<4, MODE>, rg, rb, 0, s, a);
+    else if (K4 <= 6 * kQThreads) e = launch_pdl(quant_rows_vec<6, MODE>, rg, rb, 0, s, a);
+    else e = launch_pdl(quant_rows_vec<8, MODE>, rg, rb, 0, s, a);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return map_cuda(e);
+    }
   } else {
-    quant_rows_generic<MODE><<<grid, block, 0, s>>>(a);
+    cudaError_t e = launch_pdl(quant_rows_generic<MODE>, grid, block, 0, s, a);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return map_cuda(e);
+    }
   }
   return check_launch();
 }

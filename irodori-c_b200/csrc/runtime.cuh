@@ -3,6 +3,8 @@
 // entry points.
 #pragma once
 
+#include <string.h>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -88,6 +90,27 @@ int make_tmap_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t r
 
 inline cudaStream_t pick_stream(Ctx* c, void* s) {
   return s ? static_cast<cudaStream_t>(s) : c->stream;
+}
+
+// Launch with programmatic stream serialization (see grid_dep_wait): the
+// kernel's launch and prologue overlap the previous kernel's tail.  Every
+// kernel launched this way calls grid_dep_wait() before its first global
+// memory access that depends on earlier work in the stream.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 // Default in-kernel wait limit (ns) for bounded mbarrier waits.
