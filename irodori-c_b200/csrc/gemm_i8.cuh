@@ -42,4 +42,9 @@ struct GemmRequest {
 
 int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
 
+// Split-K over a two-CTA cluster for plain linears with few, long tiles
+// (gemm_splitk.cu); gemm_launch picks it when eligible and IRO_GEMM_SPLITK=1.
+bool splitk_eligible(const GemmRequest& r, int num_sms);
+int splitk_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
+
 }  // namespace iro
