@@ -507,6 +507,23 @@ def run_profile_case(args):
     import iro_b200 as iro
     import oracle as oracle_mod
 
+    if args.profile == "conv7":
+        # Config-4 geometry on one 72000-frame sequence: 147 MB in and out,
+        # more than L2, a few hundred MB on the device.
+        B, T, C, N, KW = 1, 72000, 512, 512, 7
+        iro.init(0)
+        rng = np.random.default_rng(44)
+        inp = rng.standard_normal((B, T, C), dtype=np.float32) * np.float32(0.5)
+        w = rng.standard_normal((N, KW * C), dtype=np.float32) * np.float32(0.02)
+        dw = iro.DevWeight.upload(iro.HostWeight(w))
+        xd = iro.DevBuf.from_host(inp)
+        out = iro.DevBuf((B, T, N), np.float32)
+        for _ in range(args.warmup + args.steps):
+            iro.conv1d_dev(xd, B, T, C, dw, KW, 1, 1, 3, None, False, out)
+        iro.synchronize()
+        print(f"profile case conv7: {args.warmup + args.steps} launches ok")
+        return
+
     global NSETS
     NSETS = 1
     iro.init(0)
@@ -579,7 +596,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--workload", choices=["swiglu", "conv7"], default="swiglu",
                     help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
-    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block"],
+    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
