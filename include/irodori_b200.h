@@ -323,6 +323,38 @@ int iro_int8_codec_conv1_dev(const float *hidden, int rows, const IroInt8DevWeig
                              const float *bias, const float *skip, int residual,
                              float *output, void *stream);
 
+/* Checkpoints: safetensors files mapped read-only --------------------------------- */
+
+/* The reference's loader (safetensors.c, iro_st_load/iro_st_get) mmaps a
+   checkpoint and its int8 engine quantises fp32 projections on the host at
+   init (dit.c:235-259 -> ops.c:259-293).  These entry points open the same
+   files (named iro_st_file_* so they can be linked beside the reference's
+   iro_st_* functions) and quantise on the device. */
+typedef struct IroStFile IroStFile;
+/* Map a .safetensors file read-only and parse its header; every tensor's
+   bytes must lie inside the file.  Returns IRO_OK or IRO_ERR_INVALID. */
+int iro_st_file_open(IroStFile **file, const char *path);
+void iro_st_file_close(IroStFile *file);
+int iro_st_file_count(const IroStFile *file);
+const char *iro_st_file_name(const IroStFile *file, int index);
+/* Geometry of a tensor by name; dtype follows irodori.h's IroDType order
+   (0 F32, 1 F16, 2 BF16, 3 I64, 4 I32, 5 I16, 6 I8, 7 U8, 8 BOOL, 9 other);
+   shape receives ndims values (at most 8). */
+int iro_st_file_tensor(const IroStFile *file, const char *name, int *dtype, int *ndims,
+                       uint64_t *shape, uint64_t *nbytes);
+/* Pointer into the mapping (valid until iro_st_file_close). */
+const void *iro_st_file_data(const IroStFile *file, const char *name);
+/* safetensors.c:525-552: release the clean pages of every tensor whose name
+   starts with prefix (page-aligned span, clipped to the mapping); pointers
+   stay valid and pages fault back in if read.  Returns the bytes released. */
+uint64_t iro_st_file_drop_prefix(const IroStFile *file, const char *prefix);
+/* ops.c:259-306 on the device: quantise the F32 tensor `name`, [N, K]
+   row-major, or [K, N] with transposed = 1, into dst (codes, scales and
+   column sums equal iro_int8_weight_quantize's); bias_name (F32 [N]) may be
+   NULL.  Synchronous.  Returns IRO_OK or IRO_ERR_*. */
+int iro_int8_dev_weight_from_st(IroInt8DevWeight *dst, const IroStFile *file, const char *name,
+                                int transposed, const char *bias_name);
+
 /* Failure detection ------------------------------------------------------------- */
 
 /* Launches one block that waits on a device barrier nothing ever completes,

@@ -109,6 +109,14 @@ SIGNATURES = {
     "iro_int8_convtranspose1d_dev": (_i, [_vp, _i, _i, _i, _DW, _i, _i, _i, _i, _i, _vp, _i,
                                           _vp, _vp]),
     "iro_int8_codec_conv1_dev": (_i, [_vp, _i, _DW, _vp, _vp, _i, _vp, _vp]),
+    "iro_st_file_open": (_i, [_vp, C.c_char_p]),
+    "iro_st_file_close": (None, [_vp]),
+    "iro_st_file_count": (_i, [_vp]),
+    "iro_st_file_name": (C.c_char_p, [_vp, _i]),
+    "iro_st_file_tensor": (_i, [_vp, C.c_char_p, _vp, _vp, _vp, _vp]),
+    "iro_st_file_data": (_vp, [_vp, C.c_char_p]),
+    "iro_st_file_drop_prefix": (_u64, [_vp, C.c_char_p]),
+    "iro_int8_dev_weight_from_st": (_i, [_DW, _vp, C.c_char_p, _i, C.c_char_p]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
 }
 
@@ -546,6 +554,43 @@ def codec_conv1_dev(hidden, rows, w: DevWeight, bias, skip, residual, out, strea
     check(lib().iro_int8_codec_conv1_dev(_p(hidden), rows, C.byref(w.st), _p(bias), _p(skip),
                                           int(bool(residual)), _p(out), stream),
            "codec_conv1_dev")
+
+
+class StFile:
+    """A .safetensors checkpoint mapped read-only (iro_st_file_*)."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().iro_st_file_open(C.byref(h), os.fsencode(path)), "st_file_open")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().iro_st_file_close(self.h)
+            self.h = None
+
+    def names(self):
+        return [lib().iro_st_file_name(self.h, i).decode() for i in range(lib().iro_st_file_count(self.h))]
+
+    def tensor(self, name):
+        dt, nd = C.c_int(), C.c_int()
+        shape = (C.c_uint64 * 8)()
+        nb = C.c_uint64()
+        check(lib().iro_st_file_tensor(self.h, name.encode(), C.byref(dt), C.byref(nd), shape,
+                                       C.byref(nb)), "st_file_tensor")
+        return dt.value, tuple(shape[i] for i in range(nd.value)), nb.value
+
+    def drop_prefix(self, prefix):
+        return lib().iro_st_file_drop_prefix(self.h, prefix.encode())
+
+    def weight(self, name, transposed=False, bias_name=None):
+        """Device int8 weight quantised on the GPU from the file's fp32 tensor."""
+        w = DevWeight()
+        check(lib().iro_int8_dev_weight_from_st(C.byref(w.st), self.h, name.encode(),
+                                                int(bool(transposed)),
+                                                bias_name.encode() if bias_name else None),
+              "dev_weight_from_st")
+        return w
 
 
 def header_symbols(path=HEADER_PATH):
