@@ -586,6 +586,91 @@ def run_conv7(args):
                                  "ops_per_step": ops}}), flush=True)
 
 
+def run_init(args):
+    """Engine init of the real DiT's int8 weights (dit.c:235-259): the 96
+    projections of 12 layers (wq, wk, wv, gate, wo [1280, 1280], w1, w3
+    [3680, 1280], w2 [1280, 3680]; 1.07 GB fp32) read from a safetensors
+    checkpoint and quantised.  Ours: iro_int8_dev_weight_from_st per matrix
+    (copy from the mapping + device quantiser), then the reference's page
+    drop.  CPU: the reference's iro_int8_weight_quantize (fast build, one
+    thread, as its init loop runs) on layer 0's eight matrices, scaled by 12.
+    Synthetic seeded weights; the file is written (untimed) to a temp dir, so
+    reads hit the page cache, as a repeated engine start would."""
+    import tempfile
+    import iro_b200 as iro
+
+    D, Hm, L = 1280, 3680, 12
+    shapes = [("attention.wq", D, D), ("attention.wk", D, D), ("attention.wv", D, D),
+              ("attention.gate", D, D), ("attention.wo", D, D), ("mlp.w1", Hm, D),
+              ("mlp.w3", Hm, D), ("mlp.w2", D, Hm)]
+    iro.init(0)
+    rng = np.random.default_rng(7)
+    tmpd = tempfile.mkdtemp(prefix="iro_init_")
+    path = os.path.join(tmpd, "model.safetensors")
+    header, off = {}, 0
+    for layer in range(L):
+        for nm, n, k in shapes:
+            header[f"blocks.{layer}.{nm}.weight"] = {"dtype": "F32", "shape": [n, k],
+                                                     "data_offsets": [off, off + 4 * n * k]}
+            off += 4 * n * k
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    layer0 = {}
+    with open(path, "wb") as f:
+        f.write(len(hj).to_bytes(8, "little"))
+        f.write(hj)
+        for layer in range(L):
+            for nm, n, k in shapes:
+                a = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+                if layer == 0:
+                    layer0[nm] = a
+                f.write(a.tobytes())
+    total_bytes = off
+
+    def ours():
+        t0 = time.perf_counter()
+        st = iro.StFile(path)
+        ws = []
+        for layer in range(L):
+            for nm, _, _ in shapes:
+                ws.append(st.weight(f"blocks.{layer}.{nm}.weight"))
+            for nm in ("attention.wq.", "attention.wk.", "attention.wv.", "attention.gate.",
+                       "attention.wo.", "mlp."):
+                st.drop_prefix(f"blocks.{layer}.{nm}")
+        iro.synchronize()
+        el = time.perf_counter() - t0
+        for w in ws:
+            w.free()
+        st.close()
+        return el
+
+    for _ in range(max(1, args.warmup)):
+        ours()
+    times = [ours() for _ in range(max(1, args.steps))]
+    t_ours = min(times)
+
+    cpu = None
+    Lref, kind, variant = _ref_lib()
+    if Lref is not None:
+        import oracle as oracle_mod
+        t0 = time.perf_counter()
+        for nm, n, k in shapes:
+            oracle_mod.ref_weight_quantize(layer0[nm], kind=variant)
+        t_layer = time.perf_counter() - t0
+        cpu = {"value": round(t_layer * L, 4), "unit": "s", "cores": 1, "kind": kind,
+               "build": variant, "sample": "layer 0's 8 projections, x 12 layers"}
+    os.remove(path)
+    os.rmdir(tmpd)
+    print(json.dumps({"metric": "DiT int8 weight init from safetensors (96 projections)",
+                      "value": round(t_ours, 4), "unit": "s", "higher_is_better": False,
+                      "steps": len(times), "warmup": max(1, args.warmup),
+                      "gb_per_s": round(total_bytes / t_ours / 1e9, 2),
+                      "cpu_baseline": cpu, "data": "synthetic (seeded N(0,0.02) weights)",
+                      "config": {"workload": "real DiT 12 x {wq,wk,wv,gate,wo,w1,w3,w2}, "
+                                             "1280/3680, fp32 safetensors in page cache",
+                                 "fp32_bytes": total_bytes}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -594,7 +679,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["swiglu", "conv7"], default="swiglu",
+    ap.add_argument("--workload", choices=["swiglu", "conv7", "init"], default="swiglu",
                     help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
     ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
@@ -603,6 +688,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.profile:
         run_profile_case(args)
+    elif args.workload == "init" and args.impl == "ours":
+        run_init(args)
     elif args.workload == "conv7" and args.impl == "ours":
         run_conv7(args)
     elif args.impl == "reference":

@@ -323,6 +323,45 @@ int iro_int8_codec_conv1_dev(const float *hidden, int rows, const IroInt8DevWeig
                              const float *bias, const float *skip, int residual,
                              float *output, void *stream);
 
+/* DiT block ---------------------------------------------------------------------- */
+
+/* One RF-DiT transformer block (dit.c:983-1051) on the device: AdaLN,
+   int8 QKVG, per-head RMSNorm + half RoPE, joint attention over the S latent
+   tokens and the valid context tokens with the sigmoid gate, int8 Wo, gated
+   residual; AdaLN, int8 SwiGLU, gated residual.  The fp32 tensors are device
+   pointers in the reference layouts (dit.h:13-40): adaln[0] is the attention
+   AdaLN, adaln[1] the MLP one, each {shift_down [R,D], shift_up [D,R],
+   shift_bias [D], scale_down, scale_up, scale_bias, gate_down, gate_up,
+   gate_bias}; q_norm, k_norm [D].  qkvg is wq|wk|wv|gate concatenated
+   (iro_int8_dev_weight_concat), w13 the gated pair of w1, w3.
+   residual_mask follows IRO_INT8_RESIDUAL (dit.c:429-436; 8 = two-term W2,
+   the reference default); other bits are IRO_ERR_UNSUPPORTED. */
+typedef struct {
+    const float *adaln[2][9];
+    const float *q_norm;
+    const float *k_norm;
+    IroInt8DevWeight qkvg, wo, w13, w2;
+    int model_dim, heads, head_dim, adaln_rank, mlp_dim;
+    float norm_eps;
+    int residual_mask;
+} IroDiTBlockDev;
+
+/* dit.c:644-705: RoPE cos/sin tables [S, head_dim/2] as the reference builds
+   them (double-precision rotation recurrence, rounded to float); host
+   buffers. */
+int iro_dit_rope_table(float *cos_out, float *sin_out, int S, int head_dim);
+size_t iro_dit_block_workspace_bytes(const IroDiTBlockDev *blk, int B, int S, int C,
+                                     int context_batch);
+/* x [B*S, D] is updated in place; cond [B, 3*D]; ctx_k/ctx_v [context_batch,
+   C, D] (context_batch 1 = one context shared by the batch, dit.c:903-911);
+   mask [B, C] per batch row in either case (dit.c:811-813); rope_cos/sin
+   device [S, 32].  workspace NULL uses the library's scratch.  Returns IRO_OK
+   or IRO_ERR_*. */
+int iro_dit_block_dev(const IroDiTBlockDev *blk, float *x, const float *cond,
+                      const float *ctx_k, const float *ctx_v, const uint8_t *ctx_mask,
+                      int context_batch, int B, int S, int C, const float *rope_cos,
+                      const float *rope_sin, void *workspace, void *stream);
+
 /* Checkpoints: safetensors files mapped read-only --------------------------------- */
 
 /* The reference's loader (safetensors.c, iro_st_load/iro_st_get) mmaps a

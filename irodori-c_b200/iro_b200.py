@@ -48,9 +48,18 @@ class IroInt8DevWeight(C.Structure):
                 ("device", C.c_int), ("priv", C.c_void_p)]
 
 
+class IroDiTBlockDev(C.Structure):
+    _fields_ = [("adaln", (C.c_void_p * 9) * 2), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p),
+                ("qkvg", IroInt8DevWeight), ("wo", IroInt8DevWeight), ("w13", IroInt8DevWeight),
+                ("w2", IroInt8DevWeight), ("model_dim", C.c_int), ("heads", C.c_int),
+                ("head_dim", C.c_int), ("adaln_rank", C.c_int), ("mlp_dim", C.c_int),
+                ("norm_eps", C.c_float), ("residual_mask", C.c_int)]
+
+
 _vp, _i, _sz, _u64 = C.c_void_p, C.c_int, C.c_size_t, C.c_uint64
 _W = C.POINTER(IroInt8Weight)
 _DW = C.POINTER(IroInt8DevWeight)
+_DB = C.POINTER(IroDiTBlockDev)
 
 # name -> (restype, argtypes); every symbol declared in the public header.
 SIGNATURES = {
@@ -117,6 +126,9 @@ SIGNATURES = {
     "iro_st_file_data": (_vp, [_vp, C.c_char_p]),
     "iro_st_file_drop_prefix": (_u64, [_vp, C.c_char_p]),
     "iro_int8_dev_weight_from_st": (_i, [_DW, _vp, C.c_char_p, _i, C.c_char_p]),
+    "iro_dit_rope_table": (_i, [_vp, _vp, _i, _i]),
+    "iro_dit_block_workspace_bytes": (_sz, [_DB, _i, _i, _i, _i]),
+    "iro_dit_block_dev": (_i, [_DB, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
 }
 
@@ -554,6 +566,45 @@ def codec_conv1_dev(hidden, rows, w: DevWeight, bias, skip, residual, out, strea
     check(lib().iro_int8_codec_conv1_dev(_p(hidden), rows, C.byref(w.st), _p(bias), _p(skip),
                                           int(bool(residual)), _p(out), stream),
            "codec_conv1_dev")
+
+
+def dit_rope_table(S, head_dim=64):
+    """dit.c:644-705 RoPE tables as host arrays [S, head_dim/2]."""
+    c = np.empty((S, head_dim // 2), np.float32)
+    sn = np.empty((S, head_dim // 2), np.float32)
+    check(lib().iro_dit_rope_table(_p(c), _p(sn), S, head_dim), "dit_rope_table")
+    return c, sn
+
+
+class DiTBlock:
+    """One DiT block's device weights (IroDiTBlockDev), built from host fp32
+    AdaLN/norm arrays and int8 weights (HostWeight or (data, scale, colsum))."""
+
+    def __init__(self, adaln, q_norm, k_norm, wq, wk, wv, wg, wo, w1, w3, w2, model_dim=1280,
+                 heads=20, rank=192, mlp_dim=3680, eps=1e-5, residual_mask=8):
+        self.bufs = [DevBuf.from_host(np.ascontiguousarray(a, np.float32)) for a in adaln]
+        self.qn = DevBuf.from_host(np.ascontiguousarray(q_norm, np.float32))
+        self.kn = DevBuf.from_host(np.ascontiguousarray(k_norm, np.float32))
+        self.qkvg = DevWeight.concat([wq, wk, wv, wg])
+        self.wo = DevWeight.upload(wo)
+        self.w13 = DevWeight.gated_pair(w1, w3)
+        self.w2 = DevWeight.upload(w2)
+        st = IroDiTBlockDev()
+        for i in range(2):
+            for j in range(9):
+                st.adaln[i][j] = self.bufs[9 * i + j].ptr
+        st.q_norm, st.k_norm = self.qn.ptr, self.kn.ptr
+        st.qkvg, st.wo, st.w13, st.w2 = self.qkvg.st, self.wo.st, self.w13.st, self.w2.st
+        st.model_dim, st.heads, st.head_dim, st.adaln_rank, st.mlp_dim = (model_dim, heads, 64,
+                                                                          rank, mlp_dim)
+        st.norm_eps, st.residual_mask = eps, residual_mask
+        self.st = st
+
+    def run(self, x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C, rope_cos, rope_sin,
+            workspace=None, stream=None):
+        check(lib().iro_dit_block_dev(C.byref(self.st), _p(x), _p(cond), _p(ctx_k), _p(ctx_v),
+                                      _p(mask), context_batch, B, S, C, _p(rope_cos),
+                                      _p(rope_sin), _p(workspace), stream), "dit_block_dev")
 
 
 class StFile:

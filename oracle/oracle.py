@@ -346,6 +346,10 @@ def ref_lib(kind="ieee"):
         if kind == "dit":
             L.ref_dit_swiglu_int8.argtypes = [_vp, C.c_int] + [_vp] * 10
             L.ref_dit_swiglu_int8.restype = C.c_int
+            L.ref_dit_block_int8.argtypes = [_vp] * 5 + [C.c_int] * 4 + [_vp] * 6
+            L.ref_dit_block_int8.restype = C.c_int
+            L.ref_dit_block_dims.argtypes = [C.POINTER(C.c_int)] * 4
+            L.ref_dit_block_dims.restype = C.c_int
             L.ref_dit_dims.argtypes = [C.POINTER(C.c_int), C.POINTER(C.c_int)]
             L.ref_dit_dims.restype = C.c_int
         _ref_libs[kind] = L
@@ -485,6 +489,35 @@ def ref_convtranspose1d_int8(inp, w: Weight, C_out, kernel, stride, padding, out
 
 def ref_codec_upsample_residual():
     return bool(ref_lib("codec").ref_codec_upsample_residual())
+
+
+def ref_dit_block(x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C_ctx, adaln, q_norm,
+                  k_norm, weights):
+    """The reference's dit_block (dit.c:983-1051) at layer 0 with int8
+    projections.  weights: Weight objects wq, wk, wv, gate, wo, w1, w3, w2.
+    Returns the updated x [B*S, D]."""
+    L = ref_lib("dit")
+    x = _c(x, np.float32).copy()
+    keep = [_c(a, np.float32) for a in adaln]
+    ada = (_vp * 18)(*[a.ctypes.data for a in keep])
+    wd = (_vp * 8)(*[w.data.ctypes.data for w in weights])
+    wsc = (_vp * 8)(*[w.scale.ctypes.data for w in weights])
+    wcs = (_vp * 8)(*[w.colsum.ctypes.data for w in weights])
+    cond = _c(cond, np.float32); ctx_k = _c(ctx_k, np.float32); ctx_v = _c(ctx_v, np.float32)
+    mask = _c(mask, np.uint8); q_norm = _c(q_norm, np.float32); k_norm = _c(k_norm, np.float32)
+    rc = L.ref_dit_block_int8(_ptr(x), _ptr(cond), _ptr(ctx_k), _ptr(ctx_v), _ptr(mask),
+                              context_batch, B, S, C_ctx, ada, _ptr(q_norm), _ptr(k_norm),
+                              wd, wsc, wcs)
+    if rc != 0:
+        raise RuntimeError("reference dit_block failed")
+    return x
+
+
+def ref_dit_block_dims():
+    L = ref_lib("dit")
+    v = [C.c_int() for _ in range(4)]
+    L.ref_dit_block_dims(*[C.byref(i) for i in v])
+    return tuple(i.value for i in v)
 
 
 def ref_dit_dims():

@@ -39,3 +39,51 @@ int ref_dit_swiglu_int8(const float *x, int rows,
     layer.w2 = ref_weight(w2, s2, c2, MODEL_DIM, MLP_DIM);
     return dit_swiglu(&mlp, x, 1, rows, out, -1, NULL, &layer);
 }
+
+/* The reference's whole transformer block, dit.c:983-1051, at layer 0 with
+   the int8 projections (the engine's default int8 path: IRO_INT8_MASK 15,
+   residual policy from IRO_INT8_RESIDUAL, W2 two-term by default).
+   adaln: 18 fp32 pointers, attention then MLP AdaLN, each in IroAdaLN order;
+   wq, wk, wv, gate, wo, w1, w3, w2: int8 weights quantised by the caller with
+   iro_int8_weight_quantize.  x [B*S, 1280] is updated in place. */
+int ref_dit_block_int8(float *x, const float *cond, const float *ctx_k,
+                       const float *ctx_v, const uint8_t *ctx_mask,
+                       int context_batch, int B, int S, int C,
+                       const float *const *adaln, const float *q_norm,
+                       const float *k_norm, const int8_t *const *wdata,
+                       const float *const *wscale, const int32_t *const *wcolsum) {
+    IroDiT *d = calloc(1, sizeof(IroDiT));
+    IroDiTInt8 *q = calloc(1, sizeof(IroDiTInt8));
+    if (!d || !q) { free(d); free(q); return -1; }
+    IroAdaLN *sets[2] = {&d->attention_adaln[0], &d->mlp_adaln[0]};
+    for (int i = 0; i < 2; i++) {
+        const float *const *a = adaln + 9 * i;
+        sets[i]->shift_down = a[0]; sets[i]->shift_up = a[1]; sets[i]->shift_bias = a[2];
+        sets[i]->scale_down = a[3]; sets[i]->scale_up = a[4]; sets[i]->scale_bias = a[5];
+        sets[i]->gate_down = a[6]; sets[i]->gate_up = a[7]; sets[i]->gate_bias = a[8];
+    }
+    d->attention[0].q_norm = q_norm;
+    d->attention[0].k_norm = k_norm;
+    d->norm_eps = 1e-5f;
+    IroDiTInt8Layer *l = &q->layer[0];
+    const int shapes[8][2] = {{MODEL_DIM, MODEL_DIM}, {MODEL_DIM, MODEL_DIM},
+                              {MODEL_DIM, MODEL_DIM}, {MODEL_DIM, MODEL_DIM},
+                              {MODEL_DIM, MODEL_DIM}, {MLP_DIM, MODEL_DIM},
+                              {MLP_DIM, MODEL_DIM}, {MODEL_DIM, MLP_DIM}};
+    IroInt8Weight *ws[8] = {&l->wq, &l->wk, &l->wv, &l->gate, &l->wo, &l->w1, &l->w3, &l->w2};
+    for (int i = 0; i < 8; i++)
+        *ws[i] = ref_weight(wdata[i], wscale[i], wcolsum[i], shapes[i][0], shapes[i][1]);
+    d->int8 = q;
+    int rc = dit_block(d, 0, x, cond, ctx_k, ctx_v, ctx_mask, context_batch, B, S, C);
+    free(d);
+    free(q);
+    return rc;
+}
+
+int ref_dit_block_dims(int *model_dim, int *heads, int *rank, int *mlp_dim) {
+    *model_dim = MODEL_DIM;
+    *heads = IRO_DIT_HEADS;
+    *rank = ADALN_RANK;
+    *mlp_dim = MLP_DIM;
+    return 0;
+}

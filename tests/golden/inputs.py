@@ -113,6 +113,35 @@ def conv1_case():
     return hidden, skip, w, bias
 
 
+DIT_D, DIT_HEADS, DIT_RANK, DIT_H = 1280, 20, 192, 3680
+
+
+def dit_block_case(seed, B, S, C, context_batch):
+    """Synthetic inputs of one DiT block at the reference's fixed dimensions:
+    x [B*S, D], cond [B, 3D], context K/V [context_batch, C, D] with a mask
+    [B, C] per batch row that drops some context tokens (the reference reads
+    the mask per batch row even for a shared context), AdaLN matrices
+    (attention then MLP, each
+    in IroAdaLN order), q/k norm weights, and fp32 projection weights
+    (wq, wk, wv, gate, wo, w1, w3, w2) to be quantised."""
+    D, R, H = DIT_D, DIT_RANK, DIT_H
+    rng = np.random.default_rng(seed)
+    f = lambda *sh, s=1.0: (rng.standard_normal(sh) * s).astype(np.float32)
+    x = f(B * S, D)
+    cond = f(B, 3 * D, s=0.5)
+    ctx_k, ctx_v = f(context_batch, C, D), f(context_batch, C, D)
+    mask = (rng.random((B, C)) < 0.8).astype(np.uint8)
+    mask[:, 0] = 1
+    adaln = []
+    for _ in range(2):
+        for _ in range(3):
+            adaln += [f(R, D, s=0.03), f(D, R, s=0.03), f(D, s=0.02)]
+    q_norm = (1.0 + f(D, s=0.1)).astype(np.float32)
+    k_norm = (1.0 + f(D, s=0.1)).astype(np.float32)
+    ws = [f(D, D, s=0.03) for _ in range(5)] + [f(H, D, s=0.03), f(H, D, s=0.03), f(D, H, s=0.02)]
+    return x, cond, ctx_k, ctx_v, mask, adaln, q_norm, k_norm, ws
+
+
 def sym_input():
     rng = np.random.default_rng(77)
     x = rng.standard_normal((40, 96)).astype(np.float32)

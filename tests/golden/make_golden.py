@@ -162,7 +162,38 @@ def conv1():
             "out_single": y1, "out_two_term": y2}
 
 
+DIT_BLOCK_CASES = [(11, 2, 40, 12, 1), (12, 2, 70, 9, 2)]  # seed, B, S, C, context_batch
+
+
+def dit_block_child():
+    """Child process with IRO_INT8_RESIDUAL unset: the reference's default
+    policy (two-term W2, dit.c:429-436)."""
+    res = {}
+    for i, (seed, B, S, C, cb) in enumerate(DIT_BLOCK_CASES):
+        x, cond, ck, cv, mask, adaln, qn, kn, ws = inputs.dit_block_case(seed, B, S, C, cb)
+        W = [oracle.ref_weight_quantize(w) for w in ws]
+        res[f"c{i}_out"] = oracle.ref_dit_block(x, cond, ck, cv, mask, cb, B, S, C, adaln, qn,
+                                                kn, W)
+        res[f"c{i}_inputs_sha"] = np.frombuffer(
+            inputs.sha(x, cond, ck, cv, mask, *adaln, qn, kn, *ws), np.uint8)
+        res[f"c{i}_case"] = np.array([seed, B, S, C, cb], np.int32)
+    np.savez(os.path.join(HERE, "_tmp_dit_block.npz"), **res)
+
+
+def dit_block():
+    e = dict(os.environ)
+    e.pop("IRO_INT8_RESIDUAL", None)
+    subprocess.run([sys.executable, __file__, "--dit-block-child", "x"], check=True, env=e)
+    path = os.path.join(HERE, "_tmp_dit_block.npz")
+    got = dict(np.load(path))
+    os.remove(path)
+    return got
+
+
 def main():
+    if len(sys.argv) > 2 and sys.argv[1] == "--dit-block-child":
+        dit_block_child()
+        return
     if len(sys.argv) > 2 and sys.argv[1] == "--swiglu-child":
         dit_swiglu_child(sys.argv[2])
         return
@@ -172,7 +203,7 @@ def main():
     only = set(sys.argv[1:])
     for name, fn in (("int8_ops", int8_ops), ("residual", residual), ("conv7", conv7),
                      ("sym_quant", sym), ("dit_swiglu", dit_swiglu), ("convt", convt),
-                     ("conv1", conv1)):
+                     ("conv1", conv1), ("dit_block", dit_block)):
         if only and name not in only:
             continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())
