@@ -671,6 +671,127 @@ def run_init(args):
                                  "fp32_bytes": total_bytes}}), flush=True)
 
 
+def _count_kernels(fn):
+    """Kernel launches of fn() seen by the CUDA activity profiler (untimed)."""
+    try:
+        import torch
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return sum(1 for e in prof.events()
+                   if getattr(e, "device_type", None) is not None
+                   and str(e.device_type).endswith("CUDA") and "emcpy" not in e.name
+                   and "emset" not in e.name)
+    except Exception:  # noqa: BLE001 - the count is informational
+        return None
+
+
+def run_dit(args):
+    """whole DiT Euler steps at the config's dimensions
+    (12 blocks, d_model 1024, 16 heads of 64, SwiGLU 2816, AdaLN rank 192),
+    8 requests x 4 CFG rows (cond, text, speaker and caption uncond) x 750
+    latent frames = 24000 rows per linear, 128 context tokens per request
+    (their per-layer K/V precomputed, as the sampler's KV-cache prep does
+    once per request, sampler.c:205-237).  A step is one Euler step through
+    iro_dit_sample_euler_dev: conditioner, input projection, 12 blocks,
+    output head, CFG-guided update.  Random-init weights quantised by the
+    library's own quantiser; N(0,1) latents; CFG window open for every step.
+    The weights (164 MB of int8) and every activation tensor (98 MB each)
+    exceed the 126 MB L2, so no flush is needed between steps."""
+    import torch
+    import iro_b200 as iro
+
+    D, NH, H, RK, L = 1024, 16, 2816, 192, 12
+    R, CFG, S, Cx = 8, 4, 750, 128
+    if args.dit_dims == "reference":
+        D, NH, H = 1280, 20, 3680
+    iro.init(0)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
+    rng = np.random.default_rng(33)
+    f = lambda *sh, s=1.0: (rng.standard_normal(sh, dtype=np.float32) * np.float32(s))
+    blocks = []
+    for _ in range(L):
+        adaln = []
+        for _ in range(6):
+            adaln += [f(RK, D, s=0.03), f(D, RK, s=0.03), f(D, s=0.02)]
+        ws = [iro.HostWeight(f(D, D, s=0.03)) for _ in range(5)]
+        ws += [iro.HostWeight(f(H, D, s=0.03)), iro.HostWeight(f(H, D, s=0.03)),
+               iro.HostWeight(f(D, H, s=0.02))]
+        blocks.append(iro.DiTBlock(adaln, 1.0 + f(D, s=0.1), 1.0 + f(D, s=0.1), *ws,
+                                   model_dim=D, heads=NH, rank=RK, mlp_dim=H))
+    model = iro.DiTModel(blocks, f(D, 512, s=0.04), f(D, D, s=0.03), f(3 * D, D, s=0.03),
+                         f(D, 32, s=0.15), f(D, s=0.02), 1.0 + f(D, s=0.1), f(32, D, s=0.03),
+                         f(32, s=0.02))
+    ctx_k = [iro.DevBuf.from_host(f(R, Cx, D)) for _ in range(L)]
+    ctx_v = [iro.DevBuf.from_host(f(R, Cx, D)) for _ in range(L)]
+    mask = (rng.random((R * CFG, Cx)) < 0.9).astype(np.uint8)
+    mask[:, 0] = 1
+    maskd = iro.DevBuf.from_host(mask)
+    ws = iro.DevBuf(model.workspace_bytes(R, CFG, S, Cx), np.uint8)
+    state0 = f(R, S, 32)
+    host_in = torch.from_numpy(state0).pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    state = torch.empty(host_in.shape, dtype=torch.float32, device="cuda")
+    scales = [2.0, 1.5, 1.0]
+
+    def sample(k):
+        model.sample_euler(state, R, CFG, S, k, 1.0, 0.0, 1.0, scales, ctx_k, ctx_v, maskd, Cx,
+                           workspace=ws)
+
+    with torch.cuda.stream(stream):
+        state.copy_(host_in, non_blocking=True)
+    sample(args.warmup)
+    iro.synchronize()
+    n1 = _count_kernels(lambda: sample(1))
+    n2 = _count_kernels(lambda: sample(2))
+    clocks = ClockSampler(physical_gpu(0))
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    sample(args.steps)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # End to end: the latents in from pinned host memory, the sampled
+    # latents back, inside the timed region.
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        state.copy_(host_in, non_blocking=True)
+    sample(args.steps)
+    with torch.cuda.stream(stream):
+        host_out.copy_(state, non_blocking=True)
+    e1.record(stream)
+    e1.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    M = R * CFG * S
+    gemm_ops = 2.0 * M * L * (4 * D * D + D * D + 2 * H * D + H * D)
+    attn_flops = 4.0 * M * L * NH * 64 * (S + Cx)
+    launches = None
+    if n1 is not None and n2 is not None:
+        launches = (2 * n1 - n2) + args.steps * (n2 - n1)
+    dims = f"d{D}/h{NH}x64/mlp{H}/rank{RK}"
+    print(json.dumps({
+        "metric": "DiT Euler steps/sec", "value": round(1000.0 / ms, 3), "unit": "steps/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMMs, fp32 attention",
+        "data": "synthetic (random-init weights, N(0,1) latents)",
+        "e2e": {"value": round(1000.0 / ms_e2e, 3), "unit": "steps/s",
+                "h2d_bytes_per_step": host_in.numel() * 4 / args.steps,
+                "d2h_bytes_per_step": host_out.numel() * 4 / args.steps},
+        "int8_linear_tops": round(gemm_ops / ms / 1e9, 1),
+        "attention_tflop_per_step": round(attn_flops / 1e12, 3),
+        "gpu_launches": launches, "launches_per_step": None if launches is None else n2 - n1,
+        "clocks": clk,
+        "config": {"workload": f"cfg3 DiT {L} blocks {dims}, {R} requests x {CFG} CFG rows x "
+                               f"{S} frames ({M} rows/linear), {Cx} context tokens",
+                   "l2": "working set > L2 (164 MB int8 weights, 98 MB activations)",
+                   "int8_ops_per_step": gemm_ops}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -679,10 +800,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["swiglu", "conv7", "init"], default="swiglu",
+    ap.add_argument("--workload", choices=["swiglu", "conv7", "init", "dit"], default="swiglu",
                     help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
     ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
+    ap.add_argument("--dit-dims", choices=["cfg3", "reference"], default="cfg3",
+                    help="dit workload: config 3's d1024/16 heads/2816, or the reference "
+                         "checkpoint's d1280/20 heads/3680")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         raise SystemExit("--warmup must be >= 3")
@@ -690,6 +814,8 @@ def main():
         run_profile_case(args)
     elif args.workload == "init" and args.impl == "ours":
         run_init(args)
+    elif args.workload == "dit" and args.impl == "ours":
+        run_dit(args)
     elif args.workload == "conv7" and args.impl == "ours":
         run_conv7(args)
     elif args.impl == "reference":

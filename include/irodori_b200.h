@@ -352,15 +352,58 @@ typedef struct {
 int iro_dit_rope_table(float *cos_out, float *sin_out, int S, int head_dim);
 size_t iro_dit_block_workspace_bytes(const IroDiTBlockDev *blk, int B, int S, int C,
                                      int context_batch);
-/* x [B*S, D] is updated in place; cond [B, 3*D]; ctx_k/ctx_v [context_batch,
-   C, D] (context_batch 1 = one context shared by the batch, dit.c:903-911);
-   mask [B, C] per batch row in either case (dit.c:811-813); rope_cos/sin
-   device [S, 32].  workspace NULL uses the library's scratch.  Returns IRO_OK
-   or IRO_ERR_*. */
-int iro_dit_block_dev(const IroDiTBlockDev *blk, float *x, const float *cond,
+/* x [B*S, D] is updated in place.  cond [cond_rows, 3*D]: cond_rows = B
+   (one conditioning row per batch row) or 1 (one row for the whole batch, as
+   in a sampler step where every row shares the timestep, sampler.c:246-253).
+   ctx_k/ctx_v [context_batch, C, D], context block b / (B / context_batch)
+   serving batch row b (1 = shared by the batch, dit.c:903-911; a request's
+   CFG rows share its block, sampler.c:219-224); mask [B, C] per batch row
+   (dit.c:811-813); rope_cos/sin device [S, 32].  workspace NULL uses the
+   library's scratch.  Returns IRO_OK or IRO_ERR_*. */
+int iro_dit_block_dev(const IroDiTBlockDev *blk, float *x, const float *cond, int cond_rows,
                       const float *ctx_k, const float *ctx_v, const uint8_t *ctx_mask,
                       int context_batch, int B, int S, int C, const float *rope_cos,
                       const float *rope_sin, void *workspace, void *stream);
+
+/* The blocks and the surrounding fp32 layers of the whole DiT (dit.c:137-
+   233): cond_w0 [D, timestep_dim], cond_w1 [D, D], cond_w2 [3D, D], in_w
+   [D, latent_dim], in_b [D], out_norm [D], out_w [latent_dim, D], out_b
+   [latent_dim]; device pointers. */
+#define IRO_DIT_MAX_LAYERS 16
+typedef struct {
+    IroDiTBlockDev block[IRO_DIT_MAX_LAYERS];
+    int layers;
+    const float *cond_w0, *cond_w1, *cond_w2;
+    const float *in_w, *in_b;
+    const float *out_norm, *out_w, *out_b;
+    int timestep_dim, latent_dim;
+    float norm_eps;
+} IroDiTModelDev;
+
+size_t iro_dit_step_workspace_bytes(const IroDiTModelDev *m, int R, int cfg, int S, int C);
+/* One Euler step of R requests (sampler.c:238-297): state [R, S, latent_dim]
+   on the device is advanced from t to t_next.  Each request runs cfg rows
+   (1 = conditional only; row i+1 is the i-th unconditional branch, guided
+   with cfg_scales[i], host floats, in the reference's order text, speaker,
+   caption of the active branches).  ctx_k[l], ctx_v[l]: host arrays of
+   device pointers, layer l's context K/V [R, C, D]; mask [R*cfg, C].
+   Returns IRO_OK or IRO_ERR_*. */
+int iro_dit_euler_step_dev(const IroDiTModelDev *m, float *state, int R, int cfg, int S,
+                           float t, float t_next, const float *cfg_scales,
+                           const float *const *ctx_k, const float *const *ctx_v,
+                           const uint8_t *mask, int C, void *workspace, void *stream);
+
+/* The Euler sampling loop (sampler.c:241-297) over `steps` steps from
+   init_scale down to 0: step i runs at t = (1 - i/steps) * init_scale, with
+   all cfg rows while cfg_min_t <= t <= cfg_max_t and the conditional row
+   alone outside that window.  Arguments as iro_dit_euler_step_dev; the
+   workspace is iro_dit_step_workspace_bytes(m, R, cfg, S, C).  The RoPE
+   tables are built once per call. */
+int iro_dit_sample_euler_dev(const IroDiTModelDev *m, float *state, int R, int cfg, int S,
+                             int steps, float init_scale, float cfg_min_t, float cfg_max_t,
+                             const float *cfg_scales, const float *const *ctx_k,
+                             const float *const *ctx_v, const uint8_t *mask, int C,
+                             void *workspace, void *stream);
 
 /* Checkpoints: safetensors files mapped read-only --------------------------------- */
 

@@ -80,8 +80,9 @@ __global__ void __launch_bounds__(256) adaln_params_kernel(
 }
 
 // h = x * inv * (1 + scale) + shift per row (dit.c:597-609), one warp per row.
+// The AdaLN parameters of batch row b are row (b / prow) of shift/scale.
 __global__ void __launch_bounds__(256) adaln_apply_kernel(const float* __restrict__ x, int rows,
-                                                          int S, int D, float eps,
+                                                          int S, int D, float eps, int prow,
                                                           const float* __restrict__ shift,
                                                           const float* __restrict__ scale,
                                                           float* __restrict__ h) {
@@ -94,7 +95,7 @@ __global__ void __launch_bounds__(256) adaln_apply_kernel(const float* __restric
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ms += __shfl_xor_sync(0xffffffffu, ms, o);
   const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, (float)D), eps)));
-  const int b = row / S;
+  const int b = row / S / prow;
   const float* sh = shift + (size_t)b * D;
   const float* sc = scale + (size_t)b * D;
   float* hr = h + (size_t)row * D;
@@ -176,7 +177,7 @@ struct AttnArgs {
   const float* cv;
   const int* clist;      // [B, C] valid context positions per batch row
   const int* ccount;     // [B]
-  int context_batch;     // 1 (shared) or B
+  int ctx_group;         // batch rows per context block
   int S, C, D;
   float* mix;
 };
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(AttnArgs a) {
   const int half = t & 1;       // which 32 keys / 32 dims
   const int qrow = q0 + qi;
   const bool qok = qrow < a.S;
-  const int cb = a.context_batch == 1 ? 0 : b;  // K/V row block
+  const int cb = b / a.ctx_group;  // K/V row block
   const int nctx = a.ccount[b];
   const int joined = a.S + nctx;
   const size_t base = (size_t)b * a.S;
@@ -290,14 +291,15 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(AttnArgs a) {
   }
 }
 
-// x += gate[b] * branch (dit.c:1013-1020).
+// x += gate[b] * branch (dit.c:1013-1020); gate row b / prow.
 __global__ void gated_residual_kernel(float* __restrict__ x, const float* __restrict__ branch,
-                                      const float* __restrict__ gate, long long n, int S, int D) {
+                                      const float* __restrict__ gate, long long n, int S, int D,
+                                      int prow) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
     const long long row = i / D;
     const int d = (int)(i - row * D);
-    const int b = (int)(row / S);
+    const int b = (int)(row / S) / prow;
     x[i] = __fadd_rn(x[i], __fmul_rn(gate[(size_t)b * D + d], branch[i]));
   }
 }
@@ -349,12 +351,13 @@ size_t iro_dit_block_workspace_bytes(const IroDiTBlockDev* blk, int B, int S, in
   return t;
 }
 
-int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond,
+int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, int cond_rows,
                       const float* ctx_k, const float* ctx_v, const uint8_t* ctx_mask,
                       int context_batch, int B, int S, int C, const float* rope_cos,
                       const float* rope_sin, void* workspace, void* stream) {
   if (!blk || !x || !cond || !ctx_k || !ctx_v || !ctx_mask || !rope_cos || !rope_sin ||
-      B <= 0 || S <= 0 || C <= 0 || (context_batch != 1 && context_batch != B))
+      B <= 0 || S <= 0 || C <= 0 || context_batch <= 0 || B % context_batch != 0 ||
+      (cond_rows != 1 && cond_rows != B))
     return IRO_ERR_INVALID;
   const int D = blk->model_dim, NH = blk->heads, R = blk->adaln_rank, H = blk->mlp_dim;
   if (blk->head_dim != kHD || NH * kHD != D || R <= 0 || H <= 0 || D % 16 != 0)
@@ -405,17 +408,18 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond,
   if ((st = check_launch())) return st;
 
   const size_t ada_smem = sizeof(float) * (size_t)(D + R);
+  const int prow = B / cond_rows;  // batch rows per AdaLN parameter row
   const long long n = (long long)M * D;
   const int res_blocks = (int)std::min<long long>((n + 255) / 256, (long long)c->num_sms * 16);
   for (int half = 0; half < 2; half++) {
     // AdaLN (attention: matrices 0..8, MLP: 9..17) and apply.
     AdaMats am;
     for (int i = 0; i < 9; i++) am.m[i] = blk->adaln[half][i];
-    adaln_params_kernel<<<dim3(B, 3), 256, ada_smem, s>>>(cond, D, R, am, ada[0], ada[1],
-                                                          ada[2]);
+    adaln_params_kernel<<<dim3(cond_rows, 3), 256, ada_smem, s>>>(cond, D, R, am, ada[0],
+                                                                  ada[1], ada[2]);
     if ((st = check_launch())) return st;
-    adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, ada[0],
-                                                       ada[1], h);
+    adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
+                                                       ada[0], ada[1], h);
     if ((st = check_launch())) return st;
     if (half == 0) {
       // QKVG on one quantised copy of h (dit.c:785-792).
@@ -440,7 +444,7 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond,
       qk_norm_rope_kernel<<<cdiv((int)M * NH, 8), 256, 0, s>>>(
           q, k, (int)M, S, D, NH, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
       if ((st = check_launch())) return st;
-      AttnArgs aa{q, k, v, g, ctx_k, ctx_v, clist, ccount, context_batch, S, C, D, mix};
+      AttnArgs aa{q, k, v, g, ctx_k, ctx_v, clist, ccount, B / context_batch, S, C, D, mix};
       attention_kernel<<<dim3(cdiv(S, kAQ), NH, B), kAThreads, 0, s>>>(aa);
       if ((st = check_launch())) return st;
       // Wo on the quantised gated mix (dit.c:876-884).
@@ -462,7 +466,7 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond,
                                (blk->residual_mask & 8) != 0, sw_ws, s);
       if (st) return st;
     }
-    gated_residual_kernel<<<res_blocks, 256, 0, s>>>(x, branch, ada[2], n, S, D);
+    gated_residual_kernel<<<res_blocks, 256, 0, s>>>(x, branch, ada[2], n, S, D, prow);
     if ((st = check_launch())) return st;
   }
   return IRO_OK;

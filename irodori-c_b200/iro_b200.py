@@ -128,7 +128,13 @@ SIGNATURES = {
     "iro_int8_dev_weight_from_st": (_i, [_DW, _vp, C.c_char_p, _i, C.c_char_p]),
     "iro_dit_rope_table": (_i, [_vp, _vp, _i, _i]),
     "iro_dit_block_workspace_bytes": (_sz, [_DB, _i, _i, _i, _i]),
-    "iro_dit_block_dev": (_i, [_DB, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "iro_dit_block_dev": (_i, [_DB, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp,
+                               _vp]),
+    "iro_dit_step_workspace_bytes": (_sz, [_vp, _i, _i, _i, _i]),
+    "iro_dit_euler_step_dev": (_i, [_vp, _vp, _i, _i, _i, C.c_float, C.c_float, _vp, _vp, _vp,
+                                    _vp, _i, _vp, _vp]),
+    "iro_dit_sample_euler_dev": (_i, [_vp, _vp, _i, _i, _i, _i, C.c_float, C.c_float, C.c_float,
+                                      _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
 }
 
@@ -601,10 +607,64 @@ class DiTBlock:
         self.st = st
 
     def run(self, x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C, rope_cos, rope_sin,
-            workspace=None, stream=None):
-        check(lib().iro_dit_block_dev(C.byref(self.st), _p(x), _p(cond), _p(ctx_k), _p(ctx_v),
+            cond_rows=None, workspace=None, stream=None):
+        check(lib().iro_dit_block_dev(C.byref(self.st), _p(x), _p(cond),
+                                      B if cond_rows is None else cond_rows, _p(ctx_k), _p(ctx_v),
                                       _p(mask), context_batch, B, S, C, _p(rope_cos),
                                       _p(rope_sin), _p(workspace), stream), "dit_block_dev")
+
+
+class IroDiTModelDev(C.Structure):
+    _fields_ = [("block", IroDiTBlockDev * 16), ("layers", C.c_int),
+                ("cond_w0", C.c_void_p), ("cond_w1", C.c_void_p), ("cond_w2", C.c_void_p),
+                ("in_w", C.c_void_p), ("in_b", C.c_void_p), ("out_norm", C.c_void_p),
+                ("out_w", C.c_void_p), ("out_b", C.c_void_p), ("timestep_dim", C.c_int),
+                ("latent_dim", C.c_int), ("norm_eps", C.c_float)]
+
+
+class DiTModel:
+    """The whole DiT on the device: blocks (DiTBlock) plus the conditioner,
+    input and output fp32 layers (host arrays, uploaded)."""
+
+    def __init__(self, blocks, cond_w0, cond_w1, cond_w2, in_w, in_b, out_norm, out_w, out_b,
+                 eps=1e-5):
+        self.blocks = list(blocks)
+        self.bufs = [DevBuf.from_host(np.ascontiguousarray(a, np.float32))
+                     for a in (cond_w0, cond_w1, cond_w2, in_w, in_b, out_norm, out_w, out_b)]
+        st = IroDiTModelDev()
+        for i, b in enumerate(self.blocks):
+            st.block[i] = b.st
+        st.layers = len(self.blocks)
+        (st.cond_w0, st.cond_w1, st.cond_w2, st.in_w, st.in_b, st.out_norm, st.out_w,
+         st.out_b) = [b.ptr for b in self.bufs]
+        st.timestep_dim = cond_w0.shape[1]
+        st.latent_dim = in_w.shape[1]
+        st.norm_eps = eps
+        self.st = st
+
+    def euler_step(self, state, R, cfg, S, t, t_next, cfg_scales, ctx_k, ctx_v, mask, C,
+                   workspace=None, stream=None):
+        """ctx_k/ctx_v: per layer DevBuf [R, C, D]; mask DevBuf [R*cfg, C]."""
+        ks = (_vp * len(ctx_k))(*[k.ptr for k in ctx_k])
+        vs = (_vp * len(ctx_v))(*[v.ptr for v in ctx_v])
+        sc = (C.c_float * 3)(*(list(cfg_scales) + [0.0] * (3 - len(cfg_scales))))
+        check(lib().iro_dit_euler_step_dev(C.byref(self.st), _p(state), R, cfg, S, t, t_next, sc,
+                                           ks, vs, _p(mask), C, _p(workspace), stream),
+              "dit_euler_step_dev")
+
+
+    def sample_euler(self, state, R, cfg, S, steps, init_scale, cfg_min_t, cfg_max_t,
+                     cfg_scales, ctx_k, ctx_v, mask, C, workspace=None, stream=None):
+        ks = (_vp * len(ctx_k))(*[k.ptr for k in ctx_k])
+        vs = (_vp * len(ctx_v))(*[v.ptr for v in ctx_v])
+        sc = (C.c_float * 3)(*(list(cfg_scales) + [0.0] * (3 - len(cfg_scales))))
+        check(lib().iro_dit_sample_euler_dev(C.byref(self.st), _p(state), R, cfg, S, steps,
+                                             init_scale, cfg_min_t, cfg_max_t, sc, ks, vs,
+                                             _p(mask), C, _p(workspace), stream),
+              "dit_sample_euler_dev")
+
+    def workspace_bytes(self, R, cfg, S, C):
+        return lib().iro_dit_step_workspace_bytes(C.byref(self.st), R, cfg, S, C)
 
 
 class StFile:

@@ -350,6 +350,12 @@ def ref_lib(kind="ieee"):
             L.ref_dit_block_int8.restype = C.c_int
             L.ref_dit_block_dims.argtypes = [C.POINTER(C.c_int)] * 4
             L.ref_dit_block_dims.restype = C.c_int
+            L.ref_dit_condition_w.argtypes = [_vp] * 4 + [C.c_int, _vp]
+            L.ref_dit_condition_w.restype = C.c_int
+            L.ref_dit_input_w.argtypes = [_vp] * 3 + [C.c_int, C.c_int, _vp]
+            L.ref_dit_input_w.restype = C.c_int
+            L.ref_dit_output_w.argtypes = [_vp] * 4 + [C.c_int, C.c_int, _vp]
+            L.ref_dit_output_w.restype = C.c_int
             L.ref_dit_dims.argtypes = [C.POINTER(C.c_int), C.POINTER(C.c_int)]
             L.ref_dit_dims.restype = C.c_int
         _ref_libs[kind] = L
@@ -511,6 +517,85 @@ def ref_dit_block(x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C_ctx, adaln
     if rc != 0:
         raise RuntimeError("reference dit_block failed")
     return x
+
+
+def ref_dit_condition(w0, w1, w2, t):
+    """dit.c:502-530 for timesteps t [B] -> cond [B, 3*1280]."""
+    t = _c(np.atleast_1d(t), np.float32)
+    out = np.empty((t.size, w2.shape[0]), np.float32)
+    ws = [_c(w, np.float32) for w in (w0, w1, w2)]
+    if ref_lib("dit").ref_dit_condition_w(*[_ptr(w) for w in ws], _ptr(t), t.size, _ptr(out)):
+        raise RuntimeError("reference conditioner failed")
+    return out
+
+
+def ref_dit_input(in_w, in_b, x, B, S):
+    """dit.c:532-541: x [B*S, 32] -> [B*S, 1280]."""
+    x = _c(x, np.float32)
+    out = np.empty((B * S, in_w.shape[0]), np.float32)
+    if ref_lib("dit").ref_dit_input_w(_ptr(_c(in_w, np.float32)), _ptr(_c(in_b, np.float32)),
+                                      _ptr(x), B, S, _ptr(out)):
+        raise RuntimeError("reference input projection failed")
+    return out
+
+
+def ref_dit_output(out_norm, out_w, out_b, x, B, S):
+    """dit.c:1070-1090: RMSNorm + linear -> velocity [B*S, 32]."""
+    x = _c(x, np.float32)
+    out = np.empty((B * S, out_w.shape[0]), np.float32)
+    if ref_lib("dit").ref_dit_output_w(_ptr(_c(out_norm, np.float32)), _ptr(_c(out_w, np.float32)),
+                                       _ptr(_c(out_b, np.float32)), _ptr(x), B, S, _ptr(out)):
+        raise RuntimeError("reference output head failed")
+    return out
+
+
+def ref_dit_euler_step(state, ctx_k, ctx_v, mask, blocks, head, R, cfg, S, C, t, t_next,
+                       scales):
+    """One Euler step of R independent requests composed from the
+    reference's own pieces, per request as sampler.c:241-297 runs it:
+    conditioner once (B=1) broadcast to the cfg rows, input projection
+    broadcast likewise, each layer's block with the request's shared context
+    (context_batch 1), the output head, then guided = v0 + sum_i s_i (v0 -
+    v_i) in row order and state += guided * dt in float32.
+
+    blocks: per layer (adaln, q_norm, k_norm, [8 Weight]).  Returns the new
+    state [R, S, 32]."""
+    D = head["in_w"].shape[0]
+    out = np.array(state, np.float32, copy=True)
+    for r in range(R):
+        cond = ref_dit_condition(head["cond_w0"], head["cond_w1"], head["cond_w2"],
+                                 np.float32(t))
+        proj = ref_dit_input(head["in_w"], head["in_b"], out[r], 1, S)
+        x = np.tile(proj, (cfg, 1))
+        cond_b = np.tile(cond, (cfg, 1))
+        m = mask[r * cfg:(r + 1) * cfg]
+        for l, (adaln, qn, kn, W) in enumerate(blocks):
+            x = ref_dit_block(x, cond_b, ctx_k[l][r:r + 1], ctx_v[l][r:r + 1], m, 1, cfg, S, C,
+                              adaln, qn, kn, W)
+        v = ref_dit_output(head["out_norm"], head["out_w"], head["out_b"], x, cfg, S)
+        v = v.reshape(cfg, S, -1)
+        g = v[0].copy()
+        for i in range(1, cfg):
+            g = g + np.float32(scales[i - 1]) * (v[0] - v[i])
+        dt = np.float32(np.float32(t_next) - np.float32(t))
+        out[r] = out[r] + g * dt
+    del D
+    return out
+
+
+def ref_dit_sample_euler(state, ctx_k, ctx_v, mask, blocks, head, R, cfg, S, C, steps,
+                         init_scale, cfg_min_t, cfg_max_t, scales):
+    """sampler.c:241-297's loop: the timestep schedule in float32 and the
+    conditional row alone outside [cfg_min_t, cfg_max_t]."""
+    f = np.float32
+    cond_rows = mask.reshape(R, cfg, C)[:, 0]
+    for step in range(steps):
+        u, un = f(step) / f(steps), f(step + 1) / f(steps)
+        t, tn = (f(1) - u) * f(init_scale), (f(1) - un) * f(init_scale)
+        use = cfg > 1 and f(cfg_min_t) <= t <= f(cfg_max_t)
+        state = ref_dit_euler_step(state, ctx_k, ctx_v, mask if use else cond_rows, blocks, head,
+                                   R, cfg if use else 1, S, C, t, tn, scales)
+    return state
 
 
 def ref_dit_block_dims():

@@ -87,3 +87,36 @@ int ref_dit_block_dims(int *model_dim, int *heads, int *rank, int *mlp_dim) {
     *mlp_dim = MLP_DIM;
     return 0;
 }
+
+/* The reference's conditioner, input projection and output head
+   (dit.c:488-541, 1070-1090) on caller-owned fp32 weights. */
+int ref_dit_condition_w(const float *w0, const float *w1, const float *w2,
+                        const float *t, int B, float *cond) {
+    IroDiT *d = calloc(1, sizeof(IroDiT));
+    if (!d) return -1;
+    d->cond_w0 = w0; d->cond_w1 = w1; d->cond_w2 = w2;
+    int rc = iro_dit_condition(d, t, B, cond);
+    free(d);
+    return rc;
+}
+
+int ref_dit_input_w(const float *in_w, const float *in_b, const float *x,
+                    int B, int S, float *out) {
+    IroDiT *d = calloc(1, sizeof(IroDiT));
+    if (!d) return -1;
+    d->in_w = in_w; d->in_b = in_b;
+    int rc = iro_dit_input(d, x, B, S, out);
+    free(d);
+    return rc;
+}
+
+int ref_dit_output_w(const float *out_norm, const float *out_w, const float *out_b,
+                     const float *x, int B, int S, float *velocity) {
+    IroDiT *d = calloc(1, sizeof(IroDiT));
+    if (!d) return -1;
+    d->out_norm = out_norm; d->out_w = out_w; d->out_b = out_b;
+    d->norm_eps = 1e-5f;
+    int rc = iro_dit_output(d, x, B, S, velocity);
+    free(d);
+    return rc;
+}

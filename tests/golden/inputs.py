@@ -142,6 +142,33 @@ def dit_block_case(seed, B, S, C, context_batch):
     return x, cond, ctx_k, ctx_v, mask, adaln, q_norm, k_norm, ws
 
 
+DIT_TIMESTEP, DIT_LATENT = 512, 32
+
+
+def dit_model_case(seed, layers, R, cfg, S, C):
+    """Synthetic inputs of whole DiT Euler steps: the latent state
+    [R, S, 32], per-layer context K/V [R, C, D] and block parameters (as
+    dit_block_case), the CFG mask [R*cfg, C], and the conditioner, input and
+    output weights in the reference's layouts (dit.c:488-541, 1070-1090)."""
+    D = DIT_D
+    rng = np.random.default_rng(seed)
+    f = lambda *sh, s=1.0: (rng.standard_normal(sh) * s).astype(np.float32)
+    state = f(R, S, DIT_LATENT)
+    mask = (rng.random((R * cfg, C)) < 0.75).astype(np.uint8)
+    mask[:, 0] = 1
+    ctx_k, ctx_v, blocks = [], [], []
+    for layer in range(layers):
+        ctx_k.append(f(R, C, D))
+        ctx_v.append(f(R, C, D))
+        _, _, _, _, _, adaln, qn, kn, ws = dit_block_case(seed * 100 + layer, 1, 1, 1, 1)
+        blocks.append((adaln, qn, kn, ws))
+    head = {"cond_w0": f(D, DIT_TIMESTEP, s=0.04), "cond_w1": f(D, D, s=0.03),
+            "cond_w2": f(3 * D, D, s=0.03), "in_w": f(D, DIT_LATENT, s=0.15),
+            "in_b": f(D, s=0.02), "out_norm": (1.0 + f(D, s=0.1)).astype(np.float32),
+            "out_w": f(DIT_LATENT, D, s=0.03), "out_b": f(DIT_LATENT, s=0.02)}
+    return state, ctx_k, ctx_v, mask, blocks, head
+
+
 def sym_input():
     rng = np.random.default_rng(77)
     x = rng.standard_normal((40, 96)).astype(np.float32)

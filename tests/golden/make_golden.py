@@ -190,7 +190,45 @@ def dit_block():
     return got
 
 
+# seed, layers, R, cfg, S, C; then the step's t, t_next and CFG scales, and the
+# sampler's steps, init_scale, cfg_min_t, cfg_max_t.
+DIT_STEP_CASE = (21, 2, 1, 3, 32, 16)
+DIT_STEP_T = (1.0, 0.5, (2.0, 1.5))
+DIT_SAMPLE = (2, 1.0, 0.6, 1.0)
+
+
+def dit_step_child():
+    seed, layers, R, cfg, S, C = DIT_STEP_CASE
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(*DIT_STEP_CASE)
+    bw = [(a, q, k, [oracle.ref_weight_quantize(w) for w in ws]) for a, q, k, ws in blocks]
+    t, tn, sc = DIT_STEP_T
+    steps, init, lo, hi = DIT_SAMPLE
+    flat = [state, *ck, *cv, mask] + [a for b in blocks for a in (*b[0], b[1], b[2], *b[3])]
+    res = {"case": np.array(DIT_STEP_CASE, np.int32),
+           "step_args": np.array([t, tn, *sc], np.float32),
+           "sample_args": np.array([steps, init, lo, hi], np.float32),
+           "inputs_sha": np.frombuffer(inputs.sha(*flat, *head.values()), np.uint8),
+           "step_out": oracle.ref_dit_euler_step(state, ck, cv, mask, bw, head, R, cfg, S, C, t,
+                                                 tn, sc),
+           "sample_out": oracle.ref_dit_sample_euler(state, ck, cv, mask, bw, head, R, cfg, S, C,
+                                                     steps, init, lo, hi, sc)}
+    np.savez(os.path.join(HERE, "_tmp_dit_step.npz"), **res)
+
+
+def dit_step():
+    e = dict(os.environ)
+    e.pop("IRO_INT8_RESIDUAL", None)
+    subprocess.run([sys.executable, __file__, "--dit-step-child", "x"], check=True, env=e)
+    path = os.path.join(HERE, "_tmp_dit_step.npz")
+    got = dict(np.load(path))
+    os.remove(path)
+    return got
+
+
 def main():
+    if len(sys.argv) > 2 and sys.argv[1] == "--dit-step-child":
+        dit_step_child()
+        return
     if len(sys.argv) > 2 and sys.argv[1] == "--dit-block-child":
         dit_block_child()
         return
@@ -203,7 +241,8 @@ def main():
     only = set(sys.argv[1:])
     for name, fn in (("int8_ops", int8_ops), ("residual", residual), ("conv7", conv7),
                      ("sym_quant", sym), ("dit_swiglu", dit_swiglu), ("convt", convt),
-                     ("conv1", conv1), ("dit_block", dit_block)):
+                     ("conv1", conv1), ("dit_block", dit_block),
+                     ("dit_step", dit_step)):
         if only and name not in only:
             continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())

@@ -1,0 +1,113 @@
+"""Whole DiT Euler steps on the device (iro_dit_euler_step_dev and the
+sampling loop iro_dit_sample_euler_dev, sampler.c:241-297) against the
+reference's own conditioner, input projection, blocks and output head
+composed per request (oracle.ref_dit_euler_step): the committed fixture
+tests/golden/dit_step.npz and, where the reference build is present, live
+cases with several requests.
+
+The fp32 conditioner, input and output linears sum in the reference's order;
+the blocks carry the block tolerance (their support math sums in another
+order and requantises activations), so the bar is on the state update
+(new state - old state = guided velocity x dt): max error <= 5e-3 x its
+largest magnitude and mean error <= 5e-4 x that magnitude."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import iro_b200 as iro
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+sys.path.insert(0, GOLDEN)
+import inputs  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 5e-3
+MEAN_REL = 5e-4
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    iro.init(0)
+    yield
+
+
+def build_model(blocks, head):
+    dev_blocks = []
+    for adaln, qn, kn, ws in blocks:
+        W = [oracle.weight_quantize(w) for w in ws]
+        dev_blocks.append(iro.DiTBlock(adaln, qn, kn, *[(w.data, w.scale, w.colsum) for w in W]))
+    m = iro.DiTModel(dev_blocks, head["cond_w0"], head["cond_w1"], head["cond_w2"], head["in_w"],
+                     head["in_b"], head["out_norm"], head["out_w"], head["out_b"])
+    return m
+
+
+def dev_context(ck, cv, mask):
+    return ([iro.DevBuf.from_host(k) for k in ck], [iro.DevBuf.from_host(v) for v in cv],
+            iro.DevBuf.from_host(mask))
+
+
+def check_update(got, want, state, what):
+    dg = got.astype(np.float64) - state
+    dw = want.astype(np.float64) - state
+    err = np.abs(dg - dw)
+    scale = float(np.abs(dw).max())
+    print(f"{what}: max err {err.max():.3e} mean {err.mean():.3e} (max |update| {scale:.3f})")
+    assert np.isfinite(got).all()
+    assert err.max() <= MAX_REL * scale, what
+    assert err.mean() <= MEAN_REL * scale, what
+
+
+def test_euler_step_and_sampler_match_fixture():
+    g = np.load(os.path.join(GOLDEN, "dit_step.npz"))
+    seed, layers, R, cfg, S, C = (int(v) for v in g["case"])
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(seed, layers, R, cfg, S, C)
+    flat = [state, *ck, *cv, mask] + [a for b in blocks for a in (*b[0], b[1], b[2], *b[3])]
+    assert bytes(g["inputs_sha"]) == inputs.sha(*flat, *head.values())
+    t, tn, s1, s2 = (float(v) for v in g["step_args"])
+    steps, init, lo, hi = (float(v) for v in g["sample_args"])
+    m = build_model(blocks, head)
+    kd, vd, md = dev_context(ck, cv, mask)
+
+    sd = iro.DevBuf.from_host(state)
+    m.euler_step(sd, R, cfg, S, t, tn, [s1, s2], kd, vd, md, C)
+    iro.synchronize()
+    check_update(sd.get().reshape(state.shape), g["step_out"], state, "fixture step")
+
+    sd = iro.DevBuf.from_host(state)
+    m.sample_euler(sd, R, cfg, S, int(steps), init, lo, hi, [s1, s2], kd, vd, md, C)
+    iro.synchronize()
+    check_update(sd.get().reshape(state.shape), g["sample_out"], state, "fixture sampler")
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(oracle.REF_DIR, "libiro_ref_dit.so")),
+                    reason="reference build absent")
+@pytest.mark.parametrize("R,cfg,S,C", [(2, 4, 40, 24), (3, 1, 33, 7)])
+def test_euler_step_matches_reference(R, cfg, S, C):
+    if os.environ.get("IRO_INT8_RESIDUAL"):
+        pytest.skip("the reference reads its residual policy from the environment")
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(R * 10 + S, 2, R, cfg, S, C)
+    scales = [1.5, 0.7, 2.5][:cfg - 1]
+    m = build_model(blocks, head)
+    kd, vd, md = dev_context(ck, cv, mask)
+    sd = iro.DevBuf.from_host(state)
+    ws = iro.DevBuf(m.workspace_bytes(R, cfg, S, C), np.uint8)
+    m.euler_step(sd, R, cfg, S, 0.8, 0.6, scales, kd, vd, md, C, workspace=ws)
+    iro.synchronize()
+    bw = [(a, q, k, [oracle.weight_quantize(w) for w in ws_]) for a, q, k, ws_ in blocks]
+    want = oracle.ref_dit_euler_step(state, ck, cv, mask, bw, head, R, cfg, S, C, 0.8, 0.6, scales)
+    check_update(sd.get().reshape(state.shape), want, state, f"R={R} cfg={cfg} S={S} C={C}")
+
+
+def test_step_rejects_bad_arguments():
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(3, 1, 1, 2, 8, 4)
+    m = build_model(blocks, head)
+    kd, vd, md = dev_context(ck, cv, mask)
+    sd = iro.DevBuf.from_host(state)
+    with pytest.raises(iro.IroError):  # five CFG rows
+        m.euler_step(sd, 1, 5, 8, 1.0, 0.5, [1.0, 1.0, 1.0], kd, vd, md, 4)
+    with pytest.raises(iro.IroError):  # no steps
+        m.sample_euler(sd, 1, 2, 8, 0, 1.0, 0.0, 1.0, [1.0], kd, vd, md, 4)
