@@ -744,8 +744,10 @@ def run_dit(args):
         state.copy_(host_in, non_blocking=True)
     sample(args.warmup)
     iro.synchronize()
-    n1 = _count_kernels(lambda: sample(1))
-    n2 = _count_kernels(lambda: sample(2))
+    n1 = n2 = None
+    if not args.no_count:
+        n1 = _count_kernels(lambda: sample(1))
+        n2 = _count_kernels(lambda: sample(2))
     clocks = ClockSampler(physical_gpu(0))
     clocks.start()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -807,6 +809,8 @@ def main():
     ap.add_argument("--dit-dims", choices=["cfg3", "reference"], default="cfg3",
                     help="dit workload: config 3's d1024/16 heads/2816, or the reference "
                          "checkpoint's d1280/20 heads/3680")
+    ap.add_argument("--no-count", action="store_true",
+                    help="dit workload: skip the profiler-based launch count (for ncu runs)")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         raise SystemExit("--warmup must be >= 3")

@@ -393,6 +393,24 @@ int iro_dit_euler_step_dev(const IroDiTModelDev *m, float *state, int R, int cfg
                            const float *const *ctx_k, const float *const *ctx_v,
                            const uint8_t *mask, int C, void *workspace, void *stream);
 
+/* The reference's public DiT pieces on device buffers (dit.c:502-541,
+   1070-1090), stream-ordered; workspace NULL uses the library arena.
+   iro_dit_condition_dev: t [B] host floats -> cond [B, 3*model_dim]
+   (replaces iro_dit_condition, dit.c:502); workspace is
+   iro_dit_stage_workspace_bytes(m, B).  iro_dit_input_dev: x [B*S, latent]
+   -> projected [B*S, model_dim] (replaces iro_dit_input, dit.c:532).
+   iro_dit_output_dev: RMSNorm + linear -> velocity [B*S, latent] (replaces
+   iro_dit_output, dit.c:1070); workspace >= 4*B*S*model_dim bytes.  The fp32
+   linears sum each output in the reference's scalar order without fused
+   multiply-adds. */
+size_t iro_dit_stage_workspace_bytes(const IroDiTModelDev *m, int rows);
+int iro_dit_condition_dev(const IroDiTModelDev *m, const float *t, int B, float *cond,
+                          void *workspace, void *stream);
+int iro_dit_input_dev(const IroDiTModelDev *m, const float *x, int B, int S, float *projected,
+                      void *stream);
+int iro_dit_output_dev(const IroDiTModelDev *m, const float *x, int B, int S, float *velocity,
+                       void *workspace, void *stream);
+
 /* The Euler sampling loop (sampler.c:241-297) over `steps` steps from
    init_scale down to 0: step i runs at t = (1 - i/steps) * init_scale, with
    all cfg rows while cfg_min_t <= t <= cfg_max_t and the conditional row

@@ -86,10 +86,15 @@ int linear_ref(const float* x, const float* w, const float* bias, float* y, int 
 }
 
 // dit.c:488-500: [cos(t f_i) | sin(t f_i)], f_i = 1000 exp(-ln(1e4) i / half).
-__global__ void timestep_embedding_kernel(float t, int dim, float* __restrict__ emb) {
+// Row b = blockIdx.y takes its timestep from t_dev[b], or t_scalar when
+// t_dev is null.
+__global__ void timestep_embedding_kernel(const float* __restrict__ t_dev, float t_scalar,
+                                          int dim, float* __restrict__ emb_rows) {
   const int half = dim / 2;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= half) return;
+  const float t = t_dev ? t_dev[blockIdx.y] : t_scalar;
+  float* emb = emb_rows + (size_t)blockIdx.y * dim;
   const float log_theta = logf(10000.0f);
   const float freq = __fmul_rn(1000.0f, expf(__fdiv_rn(__fmul_rn(-log_theta, (float)i), (float)half)));
   const float arg = __fmul_rn(t, freq);
@@ -238,7 +243,7 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
   void* blk_ws = ws + off;
   int st;
   // Conditioner, once: every row shares the timestep.
-  timestep_embedding_kernel<<<cdiv(TD / 2, 128), 128, 0, s>>>(t, TD, emb);
+  timestep_embedding_kernel<<<cdiv(TD / 2, 128), 128, 0, s>>>(nullptr, t, TD, emb);
   if ((st = check_launch())) return st;
   if ((st = linear_ref(emb, m->cond_w0, nullptr, h0, 1, D, TD, 1, s))) return st;
   if ((st = linear_ref(h0, m->cond_w1, nullptr, h1, 1, D, D, 1, s))) return st;
@@ -354,6 +359,74 @@ int iro_dit_sample_euler_dev(const IroDiTModelDev* m, float* state, int R, int c
     if (st) return st;
   }
   return IRO_OK;
+}
+
+// The reference's public DiT pieces on device buffers, for callers that
+// compose their own loop and for stage-level parity.
+
+size_t iro_dit_stage_workspace_bytes(const IroDiTModelDev* m, int rows) {
+  if (!valid_model(m) || rows <= 0) return 0;
+  const size_t D = (size_t)m->block[0].model_dim;
+  return al256(sizeof(float) * rows) + al256(sizeof(float) * rows * m->timestep_dim) +
+         2 * al256(sizeof(float) * rows * D) + al256(sizeof(float) * rows * D);
+}
+
+int iro_dit_condition_dev(const IroDiTModelDev* m, const float* t, int B, float* cond,
+                          void* workspace, void* stream) {
+  if (!valid_model(m) || !t || B <= 0 || !cond) return IRO_ERR_INVALID;
+  int st;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  cudaStream_t s = pick_stream(c, stream);
+  const int D = m->block[0].model_dim, TD = m->timestep_dim;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (!ws) {
+    ws = static_cast<uint8_t*>(arena_get(c, iro_dit_stage_workspace_bytes(m, B), &st));
+    if (!ws) return st;
+  }
+  float* td = reinterpret_cast<float*>(ws);
+  float* emb = reinterpret_cast<float*>(ws + al256(sizeof(float) * B));
+  float* h0 = emb + al256(sizeof(float) * (size_t)B * TD) / sizeof(float);
+  float* h1 = h0 + al256(sizeof(float) * (size_t)B * D) / sizeof(float);
+  // Pageable source: the copy is staged before the call returns.
+  cudaError_t e = cudaMemcpyAsync(td, t, sizeof(float) * B, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return map_cuda(e);
+  }
+  timestep_embedding_kernel<<<dim3(cdiv(TD / 2, 128), B), 128, 0, s>>>(td, 0.0f, TD, emb);
+  if ((st = check_launch())) return st;
+  if ((st = linear_ref(emb, m->cond_w0, nullptr, h0, B, D, TD, 1, s))) return st;
+  if ((st = linear_ref(h0, m->cond_w1, nullptr, h1, B, D, D, 1, s))) return st;
+  return linear_ref(h1, m->cond_w2, nullptr, cond, B, 3 * D, D, 0, s);
+}
+
+int iro_dit_input_dev(const IroDiTModelDev* m, const float* x, int B, int S, float* projected,
+                      void* stream) {
+  if (!valid_model(m) || !x || B <= 0 || S <= 0 || !projected) return IRO_ERR_INVALID;
+  int st;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  return linear_ref(x, m->in_w, m->in_b, projected, B * S, m->block[0].model_dim, m->latent_dim,
+                    0, pick_stream(c, stream));
+}
+
+int iro_dit_output_dev(const IroDiTModelDev* m, const float* x, int B, int S, float* velocity,
+                       void* workspace, void* stream) {
+  if (!valid_model(m) || !x || B <= 0 || S <= 0 || !velocity) return IRO_ERR_INVALID;
+  int st;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  cudaStream_t s = pick_stream(c, stream);
+  const int D = m->block[0].model_dim, rows = B * S;
+  float* norm = static_cast<float*>(workspace);
+  if (!norm) {
+    norm = static_cast<float*>(arena_get(c, sizeof(float) * (size_t)rows * D, &st));
+    if (!norm) return st;
+  }
+  rmsnorm_ref_kernel<<<cdiv(rows, 128), 128, 0, s>>>(x, m->out_norm, norm, rows, D, m->norm_eps);
+  if ((st = check_launch())) return st;
+  return linear_ref(norm, m->out_w, m->out_b, velocity, rows, m->latent_dim, D, 0, s);
 }
 
 }  // extern "C"

@@ -133,6 +133,10 @@ SIGNATURES = {
     "iro_dit_step_workspace_bytes": (_sz, [_vp, _i, _i, _i, _i]),
     "iro_dit_euler_step_dev": (_i, [_vp, _vp, _i, _i, _i, C.c_float, C.c_float, _vp, _vp, _vp,
                                     _vp, _i, _vp, _vp]),
+    "iro_dit_stage_workspace_bytes": (_sz, [_vp, _i]),
+    "iro_dit_condition_dev": (_i, [_vp, _vp, _i, _vp, _vp, _vp]),
+    "iro_dit_input_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "iro_dit_output_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
     "iro_dit_sample_euler_dev": (_i, [_vp, _vp, _i, _i, _i, _i, C.c_float, C.c_float, C.c_float,
                                       _vp, _vp, _vp, _vp, _i, _vp, _vp]),
     "iro_debug_bounded_wait_probe": (_i, [_u64]),
@@ -606,11 +610,11 @@ class DiTBlock:
         st.norm_eps, st.residual_mask = eps, residual_mask
         self.st = st
 
-    def run(self, x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C, rope_cos, rope_sin,
+    def run(self, x, cond, ctx_k, ctx_v, mask, context_batch, B, S, n_ctx, rope_cos, rope_sin,
             cond_rows=None, workspace=None, stream=None):
         check(lib().iro_dit_block_dev(C.byref(self.st), _p(x), _p(cond),
                                       B if cond_rows is None else cond_rows, _p(ctx_k), _p(ctx_v),
-                                      _p(mask), context_batch, B, S, C, _p(rope_cos),
+                                      _p(mask), context_batch, B, S, n_ctx, _p(rope_cos),
                                       _p(rope_sin), _p(workspace), stream), "dit_block_dev")
 
 
@@ -642,29 +646,41 @@ class DiTModel:
         st.norm_eps = eps
         self.st = st
 
-    def euler_step(self, state, R, cfg, S, t, t_next, cfg_scales, ctx_k, ctx_v, mask, C,
+    def euler_step(self, state, R, cfg, S, t, t_next, cfg_scales, ctx_k, ctx_v, mask, n_ctx,
                    workspace=None, stream=None):
         """ctx_k/ctx_v: per layer DevBuf [R, C, D]; mask DevBuf [R*cfg, C]."""
         ks = (_vp * len(ctx_k))(*[k.ptr for k in ctx_k])
         vs = (_vp * len(ctx_v))(*[v.ptr for v in ctx_v])
         sc = (C.c_float * 3)(*(list(cfg_scales) + [0.0] * (3 - len(cfg_scales))))
         check(lib().iro_dit_euler_step_dev(C.byref(self.st), _p(state), R, cfg, S, t, t_next, sc,
-                                           ks, vs, _p(mask), C, _p(workspace), stream),
+                                           ks, vs, _p(mask), n_ctx, _p(workspace), stream),
               "dit_euler_step_dev")
 
-
     def sample_euler(self, state, R, cfg, S, steps, init_scale, cfg_min_t, cfg_max_t,
-                     cfg_scales, ctx_k, ctx_v, mask, C, workspace=None, stream=None):
+                     cfg_scales, ctx_k, ctx_v, mask, n_ctx, workspace=None, stream=None):
         ks = (_vp * len(ctx_k))(*[k.ptr for k in ctx_k])
         vs = (_vp * len(ctx_v))(*[v.ptr for v in ctx_v])
         sc = (C.c_float * 3)(*(list(cfg_scales) + [0.0] * (3 - len(cfg_scales))))
         check(lib().iro_dit_sample_euler_dev(C.byref(self.st), _p(state), R, cfg, S, steps,
                                              init_scale, cfg_min_t, cfg_max_t, sc, ks, vs,
-                                             _p(mask), C, _p(workspace), stream),
+                                             _p(mask), n_ctx, _p(workspace), stream),
               "dit_sample_euler_dev")
 
-    def workspace_bytes(self, R, cfg, S, C):
-        return lib().iro_dit_step_workspace_bytes(C.byref(self.st), R, cfg, S, C)
+    def condition(self, t, cond):
+        t = np.ascontiguousarray(np.atleast_1d(t), np.float32)
+        check(lib().iro_dit_condition_dev(C.byref(self.st), _p(t), t.size, _p(cond), None, None),
+              "dit_condition_dev")
+
+    def input(self, x, B, S, projected):
+        check(lib().iro_dit_input_dev(C.byref(self.st), _p(x), B, S, _p(projected), None),
+              "dit_input_dev")
+
+    def output(self, x, B, S, velocity):
+        check(lib().iro_dit_output_dev(C.byref(self.st), _p(x), B, S, _p(velocity), None, None),
+              "dit_output_dev")
+
+    def workspace_bytes(self, R, cfg, S, n_ctx):
+        return lib().iro_dit_step_workspace_bytes(C.byref(self.st), R, cfg, S, n_ctx)
 
 
 class StFile:

@@ -59,3 +59,19 @@ def test_header_has_reference_citations():
     for cite in ("ops.c:259-293", "ops.c:321-348", "ops.c:450-491", "ops.c:427-442",
                  "ops.c:375-398", "dacvae.c:543-688", "dit.c:785-792", "dit.c:913-969"):
         assert cite in txt, cite
+
+
+def test_wrappers_do_not_shadow_ctypes():
+    """The bindings import ctypes as `C`; a parameter of that name inside a
+    function that also calls C.byref/C.c_float breaks only at run time."""
+    import ast
+    src = open(os.path.join(os.path.dirname(iro.__file__), "iro_b200.py")).read()
+    bad = []
+    for node in ast.walk(ast.parse(src)):
+        if isinstance(node, (ast.FunctionDef, ast.Lambda)):
+            a = node.args
+            names = {x.arg for x in a.args + a.kwonlyargs + a.posonlyargs}
+            if "C" in names and any(isinstance(n, ast.Attribute) and isinstance(n.value, ast.Name)
+                                    and n.value.id == "C" for n in ast.walk(node)):
+                bad.append(getattr(node, "name", "lambda"))
+    assert not bad, bad

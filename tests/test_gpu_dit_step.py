@@ -3,13 +3,17 @@ sampling loop iro_dit_sample_euler_dev, sampler.c:241-297) against the
 reference's own conditioner, input projection, blocks and output head
 composed per request (oracle.ref_dit_euler_step): the committed fixture
 tests/golden/dit_step.npz and, where the reference build is present, live
-cases with several requests.
+cases with several requests.  The stage entry points are checked on their
+own first: the input projection and output head bit-exact against the
+reference's IEEE build, the conditioner to a few ulps (CUDA's expf, cosf and
+sinf against glibc's).
 
-The fp32 conditioner, input and output linears sum in the reference's order;
-the blocks carry the block tolerance (their support math sums in another
-order and requantises activations), so the bar is on the state update
-(new state - old state = guided velocity x dt): max error <= 5e-3 x its
-largest magnitude and mean error <= 5e-4 x that magnitude."""
+The blocks carry the block tolerance, and the CFG combination scales
+velocity differences by up to 1 + sum(scales), so the bar is on the state
+update (new state - old state = guided velocity x dt).  A one-ulp
+perturbation of the reference's own input state moves its update by up to
+4.6e-3 x max |update| (mean 6e-4 x max |update|) on these cases; the bar is
+max error <= 2e-2 x max |update| and mean error <= 3e-3 x max |update|."""
 import os
 import sys
 
@@ -25,8 +29,8 @@ import inputs  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-MAX_REL = 5e-3
-MEAN_REL = 5e-4
+MAX_REL = 2e-2
+MEAN_REL = 3e-3
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -59,6 +63,39 @@ def check_update(got, want, state, what):
     assert np.isfinite(got).all()
     assert err.max() <= MAX_REL * scale, what
     assert err.mean() <= MEAN_REL * scale, what
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(oracle.REF_DIR, "libiro_ref_dit.so")),
+                    reason="reference build absent")
+def test_stage_entry_points_match_reference():
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(9, 1, 2, 1, 37, 4)
+    m = build_model(blocks, head)
+    D = head["in_w"].shape[0]
+    B, S = 2, 37
+    # Input projection: bit-exact.
+    xd = iro.DevBuf.from_host(state)
+    proj = iro.DevBuf((B * S, D), np.float32)
+    m.input(xd, B, S, proj)
+    iro.synchronize()
+    want = oracle.ref_dit_input(head["in_w"], head["in_b"], state.reshape(B * S, -1), B, S)
+    assert (proj.get().view(np.uint32) == want.view(np.uint32)).all()
+    # Output head on a hidden state: bit-exact.
+    rng = np.random.default_rng(2)
+    hid = (rng.standard_normal((B * S, D)) * 2).astype(np.float32)
+    vel = iro.DevBuf((B * S, 32), np.float32)
+    m.output(iro.DevBuf.from_host(hid), B, S, vel)
+    iro.synchronize()
+    want = oracle.ref_dit_output(head["out_norm"], head["out_w"], head["out_b"], hid, B, S)
+    assert (vel.get().view(np.uint32) == want.view(np.uint32)).all()
+    # Conditioner: transcendental functions differ by ulps.
+    t = np.array([1.0, 0.5, 0.125, 0.0], np.float32)
+    cond = iro.DevBuf((t.size, 3 * D), np.float32)
+    m.condition(t, cond)
+    iro.synchronize()
+    want = oracle.ref_dit_condition(head["cond_w0"], head["cond_w1"], head["cond_w2"], t)
+    err = np.abs(cond.get().astype(np.float64) - want)
+    print(f"conditioner max err {err.max():.3e} (max |ref| {np.abs(want).max():.3f})")
+    assert err.max() <= 1e-5 * np.abs(want).max()
 
 
 def test_euler_step_and_sampler_match_fixture():

@@ -157,6 +157,54 @@ def _edge_matrix(rng, M, K):
     return x
 
 
+@pytest.fixture(scope="module")
+def ref_dit():
+    if not oracle.ref_available("dit"):
+        pytest.skip("oracle/_ref reference DiT build is not present")
+    if os.environ.get("IRO_INT8_RESIDUAL"):
+        pytest.skip("the reference reads its residual policy from the environment")
+    return oracle
+
+
+def test_golden_dit_block_and_step_reproduced(ref_dit):
+    """The committed DiT fixtures are what the reference block, and the
+    step composed from the reference's pieces, produce now."""
+    g = load("dit_block")
+    seed, B, S, C, cb = (int(v) for v in g["c0_case"])
+    x, cond, ck, cv, mask, adaln, qn, kn, ws = inputs.dit_block_case(seed, B, S, C, cb)
+    W = [oracle.weight_quantize(w) for w in ws]
+    assert same(oracle.ref_dit_block(x, cond, ck, cv, mask, cb, B, S, C, adaln, qn, kn, W),
+                g["c0_out"])
+    g = load("dit_step")
+    seed, layers, R, cfg, S, C = (int(v) for v in g["case"])
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(seed, layers, R, cfg, S, C)
+    bw = [(a, q, k, [oracle.weight_quantize(w) for w in w8]) for a, q, k, w8 in blocks]
+    t, tn, s1, s2 = (float(v) for v in g["step_args"])
+    assert same(oracle.ref_dit_euler_step(state, ck, cv, mask, bw, head, R, cfg, S, C, t, tn,
+                                          [s1, s2]), g["step_out"])
+
+
+def test_reference_dit_block_sensitivity(ref_dit):
+    """The int8 block is sensitive to fp32 rounding: a one-ulp perturbation
+    of the reference's own input moves its output by about 1e-3 of its
+    magnitude (an activation code moves by one step and the MLP amplifies
+    it).  The GPU block tolerance (5e-3 max, 1.5e-4 mean, relative to
+    max |out|) is set just above this envelope; this test keeps the
+    measurement behind that bound reproducible."""
+    seed, B, S, C, cb = 303, 3, 130, 33, 3
+    x, cond, ck, cv, mask, adaln, qn, kn, ws = inputs.dit_block_case(seed, B, S, C, cb)
+    W = [oracle.weight_quantize(w) for w in ws]
+    base = oracle.ref_dit_block(x, cond, ck, cv, mask, cb, B, S, C, adaln, qn, kn, W)
+    scale = float(np.abs(base).max())
+    rng = np.random.default_rng(1)
+    worst = 0.0
+    for _ in range(2):
+        xp = (x * (1 + rng.choice([-1, 1], x.shape) * 2.0 ** -23)).astype(np.float32)
+        out = oracle.ref_dit_block(xp, cond, ck, cv, mask, cb, B, S, C, adaln, qn, kn, W)
+        worst = max(worst, float(np.abs(out.astype(np.float64) - base).max()) / scale)
+    assert 5e-4 < worst < 5e-3, worst
+
+
 @pytest.mark.parametrize("M,K", [(9, 16), (16, 100), (24, 1027), (12, 2816)])
 def test_live_quantisers_match_reference(ref, M, K):
     rng = np.random.default_rng(M * K)
