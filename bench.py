@@ -524,6 +524,34 @@ def run_profile_case(args):
         print(f"profile case conv7: {args.warmup + args.steps} launches ok")
         return
 
+    if args.profile == "ditblock":
+        # One config-3 DiT block (d1024, 16 heads, mlp 2816) over 4 CFG rows of
+        # one request x 750 frames (3000 rows), 128 context tokens: 12 MB per
+        # activation tensor, a few hundred MB on the device in all.
+        Dm, NH, Hm, RK, Bq, Sq, Cx = 1024, 16, 2816, 192, 4, 750, 128
+        iro.init(0)
+        rng = np.random.default_rng(9)
+        f = lambda *sh, sc=1.0: rng.standard_normal(sh, dtype=np.float32) * np.float32(sc)
+        adaln = []
+        for _ in range(6):
+            adaln += [f(RK, Dm, sc=0.03), f(Dm, RK, sc=0.03), f(Dm, sc=0.02)]
+        wts = [iro.HostWeight(f(Dm, Dm, sc=0.03)) for _ in range(5)]
+        wts += [iro.HostWeight(f(Hm, Dm, sc=0.03)), iro.HostWeight(f(Hm, Dm, sc=0.03)),
+                iro.HostWeight(f(Dm, Hm, sc=0.02))]
+        blk = iro.DiTBlock(adaln, 1.0 + f(Dm, sc=0.1), 1.0 + f(Dm, sc=0.1), *wts, model_dim=Dm,
+                           heads=NH, rank=RK, mlp_dim=Hm)
+        xd = iro.DevBuf.from_host(f(Bq * Sq, Dm))
+        cond = iro.DevBuf.from_host(f(1, 3 * Dm, sc=0.5))
+        ck, cv = iro.DevBuf.from_host(f(1, Cx, Dm)), iro.DevBuf.from_host(f(1, Cx, Dm))
+        mask = iro.DevBuf.from_host(np.ones((Bq, Cx), np.uint8))
+        rc, rs = iro.dit_rope_table(Sq)
+        rcd, rsd = iro.DevBuf.from_host(rc), iro.DevBuf.from_host(rs)
+        for _ in range(args.warmup + args.steps):
+            blk.run(xd, cond, ck, cv, mask, 1, Bq, Sq, Cx, rcd, rsd, cond_rows=1)
+        iro.synchronize()
+        print(f"profile case ditblock: {args.warmup + args.steps} blocks ok")
+        return
+
     global NSETS
     NSETS = 1
     iro.init(0)
@@ -779,7 +807,7 @@ def run_dit(args):
     print(json.dumps({
         "metric": "DiT Euler steps/sec", "value": round(1000.0 / ms, 3), "unit": "steps/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMMs, fp32 attention",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMMs, tf32 attention (fp32 accumulate)",
         "data": "synthetic (random-init weights, N(0,1) latents)",
         "e2e": {"value": round(1000.0 / ms_e2e, 3), "unit": "steps/s",
                 "h2d_bytes_per_step": host_in.numel() * 4 / args.steps,
@@ -804,7 +832,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--workload", choices=["swiglu", "conv7", "init", "dit"], default="swiglu",
                     help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
-    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7"],
+    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7", "ditblock"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
     ap.add_argument("--dit-dims", choices=["cfg3", "reference"], default="cfg3",
                     help="dit workload: config 3's d1024/16 heads/2816, or the reference "

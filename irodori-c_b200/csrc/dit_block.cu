@@ -6,7 +6,9 @@
 //   AdaLN apply    (dit.c:597-609)           adaln_apply_kernel
 //   QKVG           (dit.c:785-792)           one int8 GEMM, four outputs
 //   head RMSNorm + half RoPE (dit.c:638-706) qk_norm_rope_kernel
-//   joint attention, sigmoid gate (dit.c:806-862)  attention_kernel
+//   joint attention, sigmoid gate (dit.c:806-862)  attention_tc_kernel
+//                  (dit_attention.cu; tf32 tensor cores), or attention_kernel
+//                  (fp32 CUDA cores)
 //   Wo             (dit.c:876-884)           int8 GEMM
 //   gated residual (dit.c:1013-1020)         gated_residual_kernel
 //   SwiGLU         (dit.c:913-969)           iro_int8_swiglu_dev
@@ -21,6 +23,8 @@
 #include <algorithm>
 #include <vector>
 
+#include "dit_attention.cuh"
+#include "dit_block.cuh"
 #include "gemm_i8.cuh"
 #include "quantize.cuh"
 
@@ -40,42 +44,72 @@ struct AdaMats {
   const float* m[9];
 };
 
-// One (batch row, branch) per block.  out = up(down(silu(c))) + bias + c for
-// c = cond[b, branch*D .. +D]; the gate branch (2) ends in tanhf.
-__global__ void __launch_bounds__(256) adaln_params_kernel(
-    const float* __restrict__ cond, int D, int R, const AdaMats mats,
-    float* __restrict__ shift, float* __restrict__ scale, float* __restrict__ gate) {
-  extern __shared__ float sh[];
-  float* act = sh;       // [D]
-  float* low = sh + D;   // [R]
-  const int b = blockIdx.x, br = blockIdx.y;
-  const float* c = cond + (size_t)b * 3 * D + (size_t)br * D;
-  const float* down = mats.m[3 * br + 0];  // [R, D]
-  const float* up = mats.m[3 * br + 1];    // [D, R]
-  const float* bias = mats.m[3 * br + 2];  // [D]
-  for (int d = threadIdx.x; d < D; d += blockDim.x) act[d] = silu_ref(c[d]);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int r = warp; r < R; r += nw) {
-    const float* row = down + (size_t)r * D;
-    float s = 0.0f;
-    for (int d = lane; d < D; d += 32) s = __fmaf_rn(act[d], row[d], s);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) low[r] = s;
+// A batch of AdaLN matrix sets and where each set's parameters go: out[set]
+// holds [3][rows][D] (shift, scale, gate).
+constexpr int kAdaMaxSets = 2 * IRO_DIT_MAX_LAYERS;
+struct AdaBatch {
+  const float* m[kAdaMaxSets][9];
+  float* out[kAdaMaxSets];
+};
+
+// AdaLN parameters (dit.c:543-559, 585-593) for a batch of matrix sets (one
+// set = one block half): out = up(down(silu(c))) + bias + c for each of the
+// three branches c = cond[row, br*D .. +D], the gate branch ending in tanhf.
+// Three launches over all sets at once, one warp per output, so that the 24
+// sets of a 12-layer step take a few microseconds instead of 24 serial
+// low-parallelism launches.
+__global__ void __launch_bounds__(256) adaln_act_kernel(const float* __restrict__ cond, int n,
+                                                        float* __restrict__ act) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    act[i] = silu_ref(cond[i]);
+}
+
+// low[set][row][br][r] = sum_d act[row][br*D + d] * down[r][d]
+__global__ void __launch_bounds__(256) adaln_down_kernel(const AdaBatch bt,
+                                                         const float* __restrict__ act, int D,
+                                                         int R, float* __restrict__ low) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o = blockIdx.x * 8 + warp;  // br * R + r
+  const int set = blockIdx.y, row = blockIdx.z, rows = gridDim.z;
+  if (o >= 3 * R) return;
+  const int br = o / R, r = o - br * R;
+  const float* a = act + ((size_t)row * 3 + br) * D;
+  const float* w = bt.m[set][3 * br] + (size_t)r * D;
+  float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+  int d = lane;
+  for (; d + 96 < D; d += 128) {
+    s0 = __fmaf_rn(a[d], w[d], s0);
+    s1 = __fmaf_rn(a[d + 32], w[d + 32], s1);
+    s2 = __fmaf_rn(a[d + 64], w[d + 64], s2);
+    s3 = __fmaf_rn(a[d + 96], w[d + 96], s3);
   }
-  __syncthreads();
-  float* out = (br == 0 ? shift : br == 1 ? scale : gate) + (size_t)b * D;
-  for (int d = warp; d < D; d += nw) {
-    const float* row = up + (size_t)d * R;
-    float s = 0.0f;
-    for (int r = lane; r < R; r += 32) s = __fmaf_rn(low[r], row[r], s);
+  for (; d < D; d += 32) s0 = __fmaf_rn(a[d], w[d], s0);
+  float sum = (s0 + s1) + (s2 + s3);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) {
-      float v = __fadd_rn(__fadd_rn(s, bias[d]), c[d]);
-      out[d] = br == 2 ? tanhf(v) : v;
-    }
+  for (int k = 16; k > 0; k >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, k);
+  if (lane == 0) low[(((size_t)set * rows + row) * 3 + br) * R + r] = sum;
+}
+
+// out[set][br][row][d] = sum_r low[set][row][br][r] * up[d][r] + bias[d] + c[d]
+__global__ void __launch_bounds__(256) adaln_up_kernel(const AdaBatch bt,
+                                                       const float* __restrict__ cond,
+                                                       const float* __restrict__ low, int D,
+                                                       int R) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o = blockIdx.x * 8 + warp;  // br * D + d
+  const int set = blockIdx.y, row = blockIdx.z, rows = gridDim.z;
+  if (o >= 3 * D) return;
+  const int br = o / D, d = o - br * D;
+  const float* lw = low + (((size_t)set * rows + row) * 3 + br) * R;
+  const float* u = bt.m[set][3 * br + 1] + (size_t)d * R;
+  float sum = 0.0f;
+  for (int r = lane; r < R; r += 32) sum = __fmaf_rn(lw[r], u[r], sum);
+#pragma unroll
+  for (int k = 16; k > 0; k >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, k);
+  if (lane == 0) {
+    const float c = cond[(size_t)row * 3 * D + (size_t)br * D + d];
+    const float v = __fadd_rn(__fadd_rn(sum, bt.m[set][3 * br + 2][d]), c);
+    bt.out[set][((size_t)br * rows + row) * D + d] = br == 2 ? tanhf(v) : v;
   }
 }
 
@@ -291,20 +325,38 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(AttnArgs a) {
   }
 }
 
-// x += gate[b] * branch (dit.c:1013-1020); gate row b / prow.
-__global__ void gated_residual_kernel(float* __restrict__ x, const float* __restrict__ branch,
-                                      const float* __restrict__ gate, long long n, int S, int D,
-                                      int prow) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / D;
-    const int d = (int)(i - row * D);
-    const int b = (int)(row / S) / prow;
-    x[i] = __fadd_rn(x[i], __fmul_rn(gate[(size_t)b * D + d], branch[i]));
+// x += gate[b] * branch (dit.c:1013-1020); gate row b / prow.  One row per
+// block iteration, float4 columns (D % 4 == 0).
+__global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__ x,
+                                                             const float* __restrict__ branch,
+                                                             const float* __restrict__ gate,
+                                                             int rows, int S, int D, int prow) {
+  const int d4n = D / 4;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float4* g = reinterpret_cast<const float4*>(gate + (size_t)(row / S / prow) * D);
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)row * D);
+    const float4* br = reinterpret_cast<const float4*>(branch + (size_t)row * D);
+    for (int i = threadIdx.x; i < d4n; i += blockDim.x) {
+      float4 xv = xr[i];
+      const float4 gv = g[i], bv = br[i];
+      xv.x = __fadd_rn(xv.x, __fmul_rn(gv.x, bv.x));
+      xv.y = __fadd_rn(xv.y, __fmul_rn(gv.y, bv.y));
+      xv.z = __fadd_rn(xv.z, __fmul_rn(gv.z, bv.z));
+      xv.w = __fadd_rn(xv.w, __fmul_rn(gv.w, bv.w));
+      xr[i] = xv;
+    }
   }
 }
 
 size_t al256(size_t b) { return (b + 255) / 256 * 256; }
+
+// IRO_DIT_ATTENTION=simt selects the fp32 CUDA-core attention kernel above
+// (exact fp32 products) instead of the tensor-core one; it also serves
+// requests the tensor-core kernel does not take (unaligned context buffers).
+int attention_mode() {
+  const char* e = getenv("IRO_DIT_ATTENTION");
+  return (e && strcmp(e, "simt") == 0) ? 1 : 0;
+}
 
 }  // namespace
 }  // namespace iro
@@ -337,30 +389,59 @@ int iro_dit_rope_table(float* cos_out, float* sin_out, int S, int head_dim) {
   return IRO_OK;
 }
 
-size_t iro_dit_block_workspace_bytes(const IroDiTBlockDev* blk, int B, int S, int C,
-                                     int context_batch) {
-  if (!blk || B <= 0 || S <= 0 || C <= 0) return 0;
+}  // extern "C"
+
+namespace iro {
+
+size_t dit_adaln_scratch_bytes(int sets, int rows, int D, int R) {
+  return al256(sizeof(float) * (size_t)rows * 3 * D) +
+         al256(sizeof(float) * (size_t)sets * rows * 3 * R);
+}
+
+int dit_adaln_params(const IroDiTBlockDev* const* blks, int n_blocks, const float* cond,
+                     int rows, float* params, void* scratch, cudaStream_t s) {
+  if (n_blocks <= 0 || 2 * n_blocks > kAdaMaxSets) return IRO_ERR_INVALID;
+  const int D = blks[0]->model_dim, R = blks[0]->adaln_rank, sets = 2 * n_blocks;
+  float* act = static_cast<float*>(scratch);
+  float* low = act + al256(sizeof(float) * (size_t)rows * 3 * D) / sizeof(float);
+  AdaBatch bt;
+  for (int i = 0; i < sets; i++) {
+    for (int k = 0; k < 9; k++) bt.m[i][k] = blks[i / 2]->adaln[i % 2][k];
+    bt.out[i] = params + (size_t)i * 3 * rows * D;
+  }
+  const int n = rows * 3 * D;
+  adaln_act_kernel<<<cdiv(n, 256), 256, 0, s>>>(cond, n, act);
+  int st = check_launch();
+  if (st) return st;
+  adaln_down_kernel<<<dim3(cdiv(3 * R, 8), sets, rows), 256, 0, s>>>(bt, act, D, R, low);
+  if ((st = check_launch())) return st;
+  adaln_up_kernel<<<dim3(cdiv(3 * D, 8), sets, rows), 256, 0, s>>>(bt, cond, low, D, R);
+  return check_launch();
+}
+
+size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int context_batch) {
   const size_t M = (size_t)B * S, D = (size_t)blk->model_dim;
   size_t t = 0;
   t += 7 * al256(sizeof(float) * M * D);                           // h, q, k, v, g, mix, branch
   t += al256(M * D) + 2 * al256(sizeof(float) * M);                // codes + row params
-  t += 6 * al256(sizeof(float) * (size_t)B * D);                   // AdaLN params
   t += al256(sizeof(int) * (size_t)B * C) + al256(sizeof(int) * B);
-  t += iro_int8_swiglu_workspace_bytes((int)M, blk->model_dim, blk->mlp_dim,
-                                       (blk->residual_mask & 8) != 0);
-  return t;
+  // The SwiGLU scratch is only live in the MLP half, the V^T copies only in
+  // the attention half: they share the tail of the workspace.
+  return t + std::max(iro_int8_swiglu_workspace_bytes((int)M, blk->model_dim, blk->mlp_dim,
+                                                      (blk->residual_mask & 8) != 0),
+                      attention_tc_workspace_bytes(B, S, C, context_batch, blk->model_dim));
 }
 
-int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, int cond_rows,
-                      const float* ctx_k, const float* ctx_v, const uint8_t* ctx_mask,
-                      int context_batch, int B, int S, int C, const float* rope_cos,
-                      const float* rope_sin, void* workspace, void* stream) {
-  if (!blk || !x || !cond || !ctx_k || !ctx_v || !ctx_mask || !rope_cos || !rope_sin ||
-      B <= 0 || S <= 0 || C <= 0 || context_batch <= 0 || B % context_batch != 0 ||
+int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, const float* ctx_k,
+                    const float* ctx_v, const uint8_t* ctx_mask, int context_batch, int B, int S,
+                    int C, const float* rope_cos, const float* rope_sin) {
+  if (!blk || !x || !ctx_k || !ctx_v || !ctx_mask || !rope_cos || !rope_sin || B <= 0 ||
+      S <= 0 || C <= 0 || context_batch <= 0 || B % context_batch != 0 ||
       (cond_rows != 1 && cond_rows != B))
     return IRO_ERR_INVALID;
   const int D = blk->model_dim, NH = blk->heads, R = blk->adaln_rank, H = blk->mlp_dim;
-  if (blk->head_dim != kHD || NH * kHD != D || R <= 0 || H <= 0 || D % 16 != 0)
+  if (blk->head_dim != kHD || NH * kHD != D || R <= 0 || H <= 0 || D % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) != 0)
     return IRO_ERR_UNSUPPORTED;
   // Residual (two-term) policy: the reference's default, W2 only (dit.c:
   // 429-436), or none; the QKVG, Wo and W1/W3 two-term forms are not built.
@@ -369,17 +450,18 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, in
       blk->w13.layout != IRO_LAYOUT_GATED_PAIR || blk->w13.K != D || blk->w13.hidden != H ||
       blk->w2.N != D || blk->w2.K != H)
     return IRO_ERR_INVALID;
-  int st;
-  Ctx* c = ctx_current(&st);
-  if (!c) return st;
-  cudaStream_t s = pick_stream(c, stream);
+  return IRO_OK;
+}
+
+// The block with its AdaLN parameters precomputed: params = [2 halves][3:
+// shift, scale, gate][cond_rows][D].
+int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* params,
+                  int cond_rows, const float* ctx_k, const float* ctx_v,
+                  const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
+                  const float* rcos, const float* rsin, void* workspace, cudaStream_t s) {
+  const int D = blk->model_dim, NH = blk->heads;
   const size_t M = (size_t)B * S;
-  const size_t need = iro_dit_block_workspace_bytes(blk, B, S, C, context_batch);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  if (!ws) {
-    ws = static_cast<uint8_t*>(arena_get(c, need, &st));
-    if (!ws) return st;
-  }
   size_t off = 0;
   auto take = [&](size_t bytes) {
     uint8_t* p = ws + off;
@@ -396,30 +478,19 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, in
   uint8_t* codes = take(M * D);
   float* rs = reinterpret_cast<float*>(take(sizeof(float) * M));
   int32_t* rz = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
-  float* ada[6];
-  for (int i = 0; i < 6; i++) ada[i] = reinterpret_cast<float*>(take(sizeof(float) * (size_t)B * D));
   int* clist = reinterpret_cast<int*>(take(sizeof(int) * (size_t)B * C));
   int* ccount = reinterpret_cast<int*>(take(sizeof(int) * B));
   void* sw_ws = ws + off;
-  const float* rcos = rope_cos;
-  const float* rsin = rope_sin;
+  int st;
 
-  context_list_kernel<<<cdiv(B, 64), 64, 0, s>>>(ctx_mask, B, C, clist, ccount);
-  if ((st = check_launch())) return st;
-
-  const size_t ada_smem = sizeof(float) * (size_t)(D + R);
   const int prow = B / cond_rows;  // batch rows per AdaLN parameter row
-  const long long n = (long long)M * D;
-  const int res_blocks = (int)std::min<long long>((n + 255) / 256, (long long)c->num_sms * 16);
+  const int res_blocks = (int)std::min<long long>((long long)M, (long long)c->num_sms * 8);
   for (int half = 0; half < 2; half++) {
-    // AdaLN (attention: matrices 0..8, MLP: 9..17) and apply.
-    AdaMats am;
-    for (int i = 0; i < 9; i++) am.m[i] = blk->adaln[half][i];
-    adaln_params_kernel<<<dim3(cond_rows, 3), 256, ada_smem, s>>>(cond, D, R, am, ada[0],
-                                                                  ada[1], ada[2]);
-    if ((st = check_launch())) return st;
+    const float* shift = params + (size_t)(half * 3 + 0) * cond_rows * D;
+    const float* scale = params + (size_t)(half * 3 + 1) * cond_rows * D;
+    const float* gate = params + (size_t)(half * 3 + 2) * cond_rows * D;
     adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
-                                                       ada[0], ada[1], h);
+                                                       shift, scale, h);
     if ((st = check_launch())) return st;
     if (half == 0) {
       // QKVG on one quantised copy of h (dit.c:785-792).
@@ -444,9 +515,17 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, in
       qk_norm_rope_kernel<<<cdiv((int)M * NH, 8), 256, 0, s>>>(
           q, k, (int)M, S, D, NH, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
       if ((st = check_launch())) return st;
-      AttnArgs aa{q, k, v, g, ctx_k, ctx_v, clist, ccount, B / context_batch, S, C, D, mix};
-      attention_kernel<<<dim3(cdiv(S, kAQ), NH, B), kAThreads, 0, s>>>(aa);
-      if ((st = check_launch())) return st;
+      AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
+                       sw_ws};
+      if (attention_mode() == 0 && attention_tc_supported(ar)) {
+        if ((st = attention_tc_launch(c, ar, s))) return st;
+      } else {
+        context_list_kernel<<<cdiv(B, 64), 64, 0, s>>>(ctx_mask, B, C, clist, ccount);
+        if ((st = check_launch())) return st;
+        AttnArgs aa{q, k, v, g, ctx_k, ctx_v, clist, ccount, B / context_batch, S, C, D, mix};
+        attention_kernel<<<dim3(cdiv(S, kAQ), NH, B), kAThreads, 0, s>>>(aa);
+        if ((st = check_launch())) return st;
+      }
       // Wo on the quantised gated mix (dit.c:876-884).
       st = quantize_rows_launch(mix, (int)M, D, codes, rs, rz, 0, s);
       if (st) return st;
@@ -466,10 +545,48 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, in
                                (blk->residual_mask & 8) != 0, sw_ws, s);
       if (st) return st;
     }
-    gated_residual_kernel<<<res_blocks, 256, 0, s>>>(x, branch, ada[2], n, S, D, prow);
+    gated_residual_kernel<<<res_blocks, 256, 0, s>>>(x, branch, gate, (int)M, S, D, prow);
     if ((st = check_launch())) return st;
   }
   return IRO_OK;
+}
+
+}  // namespace iro
+
+extern "C" {
+
+size_t iro_dit_block_workspace_bytes(const IroDiTBlockDev* blk, int B, int S, int C,
+                                     int context_batch) {
+  if (!blk || B <= 0 || S <= 0 || C <= 0) return 0;
+  const size_t D = (size_t)blk->model_dim;
+  return dit_block_body_bytes(blk, B, S, C, context_batch) +
+         al256(sizeof(float) * 6 * (size_t)B * D) +
+         dit_adaln_scratch_bytes(2, B, blk->model_dim, blk->adaln_rank);
+}
+
+int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, int cond_rows,
+                      const float* ctx_k, const float* ctx_v, const uint8_t* ctx_mask,
+                      int context_batch, int B, int S, int C, const float* rope_cos,
+                      const float* rope_sin, void* workspace, void* stream) {
+  int st = dit_block_check(blk, x, cond_rows, ctx_k, ctx_v, ctx_mask, context_batch, B, S, C,
+                           rope_cos, rope_sin);
+  if (st) return st;
+  if (!cond) return IRO_ERR_INVALID;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  cudaStream_t s = pick_stream(c, stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (!ws) {
+    ws = static_cast<uint8_t*>(
+        arena_get(c, iro_dit_block_workspace_bytes(blk, B, S, C, context_batch), &st));
+    if (!ws) return st;
+  }
+  const size_t body = dit_block_body_bytes(blk, B, S, C, context_batch);
+  float* params = reinterpret_cast<float*>(ws + body);
+  void* scratch = ws + body + al256(sizeof(float) * 6 * (size_t)B * blk->model_dim);
+  if ((st = dit_adaln_params(&blk, 1, cond, cond_rows, params, scratch, s))) return st;
+  return dit_block_run(c, blk, x, params, cond_rows, ctx_k, ctx_v, ctx_mask, context_batch, B,
+                       S, C, rope_cos, rope_sin, ws, s);
 }
 
 }  // extern "C"

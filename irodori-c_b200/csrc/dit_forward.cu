@@ -22,35 +22,42 @@
 #include <algorithm>
 #include <vector>
 
+#include "dit_block.cuh"
 #include "runtime.cuh"
 
 namespace iro {
 namespace {
 
 // y[M, N] = x[M, K] . w[N, K]^T (+ bias), optional silu on y (in place of
-// the reference's separate iro_silu_inplace).  64 x 64 output tile per
+// the reference's separate iro_silu_inplace).  BM x BN output tile per
 // 256-thread block, 4 x 4 outputs per thread, k in increasing order.
-constexpr int kLT = 64, kLK = 16;
+constexpr int kLK = 16;
 
+template <int BM, int BN>
 __global__ void __launch_bounds__(256) linear_ref_kernel(const float* __restrict__ x,
                                                          const float* __restrict__ w,
                                                          const float* __restrict__ bias,
                                                          float* __restrict__ y, int M, int N, int K,
                                                          int silu) {
-  __shared__ float xs[kLK][kLT + 1];
-  __shared__ float ws[kLK][kLT + 1];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const int m0 = blockIdx.y * kLT, n0 = blockIdx.x * kLT;
+  static_assert((BM / 4) * (BN / 4) == 256, "4 x 4 outputs per thread, 256 threads");
+  __shared__ float xs[kLK][BM + 1];
+  __shared__ float ws[kLK][BN + 1];
+  const int tx = threadIdx.x % (BN / 4), ty = threadIdx.x / (BN / 4);
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; i++)
 #pragma unroll
     for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
   for (int k0 = 0; k0 < K; k0 += kLK) {
-    for (int i = threadIdx.x; i < kLT * kLK; i += 256) {
+    for (int i = threadIdx.x; i < BM * kLK; i += 256) {
       const int r = i / kLK, kk = i % kLK;
-      const int m = m0 + r, n = n0 + r, k = k0 + kk;
+      const int m = m0 + r, k = k0 + kk;
       xs[kk][r] = (m < M && k < K) ? x[(size_t)m * K + k] : 0.0f;
+    }
+    for (int i = threadIdx.x; i < BN * kLK; i += 256) {
+      const int r = i / kLK, kk = i % kLK;
+      const int n = n0 + r, k = k0 + kk;
       ws[kk][r] = (n < N && k < K) ? w[(size_t)n * K + k] : 0.0f;
     }
     __syncthreads();
@@ -81,7 +88,12 @@ __global__ void __launch_bounds__(256) linear_ref_kernel(const float* __restrict
 
 int linear_ref(const float* x, const float* w, const float* bias, float* y, int M, int N, int K,
                int silu, cudaStream_t s) {
-  linear_ref_kernel<<<dim3(cdiv(N, kLT), cdiv(M, kLT)), 256, 0, s>>>(x, w, bias, y, M, N, K, silu);
+  if (N <= 32)
+    linear_ref_kernel<128, 32><<<dim3(cdiv(N, 32), cdiv(M, 128)), 256, 0, s>>>(x, w, bias, y, M,
+                                                                              N, K, silu);
+  else
+    linear_ref_kernel<64, 64><<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, s>>>(x, w, bias, y, M, N,
+                                                                            K, silu);
   return check_launch();
 }
 
@@ -117,17 +129,41 @@ __global__ void expand_rows_kernel(const float* __restrict__ p, float* __restric
 }
 
 // dit.c:1078 / ops.c:738-747: y = x * inv * w, inv = 1 / sqrt(mean(x^2) + eps),
-// the mean of squares summed in the reference's order (one thread per row).
-__global__ void rmsnorm_ref_kernel(const float* x, const float* __restrict__ w, float* y, int M,
-                                   int D, float eps) {
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
-  if (m >= M) return;
-  const float* xm = x + (size_t)m * D;
+// the mean of squares summed in the reference's order by one thread per row.
+// 32 rows per block; each 128-column slice of those rows is staged through
+// shared memory with coalesced loads, then every thread walks its own row.
+constexpr int kNR = 32, kNC = 128;
+
+__global__ void __launch_bounds__(256) rmsnorm_ref_kernel(const float* x,
+                                                          const float* __restrict__ w, float* y,
+                                                          int M, int D, float eps) {
+  __shared__ float tile[kNR][kNC + 1];
+  __shared__ float inv_s[kNR];
+  const int r0 = blockIdx.x * kNR;
+  const int t = threadIdx.x;
   float ms = 0.0f;
-  for (int d = 0; d < D; d++) ms = __fadd_rn(ms, __fmul_rn(xm[d], xm[d]));
-  const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, (float)D), eps)));
-  float* ym = y + (size_t)m * D;
-  for (int d = 0; d < D; d++) ym[d] = __fmul_rn(__fmul_rn(xm[d], inv), w[d]);
+  for (int c0 = 0; c0 < D; c0 += kNC) {
+    const int nc = min(kNC, D - c0);
+    __syncthreads();
+    for (int i = t; i < kNR * kNC; i += 256) {
+      const int rr = i / kNC, cc = i % kNC;
+      const int m = r0 + rr;
+      tile[rr][cc] = (m < M && cc < nc) ? x[(size_t)m * D + c0 + cc] : 0.0f;
+    }
+    __syncthreads();
+    if (t < kNR)
+      for (int cc = 0; cc < nc; cc++) ms = __fadd_rn(ms, __fmul_rn(tile[t][cc], tile[t][cc]));
+  }
+  if (t < kNR) inv_s[t] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, (float)D), eps)));
+  __syncthreads();
+  for (int i = t; i < kNR * D; i += 256) {
+    const int rr = i / D, d = i % D;
+    const int m = r0 + rr;
+    if (m < M) {
+      const size_t o = (size_t)m * D + d;
+      y[o] = __fmul_rn(__fmul_rn(x[o], inv_s[rr]), w[d]);
+    }
+  }
 }
 
 // sampler.c:283-297: guided = v_cond + sum_i scale_i (v_cond - v_uncond_i),
@@ -240,6 +276,8 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
   float* proj = reinterpret_cast<float*>(take(sizeof(float) * (size_t)R * S * D));
   float* x = reinterpret_cast<float*>(take(sizeof(float) * (size_t)Bfull * S * D));
   float* vel = reinterpret_cast<float*>(take(sizeof(float) * (size_t)Bfull * S * L));
+  float* params = reinterpret_cast<float*>(take(sizeof(float) * 6 * (size_t)m->layers * D));
+  void* ada_scratch = take(dit_adaln_scratch_bytes(2 * m->layers, 1, D, m->block[0].adaln_rank));
   void* blk_ws = ws + off;
   int st;
   // Conditioner, once: every row shares the timestep.
@@ -253,14 +291,18 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
   const int eb = (int)std::min<long long>(((long long)B * S * D + 255) / 256, c->num_sms * 16LL);
   expand_rows_kernel<<<eb, 256, 0, s>>>(proj, x, R, cfg, S, D);
   if ((st = check_launch())) return st;
+  // Every layer's AdaLN parameters in one batch: the step's rows share cond.
+  const IroDiTBlockDev* blks[IRO_DIT_MAX_LAYERS];
+  for (int l = 0; l < m->layers; l++) blks[l] = &m->block[l];
+  if ((st = dit_adaln_params(blks, m->layers, cond, 1, params, ada_scratch, s))) return st;
   for (int l = 0; l < m->layers; l++) {
-    st = iro_dit_block_dev(&m->block[l], x, cond, 1, ctx_k[l], ctx_v[l], mask, R, B, S, C,
-                           tb.rcos, tb.rsin, blk_ws, s);
+    st = dit_block_run(c, &m->block[l], x, params + (size_t)l * 6 * D, 1, ctx_k[l], ctx_v[l],
+                       mask, R, B, S, C, tb.rcos, tb.rsin, blk_ws, s);
     if (st) return st;
   }
   // Output head (normalised in place: x is rebuilt from the state next
   // step) into the velocity, then the guided Euler update.
-  rmsnorm_ref_kernel<<<cdiv(B * S, 128), 128, 0, s>>>(x, m->out_norm, x, B * S, D, m->norm_eps);
+  rmsnorm_ref_kernel<<<cdiv(B * S, kNR), 256, 0, s>>>(x, m->out_norm, x, B * S, D, m->norm_eps);
   if ((st = check_launch())) return st;
   if ((st = linear_ref(x, m->out_w, m->out_b, vel, B * S, L, D, 0, s))) return st;
   const float dt = t_next - t;
@@ -283,6 +325,22 @@ bool valid_run(const IroDiTModelDev* m, const float* state, int R, int cfg, int 
   return true;
 }
 
+// Block-level checks at the step's shapes (one row of conditioning).
+int check_blocks(const IroDiTModelDev* m, const float* state, int R, int cfg, int S,
+                 const float* const* ctx_k, const float* const* ctx_v, const uint8_t* mask,
+                 int C) {
+  // The step's own buffers (x, RoPE tables) live in the workspace, 256-byte
+  // aligned; an aligned stand-in passes the pointer checks.
+  alignas(16) static const float stand_in[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  (void)state;
+  for (int l = 0; l < m->layers; l++) {
+    int st = dit_block_check(&m->block[l], stand_in, 1, ctx_k[l], ctx_v[l], mask, R, R * cfg, S,
+                             C, stand_in, stand_in);
+    if (st) return st;
+  }
+  return IRO_OK;
+}
+
 }  // namespace
 }  // namespace iro
 
@@ -299,7 +357,9 @@ size_t iro_dit_step_workspace_bytes(const IroDiTModelDev* m, int R, int cfg, int
   t += al256(sizeof(float) * (size_t)R * S * D);                       // projected
   t += al256(sizeof(float) * (size_t)B * S * D);                       // x
   t += al256(sizeof(float) * (size_t)B * S * m->latent_dim);           // velocity
-  return t + iro_dit_block_workspace_bytes(&m->block[0], B, S, C, R);
+  t += al256(sizeof(float) * 6 * (size_t)m->layers * D);               // AdaLN params
+  t += dit_adaln_scratch_bytes(2 * m->layers, 1, D, m->block[0].adaln_rank);
+  return t + dit_block_body_bytes(&m->block[0], B, S, C, R);
 }
 
 int iro_dit_euler_step_dev(const IroDiTModelDev* m, float* state, int R, int cfg, int S,
@@ -307,7 +367,8 @@ int iro_dit_euler_step_dev(const IroDiTModelDev* m, float* state, int R, int cfg
                            const float* const* ctx_v, const uint8_t* mask, int C,
                            void* workspace, void* stream) {
   if (!valid_run(m, state, R, cfg, S, cfg_scales, ctx_k, ctx_v, mask, C)) return IRO_ERR_INVALID;
-  int st;
+  int st = check_blocks(m, state, R, cfg, S, ctx_k, ctx_v, mask, C);
+  if (st) return st;
   Ctx* c = ctx_current(&st);
   if (!c) return st;
   cudaStream_t s = pick_stream(c, stream);
@@ -330,7 +391,8 @@ int iro_dit_sample_euler_dev(const IroDiTModelDev* m, float* state, int R, int c
                              void* workspace, void* stream) {
   if (!valid_run(m, state, R, cfg, S, cfg_scales, ctx_k, ctx_v, mask, C) || steps <= 0)
     return IRO_ERR_INVALID;
-  int st;
+  int st = check_blocks(m, state, R, cfg, S, ctx_k, ctx_v, mask, C);
+  if (st) return st;
   Ctx* c = ctx_current(&st);
   if (!c) return st;
   cudaStream_t s = pick_stream(c, stream);
@@ -424,7 +486,7 @@ int iro_dit_output_dev(const IroDiTModelDev* m, const float* x, int B, int S, fl
     norm = static_cast<float*>(arena_get(c, sizeof(float) * (size_t)rows * D, &st));
     if (!norm) return st;
   }
-  rmsnorm_ref_kernel<<<cdiv(rows, 128), 128, 0, s>>>(x, m->out_norm, norm, rows, D, m->norm_eps);
+  rmsnorm_ref_kernel<<<cdiv(rows, kNR), 256, 0, s>>>(x, m->out_norm, norm, rows, D, m->norm_eps);
   if ((st = check_launch())) return st;
   return linear_ref(norm, m->out_w, m->out_b, velocity, rows, m->latent_dim, D, 0, s);
 }
