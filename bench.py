@@ -524,6 +524,37 @@ def run_profile_case(args):
         print(f"profile case conv7: {args.warmup + args.steps} launches ok")
         return
 
+    if args.profile in ("dit_qkvg", "dit_w2"):
+        # The config-3 DiT's GEMMs at full size, M = 24000 rows: the fused
+        # QKVG projection (N = 4 x 1024, K = 1024, four fp32 outputs) or the
+        # two-term W2 (N = 1024, K = 2816) with the gated residual epilogue.
+        Mq, Dm, Hm = 24000, 1024, 2816
+        iro.init(0)
+        rng = np.random.default_rng(10)
+        f = lambda *sh, sc=1.0: rng.standard_normal(sh, dtype=np.float32) * np.float32(sc)
+        if args.profile == "dit_qkvg":
+            dw = iro.DevWeight.concat([iro.HostWeight(f(Dm, Dm, sc=0.03)) for _ in range(4)])
+            xq = iro.DevBuf.from_host(f(Mq, Dm))
+            q, s_, z = (iro.DevBuf((Mq, Dm), np.uint8), iro.DevBuf(Mq, np.float32),
+                        iro.DevBuf(Mq, np.int32))
+            iro.quantize_rows_dev(xq, Mq, Dm, q, s_, z)
+            outs = [iro.DevBuf((Mq, Dm), np.float32) for _ in range(4)]
+            for _ in range(args.warmup + args.steps):
+                iro.linear_split_dev(q, s_, z, dw, outs, Dm, Mq)
+        else:
+            w2 = iro.DevWeight.upload(iro.HostWeight(f(Dm, Hm, sc=0.02)))
+            hq = iro.DevBuf.from_host(f(Mq, Hm))
+            args_ = [iro.DevBuf((Mq, Hm), np.uint8), iro.DevBuf(Mq, np.float32),
+                     iro.DevBuf(Mq, np.int32), iro.DevBuf((Mq, Hm), np.uint8),
+                     iro.DevBuf(Mq, np.float32), iro.DevBuf(Mq, np.int32)]
+            iro.quantize_rows_residual_dev(hq, Mq, Hm, *args_[:3], None, *args_[3:])
+            y = iro.DevBuf((Mq, Dm), np.float32)
+            for _ in range(args.warmup + args.steps):
+                iro.linear2_dev(*args_, w2, None, y, Mq)
+        iro.synchronize()
+        print(f"profile case {args.profile}: {args.warmup + args.steps} launches ok")
+        return
+
     if args.profile == "ditblock":
         # One config-3 DiT block (d1024, 16 heads, mlp 2816) over 4 CFG rows of
         # one request x 750 frames (3000 rows), 128 context tokens: 12 MB per
@@ -757,7 +788,8 @@ def run_dit(args):
     mask = (rng.random((R * CFG, Cx)) < 0.9).astype(np.uint8)
     mask[:, 0] = 1
     maskd = iro.DevBuf.from_host(mask)
-    ws = iro.DevBuf(model.workspace_bytes(R, CFG, S, Cx), np.uint8)
+    ws = iro.DevBuf(model.workspace_bytes(R, CFG, S, Cx, steps=max(args.steps, args.warmup, 2)),
+                    np.uint8)
     state0 = f(R, S, 32)
     host_in = torch.from_numpy(state0).pin_memory()
     host_out = torch.empty_like(host_in).pin_memory()
@@ -832,7 +864,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--workload", choices=["swiglu", "conv7", "init", "dit"], default="swiglu",
                     help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
-    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7", "ditblock"],
+    ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7", "ditblock",
+                                          "dit_qkvg", "dit_w2"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
     ap.add_argument("--dit-dims", choices=["cfg3", "reference"], default="cfg3",
                     help="dit workload: config 3's d1024/16 heads/2816, or the reference "

@@ -415,8 +415,11 @@ int iro_dit_output_dev(const IroDiTModelDev *m, const float *x, int B, int S, fl
    init_scale down to 0: step i runs at t = (1 - i/steps) * init_scale, with
    all cfg rows while cfg_min_t <= t <= cfg_max_t and the conditional row
    alone outside that window.  Arguments as iro_dit_euler_step_dev; the
-   workspace is iro_dit_step_workspace_bytes(m, R, cfg, S, C).  The RoPE
-   tables are built once per call. */
+   workspace is iro_dit_sample_workspace_bytes(m, R, cfg, S, C, steps).  The
+   RoPE tables, and every step's conditioning and AdaLN parameters, are
+   computed once per call. */
+size_t iro_dit_sample_workspace_bytes(const IroDiTModelDev *m, int R, int cfg, int S, int C,
+                                      int steps);
 int iro_dit_sample_euler_dev(const IroDiTModelDev *m, float *state, int R, int cfg, int S,
                              int steps, float init_scale, float cfg_min_t, float cfg_max_t,
                              const float *cfg_scales, const float *const *ctx_k,

@@ -722,7 +722,25 @@ size_t iro_int8_swiglu_workspace_bytes(int M, int D, int H, int residual_w2) {
 int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
                         const IroInt8DevWeight* w2, const float* b2, float* out,
                         int residual_w2, void* workspace, void* stream) {
-  if (!x || !out || !w13 || !w2 || w13->layout != IRO_LAYOUT_GATED_PAIR ||
+  if (!x || !out || !w13 || !w2 || M < 0) return IRO_ERR_INVALID;
+  if (M == 0) return IRO_OK;
+  int st;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  return swiglu_run(c, x, M, w13, w2, b2, out, residual_w2, workspace, pick_stream(c, stream),
+                    nullptr, 0);
+}
+
+}  // extern "C"
+
+namespace iro {
+
+int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
+               const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2,
+               void* workspace, cudaStream_t s, const float* rgate, int rgate_rows,
+               const uint8_t* qx_in, const float* sx_in, const int32_t* zx_in) {
+  if ((!x && !(qx_in && sx_in && zx_in)) || !out || !w13 || !w2 ||
+      w13->layout != IRO_LAYOUT_GATED_PAIR ||
       w2->layout != IRO_LAYOUT_PLAIN || w2->K != w13->hidden || M < 0)
     return IRO_ERR_INVALID;
   const int D = w13->K, H = w13->hidden;
@@ -730,9 +748,6 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
   if (D % 16 != 0 || H % 16 != 0) return IRO_ERR_UNSUPPORTED;
   if (M == 0) return IRO_OK;
   int st;
-  Ctx* c = ctx_current(&st);
-  if (!c) return st;
-  cudaStream_t s = pick_stream(c, stream);
   const size_t need = iro_int8_swiglu_workspace_bytes(M, D, H, residual_w2);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (!ws) {
@@ -761,7 +776,7 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
     sh2 = reinterpret_cast<float*>(take(sizeof(float) * M));
     zh2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
   }
-  if (swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
+  if (!rgate && !qx_in && swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
     SwigluBuffers b;
     b.qx = qx;
     b.sx = sx;
@@ -775,8 +790,14 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
     b.ctr = reinterpret_cast<int*>(ws + off);
     return swiglu_fused_launch(c, x, M, w13, w2, b2 ? b2 : w2->bias, out, b, s);
   }
-  st = quantize_rows_launch(x, M, D, qx, sx, zx, 0, s);
-  if (st) return st;
+  if (qx_in) {
+    qx = const_cast<uint8_t*>(qx_in);
+    sx = const_cast<float*>(sx_in);
+    zx = const_cast<int32_t*>(zx_in);
+  } else {
+    st = quantize_rows_launch(x, M, D, qx, sx, zx, 0, s);
+    if (st) return st;
+  }
   GemmRequest g;
   g.epi = EPI_GATED;
   g.M = M;
@@ -804,6 +825,8 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
   r.bias = b2 ? b2 : w2->bias;
   r.y = out;
   r.ldy = D;
+  r.rgate = rgate;
+  r.rgate_rows = rgate_rows;
   if (residual_w2) {
     r.epi = EPI_DUAL;
     r.a2 = qh2;
@@ -814,6 +837,10 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
   }
   return gemm_launch(c, r, s);
 }
+
+}  // namespace iro
+
+extern "C" {
 
 // True when `p` is page-locked host memory (async copies can overlap).
 static bool is_pinned(const void* p) {

@@ -422,6 +422,12 @@ int vt_ld(int n) { return (n + 3) / 4 * 4; }  // 16-byte row pitch
 
 }  // namespace
 
+int attention_tc_vt_ld(int n) { return vt_ld(n); }
+
+namespace {
+
+}  // namespace
+
 size_t attention_tc_workspace_bytes(int B, int S, int C, int context_batch, int D) {
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
   return al(sizeof(float) * (size_t)B * D * vt_ld(S)) +
@@ -452,10 +458,14 @@ int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
   const int lds = vt_ld(r.S), ldc = vt_ld(r.C);
   float* vt = static_cast<float*>(r.workspace);
   float* cvt = vt + ((sizeof(float) * (size_t)r.B * r.D * lds + 255) / 256 * 256) / sizeof(float);
-  v_transpose_kernel<<<dim3(cdiv(lds, 32), r.heads, r.B), 256, 0, s>>>(r.v, vt, r.S, r.D,
-                                                                        r.heads, lds);
-  int st = check_launch();
-  if (st) return st;
+  int st;
+  if (r.vt_self == nullptr) {
+    v_transpose_kernel<<<dim3(cdiv(lds, 32), r.heads, r.B), 256, 0, s>>>(r.v, vt, r.S, r.D,
+                                                                          r.heads, lds);
+    if ((st = check_launch())) return st;
+  } else if (r.vt_self != vt) {
+    return IRO_ERR_INVALID;
+  }
   v_transpose_kernel<<<dim3(cdiv(ldc, 32), r.heads, r.context_batch), 256, 0, s>>>(
       r.cv, cvt, r.C, r.D, r.heads, ldc);
   if ((st = check_launch())) return st;

@@ -20,7 +20,14 @@ struct AttnTcRequest {
   float* mix;
   int B, S, C, context_batch, D, heads;
   void* workspace;  // attention_tc_workspace_bytes(B, S, C, context_batch, D), 16-byte aligned
+  // Optional: the self V^T rows already in the workspace's first region
+  // (vt[((b * heads + h) * 64 + d) * attention_tc_vt_ld(S) + s], zero past S),
+  // so the launch only transposes the context V.
+  const float* vt_self;
 };
+
+// Row pitch (floats) of the V^T rows for n tokens.
+int attention_tc_vt_ld(int n);
 
 // Scratch for the per-head V^T copies of the self and context values.
 size_t attention_tc_workspace_bytes(int B, int S, int C, int context_batch, int D);

@@ -10,7 +10,7 @@
 //                  (dit_attention.cu; tf32 tensor cores), or attention_kernel
 //                  (fp32 CUDA cores)
 //   Wo             (dit.c:876-884)           int8 GEMM
-//   gated residual (dit.c:1013-1020)         gated_residual_kernel
+//   gated residual (dit.c:1013-1020)         in the Wo and W2 GEMM epilogues
 //   SwiGLU         (dit.c:913-969)           iro_int8_swiglu_dev
 //
 // The fp32 parts follow the reference's formulas and per-element operation
@@ -137,6 +137,100 @@ __global__ void __launch_bounds__(256) adaln_apply_kernel(const float* __restric
     hr[d] = __fadd_rn(__fmul_rn(__fmul_rn(xr[d], inv), __fadd_rn(1.0f, sc[d])), sh[d]);
 }
 
+// AdaLN apply fused with the row quantiser that follows it (dit.c:597-609
+// then ops.c:321-348): h = x * inv * (1 + scale) + shift is formed in
+// registers and written only as u8 codes with the row's scale and zero
+// point, so h never goes to HBM.  One warp per row, lane l holding float4
+// elements l, l + 32, ...; the range and codes use the quantiser's own
+// arithmetic (row_params, quant_code).
+template <int V>
+__global__ void __launch_bounds__(256) adaln_quant_kernel(const float* __restrict__ x, int rows,
+                                                          int S, int D, float eps, int prow,
+                                                          const float* __restrict__ shift,
+                                                          const float* __restrict__ scale,
+                                                          uint8_t* __restrict__ q,
+                                                          float* __restrict__ qs,
+                                                          int32_t* __restrict__ qz) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int D4 = D >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * D);
+  float4 v[V];
+  float ms = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; i++) {
+    const int j = i * 32 + lane;
+    v[i] = j < D4 ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ms = __fmaf_rn(v[i].x, v[i].x, ms);
+    ms = __fmaf_rn(v[i].y, v[i].y, ms);
+    ms = __fmaf_rn(v[i].z, v[i].z, ms);
+    ms = __fmaf_rn(v[i].w, v[i].w, ms);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ms += __shfl_xor_sync(0xffffffffu, ms, o);
+  const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, (float)D), eps)));
+  const int b = row / S / prow;
+  const float4* sh = reinterpret_cast<const float4*>(shift + (size_t)b * D);
+  const float4* sc = reinterpret_cast<const float4*>(scale + (size_t)b * D);
+  float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+  for (int i = 0; i < V; i++) {
+    const int j = i * 32 + lane;
+    if (j < D4) {
+      const float4 s4 = sc[j], h4 = sh[j];
+      v[i].x = __fadd_rn(__fmul_rn(__fmul_rn(v[i].x, inv), __fadd_rn(1.0f, s4.x)), h4.x);
+      v[i].y = __fadd_rn(__fmul_rn(__fmul_rn(v[i].y, inv), __fadd_rn(1.0f, s4.y)), h4.y);
+      v[i].z = __fadd_rn(__fmul_rn(__fmul_rn(v[i].z, inv), __fadd_rn(1.0f, s4.z)), h4.z);
+      v[i].w = __fadd_rn(__fmul_rn(__fmul_rn(v[i].w, inv), __fadd_rn(1.0f, s4.w)), h4.w);
+      lo = run_lo(v[i].x, lo); hi = run_hi(v[i].x, hi);
+      lo = run_lo(v[i].y, lo); hi = run_hi(v[i].y, hi);
+      lo = run_lo(v[i].z, lo); hi = run_hi(v[i].z, hi);
+      lo = run_lo(v[i].w, lo); hi = run_hi(v[i].w, hi);
+    }
+  }
+  warp_minmax(lo, hi);
+  float s, qinv;
+  int zp;
+  row_params(lo, hi, s, qinv, zp);
+  const float zpf = (float)zp;
+  uint32_t* dst = reinterpret_cast<uint32_t*>(q + (size_t)row * D);
+#pragma unroll
+  for (int i = 0; i < V; i++) {
+    const int j = i * 32 + lane;
+    if (j < D4)
+      dst[j] = quant_code(v[i].x, qinv, zpf) | (quant_code(v[i].y, qinv, zpf) << 8) |
+               (quant_code(v[i].z, qinv, zpf) << 16) | (quant_code(v[i].w, qinv, zpf) << 24);
+  }
+  if (lane == 0) {
+    qs[row] = s;
+    qz[row] = zp;
+  }
+}
+
+int adaln_quant_launch(const float* x, int rows, int S, int D, float eps, int prow,
+                       const float* shift, const float* scale, uint8_t* q, float* qs, int32_t* qz,
+                       cudaStream_t s) {
+  const int V = cdiv(D / 4, 32);
+  const dim3 grid(cdiv(rows, 8)), block(256);
+#define IRO_AQ(N)                                                                              \
+  case N:                                                                                      \
+    adaln_quant_kernel<N><<<grid, block, 0, s>>>(x, rows, S, D, eps, prow, shift, scale, q,   \
+                                                 qs, qz);                                      \
+    break;
+  switch (V) {
+    IRO_AQ(4)
+    IRO_AQ(8)
+    IRO_AQ(10)
+    IRO_AQ(12)
+    IRO_AQ(16)
+    default:
+      return IRO_ERR_UNSUPPORTED;
+  }
+#undef IRO_AQ
+  return check_launch();
+}
+
 // Per (row, head): RMSNorm of q and k with their weights, then RoPE on the
 // first half of the heads (dit.c:638-706).  Lane p holds dims 2p, 2p+1.
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
@@ -180,6 +274,69 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   *reinterpret_cast<float2*>(kr + d) =
       make_float2(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, sn)),
                   __fadd_rn(__fmul_rn(k0, sn), __fmul_rn(k1, c)));
+}
+
+// qk_norm_rope_kernel's work for a tile of 32 tokens of one batch row and one
+// head, plus that tile of V transposed into the attention kernel's per-head
+// V^T rows (vt[((b * heads + h) * 64 + d) * ld + s], zero for s in [S, ld)).
+// 8 warps x 4 tokens for q and k; V through a shared-memory transpose.
+__global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
+    float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v,
+    float* __restrict__ vt, int S, int D, int heads, int ld, float eps,
+    const float* __restrict__ qw, const float* __restrict__ kw, const float* __restrict__ rcos,
+    const float* __restrict__ rsin) {
+  __shared__ float tile[kHD][33];
+  const int s0 = blockIdx.x * 32, hd = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
+  const int d = 2 * lane;
+  const float* qwh = qw + hd * kHD;
+  const float* kwh = kw + hd * kHD;
+  const float qw0 = qwh[d], qw1 = qwh[d + 1], kw0 = kwh[d], kw1 = kwh[d + 1];
+  for (int i = 0; i < 4; i++) {
+    const int s = s0 + warp * 4 + i;
+    if (s >= S) break;  // warp-uniform
+    const size_t row = (size_t)b * S + s;
+    float* qr = q + row * D + hd * kHD;
+    float* kr = k + row * D + hd * kHD;
+    float2 qv = *reinterpret_cast<float2*>(qr + d);
+    float2 kv = *reinterpret_cast<float2*>(kr + d);
+    float qms = __fmaf_rn(qv.y, qv.y, __fmul_rn(qv.x, qv.x));
+    float kms = __fmaf_rn(kv.y, kv.y, __fmul_rn(kv.x, kv.x));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      qms += __shfl_xor_sync(0xffffffffu, qms, o);
+      kms += __shfl_xor_sync(0xffffffffu, kms, o);
+    }
+    const float qinv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(qms, (float)kHD), eps)));
+    const float kinv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(kms, (float)kHD), eps)));
+    const float q0 = __fmul_rn(qv.x, __fmul_rn(qinv, qw0));
+    const float q1 = __fmul_rn(qv.y, __fmul_rn(qinv, qw1));
+    const float k0 = __fmul_rn(kv.x, __fmul_rn(kinv, kw0));
+    const float k1 = __fmul_rn(kv.y, __fmul_rn(kinv, kw1));
+    if (hd >= heads / 2) {
+      *reinterpret_cast<float2*>(qr + d) = make_float2(q0, q1);
+      *reinterpret_cast<float2*>(kr + d) = make_float2(k0, k1);
+    } else {
+      const float c = rcos[(size_t)s * (kHD / 2) + lane], sn = rsin[(size_t)s * (kHD / 2) + lane];
+      *reinterpret_cast<float2*>(qr + d) =
+          make_float2(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, sn)),
+                      __fadd_rn(__fmul_rn(q0, sn), __fmul_rn(q1, c)));
+      *reinterpret_cast<float2*>(kr + d) =
+          make_float2(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, sn)),
+                      __fadd_rn(__fmul_rn(k0, sn), __fmul_rn(k1, c)));
+    }
+  }
+  for (int i = t; i < 32 * kHD; i += 256) {
+    const int ss = i / kHD, dd = i % kHD;
+    const int s = s0 + ss;
+    tile[dd][ss] = s < S ? v[((size_t)b * S + s) * D + (size_t)hd * kHD + dd] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = t; i < 32 * kHD; i += 256) {
+    const int dd = i / 32, ss = i % 32;
+    const int s = s0 + ss;
+    if (s < ld) vt[(((size_t)b * heads + hd) * kHD + dd) * ld + s] = tile[dd][ss];
+  }
 }
 
 // Valid context positions per batch row (dit.c:811-813, 828-839); the mask
@@ -325,29 +482,6 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(AttnArgs a) {
   }
 }
 
-// x += gate[b] * branch (dit.c:1013-1020); gate row b / prow.  One row per
-// block iteration, float4 columns (D % 4 == 0).
-__global__ void __launch_bounds__(256) gated_residual_kernel(float* __restrict__ x,
-                                                             const float* __restrict__ branch,
-                                                             const float* __restrict__ gate,
-                                                             int rows, int S, int D, int prow) {
-  const int d4n = D / 4;
-  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
-    const float4* g = reinterpret_cast<const float4*>(gate + (size_t)(row / S / prow) * D);
-    float4* xr = reinterpret_cast<float4*>(x + (size_t)row * D);
-    const float4* br = reinterpret_cast<const float4*>(branch + (size_t)row * D);
-    for (int i = threadIdx.x; i < d4n; i += blockDim.x) {
-      float4 xv = xr[i];
-      const float4 gv = g[i], bv = br[i];
-      xv.x = __fadd_rn(xv.x, __fmul_rn(gv.x, bv.x));
-      xv.y = __fadd_rn(xv.y, __fmul_rn(gv.y, bv.y));
-      xv.z = __fadd_rn(xv.z, __fmul_rn(gv.z, bv.z));
-      xv.w = __fadd_rn(xv.w, __fmul_rn(gv.w, bv.w));
-      xr[i] = xv;
-    }
-  }
-}
-
 size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
 // IRO_DIT_ATTENTION=simt selects the fp32 CUDA-core attention kernel above
@@ -422,7 +556,7 @@ int dit_adaln_params(const IroDiTBlockDev* const* blks, int n_blocks, const floa
 size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int context_batch) {
   const size_t M = (size_t)B * S, D = (size_t)blk->model_dim;
   size_t t = 0;
-  t += 7 * al256(sizeof(float) * M * D);                           // h, q, k, v, g, mix, branch
+  t += 6 * al256(sizeof(float) * M * D);                           // h, q, k, v, g, mix
   t += al256(M * D) + 2 * al256(sizeof(float) * M);                // codes + row params
   t += al256(sizeof(int) * (size_t)B * C) + al256(sizeof(int) * B);
   // The SwiGLU scratch is only live in the MLP half, the V^T copies only in
@@ -453,9 +587,9 @@ int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, co
   return IRO_OK;
 }
 
-// The block with its AdaLN parameters precomputed: params = [2 halves][3:
-// shift, scale, gate][cond_rows][D].
-int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* params,
+// The block with its AdaLN parameters precomputed: ada = shift, scale, gate
+// of the attention half, then of the MLP half, each [cond_rows][D].
+int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* const* ada,
                   int cond_rows, const float* ctx_k, const float* ctx_v,
                   const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
                   const float* rcos, const float* rsin, void* workspace, cudaStream_t s) {
@@ -474,7 +608,6 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* para
   float* v = reinterpret_cast<float*>(take(sizeof(float) * M * D));
   float* g = reinterpret_cast<float*>(take(sizeof(float) * M * D));
   float* mix = reinterpret_cast<float*>(take(sizeof(float) * M * D));
-  float* branch = reinterpret_cast<float*>(take(sizeof(float) * M * D));
   uint8_t* codes = take(M * D);
   float* rs = reinterpret_cast<float*>(take(sizeof(float) * M));
   int32_t* rz = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
@@ -484,18 +617,25 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* para
   int st;
 
   const int prow = B / cond_rows;  // batch rows per AdaLN parameter row
-  const int res_blocks = (int)std::min<long long>((long long)M, (long long)c->num_sms * 8);
   for (int half = 0; half < 2; half++) {
-    const float* shift = params + (size_t)(half * 3 + 0) * cond_rows * D;
-    const float* scale = params + (size_t)(half * 3 + 1) * cond_rows * D;
-    const float* gate = params + (size_t)(half * 3 + 2) * cond_rows * D;
-    adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
-                                                       shift, scale, h);
-    if ((st = check_launch())) return st;
+    const float* shift = ada[half * 3 + 0];
+    const float* scale = ada[half * 3 + 1];
+    const float* gate = ada[half * 3 + 2];
+    // AdaLN apply and the row quantiser of its consumer (QKVG, or W1/W3 of
+    // the SwiGLU) in one pass; h is only materialised for shapes the fused
+    // kernel does not take.
+    st = adaln_quant_launch(x, (int)M, S, D, blk->norm_eps, prow, shift, scale, codes, rs, rz, s);
+    const bool fused = st == IRO_OK;
+    if (st == IRO_ERR_UNSUPPORTED) {
+      adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
+                                                         shift, scale, h);
+      if ((st = check_launch())) return st;
+      if ((st = quantize_rows_launch(h, (int)M, D, codes, rs, rz, 0, s))) return st;
+    } else if (st) {
+      return st;
+    }
     if (half == 0) {
       // QKVG on one quantised copy of h (dit.c:785-792).
-      st = quantize_rows_launch(h, (int)M, D, codes, rs, rz, 0, s);
-      if (st) return st;
       GemmRequest r;
       r.epi = EPI_SPLIT;
       r.M = (int)M;
@@ -512,21 +652,29 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* para
       r.outs[2] = v;
       r.outs[3] = g;
       if ((st = gemm_launch(c, r, s))) return st;
-      qk_norm_rope_kernel<<<cdiv((int)M * NH, 8), 256, 0, s>>>(
-          q, k, (int)M, S, D, NH, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
-      if ((st = check_launch())) return st;
       AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
-                       sw_ws};
+                       sw_ws, nullptr};
       if (attention_mode() == 0 && attention_tc_supported(ar)) {
+        // Head norm + RoPE with the self V^T rows the attention kernel reads.
+        float* vt = static_cast<float*>(sw_ws);
+        const int ld = attention_tc_vt_ld(S);
+        qk_norm_rope_vt_kernel<<<dim3(cdiv(S, 32), NH, B), 256, 0, s>>>(
+            q, k, v, vt, S, D, NH, ld, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
+        if ((st = check_launch())) return st;
+        ar.vt_self = vt;
         if ((st = attention_tc_launch(c, ar, s))) return st;
       } else {
+        qk_norm_rope_kernel<<<cdiv((int)M * NH, 8), 256, 0, s>>>(
+            q, k, (int)M, S, D, NH, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
+        if ((st = check_launch())) return st;
         context_list_kernel<<<cdiv(B, 64), 64, 0, s>>>(ctx_mask, B, C, clist, ccount);
         if ((st = check_launch())) return st;
         AttnArgs aa{q, k, v, g, ctx_k, ctx_v, clist, ccount, B / context_batch, S, C, D, mix};
         attention_kernel<<<dim3(cdiv(S, kAQ), NH, B), kAThreads, 0, s>>>(aa);
         if ((st = check_launch())) return st;
       }
-      // Wo on the quantised gated mix (dit.c:876-884).
+      // Wo on the quantised gated mix (dit.c:876-884), with the gated
+      // residual x += gate * Wo(mix) (dit.c:1013-1020) in its epilogue.
       st = quantize_rows_launch(mix, (int)M, D, codes, rs, rz, 0, s);
       if (st) return st;
       GemmRequest o;
@@ -537,16 +685,17 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* para
       o.sx = rs;
       o.zp = rz;
       o.w = &blk->wo;
-      o.y = branch;
+      o.y = x;
       o.ldy = D;
+      o.rgate = gate;
+      o.rgate_rows = S * prow;
       if ((st = gemm_launch(c, o, s))) return st;
     } else {
-      st = iro_int8_swiglu_dev(h, (int)M, &blk->w13, &blk->w2, nullptr, branch,
-                               (blk->residual_mask & 8) != 0, sw_ws, s);
+      // SwiGLU (dit.c:913-969), x += gate * W2(...) in the W2 epilogue.
+      st = swiglu_run(c, fused ? nullptr : h, (int)M, &blk->w13, &blk->w2, nullptr, x,
+                      (blk->residual_mask & 8) != 0, sw_ws, s, gate, S * prow, codes, rs, rz);
       if (st) return st;
     }
-    gated_residual_kernel<<<res_blocks, 256, 0, s>>>(x, branch, gate, (int)M, S, D, prow);
-    if ((st = check_launch())) return st;
   }
   return IRO_OK;
 }
@@ -585,7 +734,9 @@ int iro_dit_block_dev(const IroDiTBlockDev* blk, float* x, const float* cond, in
   float* params = reinterpret_cast<float*>(ws + body);
   void* scratch = ws + body + al256(sizeof(float) * 6 * (size_t)B * blk->model_dim);
   if ((st = dit_adaln_params(&blk, 1, cond, cond_rows, params, scratch, s))) return st;
-  return dit_block_run(c, blk, x, params, cond_rows, ctx_k, ctx_v, ctx_mask, context_batch, B,
+  const float* ada[6];
+  for (int i = 0; i < 6; i++) ada[i] = params + (size_t)i * cond_rows * blk->model_dim;
+  return dit_block_run(c, blk, x, ada, cond_rows, ctx_k, ctx_v, ctx_mask, context_batch, B,
                        S, C, rope_cos, rope_sin, ws, s);
 }
 

@@ -24,9 +24,9 @@ int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, co
 // Workspace of dit_block_run.
 size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int context_batch);
 
-// The block (dit.c:983-1051) on x [B*S, D] with precomputed parameters
-// [2][3][cond_rows][D] (one block's slice of dit_adaln_params).
-int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* params,
+// The block (dit.c:983-1051) on x [B*S, D] with precomputed AdaLN
+// parameters: ada[half * 3 + branch] -> [cond_rows][D] (shift, scale, gate).
+int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* const* ada,
                   int cond_rows, const float* ctx_k, const float* ctx_v,
                   const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
                   const float* rcos, const float* rsin, void* workspace, cudaStream_t s);

@@ -4,8 +4,8 @@
 //   conditioner  timestep embedding -> linear, silu -> linear, silu -> linear
 //                (dit.c:488-530), computed once per step: every row of a step
 //                shares the timestep (sampler.c:246-253)
-//   input        x_t [R*S, 32] -> [R*S, D] (dit.c:532-541), broadcast to the
-//                request's CFG rows (sampler.c:256-262)
+//   input        x_t [R*S, 32] -> [R*S, D] (dit.c:532-541), each output row
+//                stored to the request's CFG rows (sampler.c:256-262)
 //   blocks       iro_dit_block_dev, one context block per request shared by
 //                its CFG rows (sampler.c:219-224)
 //   output       RMSNorm + linear D -> 32 (dit.c:1070-1090)
@@ -30,25 +30,25 @@ namespace {
 
 // y[M, N] = x[M, K] . w[N, K]^T (+ bias), optional silu on y (in place of
 // the reference's separate iro_silu_inplace).  BM x BN output tile per
-// 256-thread block, 4 x 4 outputs per thread, k in increasing order.
+// 256-thread block, TM x TN outputs per thread, k in increasing order.
 constexpr int kLK = 16;
 
-template <int BM, int BN>
+template <int BM, int BN, int TM, int TN>
 __global__ void __launch_bounds__(256) linear_ref_kernel(const float* __restrict__ x,
                                                          const float* __restrict__ w,
                                                          const float* __restrict__ bias,
                                                          float* __restrict__ y, int M, int N, int K,
-                                                         int silu) {
-  static_assert((BM / 4) * (BN / 4) == 256, "4 x 4 outputs per thread, 256 threads");
+                                                         int silu, int ex_cfg, int ex_S) {
+  static_assert((BM / TM) * (BN / TN) == 256, "256 threads");
   __shared__ float xs[kLK][BM + 1];
   __shared__ float ws[kLK][BN + 1];
-  const int tx = threadIdx.x % (BN / 4), ty = threadIdx.x / (BN / 4);
+  const int tx = threadIdx.x % (BN / TN), ty = threadIdx.x / (BN / TN);
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  float acc[4][4];
+  float acc[TM][TN];
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+  for (int i = 0; i < TM; i++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
   for (int k0 = 0; k0 < K; k0 += kLK) {
     for (int i = threadIdx.x; i < BM * kLK; i += 256) {
       const int r = i / kLK, kk = i % kLK;
@@ -64,36 +64,148 @@ __global__ void __launch_bounds__(256) linear_ref_kernel(const float* __restrict
     const int kn = min(kLK, K - k0);
     for (int kk = 0; kk < kn; kk++) {
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int i = 0; i < TM; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-          acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xs[kk][ty * 4 + i], ws[kk][tx * 4 + j]));
+        for (int j = 0; j < TN; j++)
+          acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xs[kk][ty * TM + i], ws[kk][tx * TN + j]));
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int m = m0 + ty * 4 + i;
+  for (int i = 0; i < TM; i++) {
+    const int m = m0 + ty * TM + i;
     if (m >= M) continue;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int n = n0 + tx * 4 + j;
+    for (int j = 0; j < TN; j++) {
+      const int n = n0 + tx * TN + j;
       if (n >= N) continue;
       float v = __fadd_rn(acc[i][j], bias ? bias[n] : 0.0f);
       if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-      y[(size_t)m * N + n] = v;
+      if (ex_cfg <= 1) {
+        y[(size_t)m * N + n] = v;
+      } else {
+        const size_t r = (size_t)(m / ex_S), t = (size_t)(m % ex_S);
+        for (int c = 0; c < ex_cfg; c++) y[((r * ex_cfg + c) * ex_S + t) * N + n] = v;
+      }
     }
   }
 }
 
+// y[M, N] = x[M, K] . w[N, K]^T (+ bias) for a few rows (the conditioner):
+// one warp per (row, 32 outputs) and one warp per block, so the warps spread
+// over the SMs; lane j sums output n0 + j in increasing k (the reference's
+// order) with float4 loads of its own weight row and the broadcast input row.
+__global__ void __launch_bounds__(32) linear_rows_kernel(const float* __restrict__ x,
+                                                          const float* __restrict__ w,
+                                                          const float* __restrict__ bias,
+                                                          float* __restrict__ y, int M, int N,
+                                                          int K, int silu) {
+  const int ngroups = (N + 31) / 32;
+  const long long gw = blockIdx.x;
+  if (gw >= (long long)M * ngroups) return;
+  const int m = (int)(gw / ngroups), n = (int)(gw % ngroups) * 32 + (threadIdx.x & 31);
+  const bool active = n < N;
+  const float* xr = x + (size_t)m * K;
+  const float* wr = w + (size_t)(active ? n : 0) * K;
+  float acc = 0.0f;
+  if ((K & 3) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const float4* w4 = reinterpret_cast<const float4*>(wr);
+#pragma unroll 8
+    for (int k = 0; k < K / 4; k++) {
+      const float4 a = x4[k], b = w4[k];
+      acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+      acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+      acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+      acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+    }
+  } else {
+    for (int k = 0; k < K; k++) acc = __fadd_rn(acc, __fmul_rn(xr[k], wr[k]));
+  }
+  if (!active) return;
+  float v = __fadd_rn(acc, bias ? bias[n] : 0.0f);
+  if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+  y[(size_t)m * N + n] = v;
+}
+
+// y[M, 32] = x[M, K] . w[32, K]^T (+ bias), the output head: W^T staged in
+// shared memory once per persistent block ([K][32], 128 KB for K = 1024), one
+// warp per row, lane j summing output j in increasing k from a conflict-free
+// 128-byte shared row per k and the broadcast input row.
+constexpr size_t kNarrowSmemMax = 160 * 1024;
+
+__global__ void __launch_bounds__(1024, 1) linear_narrow_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ bias,
+                                                                float* __restrict__ y, int M,
+                                                                int K, int silu) {
+  extern __shared__ float wt[];  // [K][32]
+  for (int i = threadIdx.x; i < K * 32; i += 1024) {
+    const int n = i & 31, k = i >> 5;
+    wt[i] = w[(size_t)n * K + k];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float b = bias ? bias[lane] : 0.0f;
+  // Four rows per warp at a time: four independent sums per lane and four
+  // input rows in flight.
+  for (int m0 = (blockIdx.x * 32 + warp) * 4; m0 < M; m0 += gridDim.x * 32 * 4) {
+    const float4* x4[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+      x4[r] = reinterpret_cast<const float4*>(x + (size_t)min(m0 + r, M - 1) * K);
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+    for (int k4 = 0; k4 < K / 4; k4++) {
+      float4 a[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++) a[r] = x4[r][k4];
+      const float* wk = wt + k4 * 128 + lane;
+      const float w0 = wk[0], w1 = wk[32], w2 = wk[64], w3 = wk[96];
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].x, w0));
+        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].y, w1));
+        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].z, w2));
+        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].w, w3));
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      if (m0 + r >= M) break;
+      float v = __fadd_rn(acc[r], b);
+      if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+      y[(size_t)(m0 + r) * 32 + lane] = v;
+    }
+  }
+}
+
+// ex_cfg > 1: output row m is written to the ex_cfg rows
+// ((m / ex_S) * ex_cfg + c) * ex_S + m % ex_S (one request's row broadcast to
+// its CFG rows, sampler.c:256-262).
 int linear_ref(const float* x, const float* w, const float* bias, float* y, int M, int N, int K,
-               int silu, cudaStream_t s) {
-  if (N <= 32)
-    linear_ref_kernel<128, 32><<<dim3(cdiv(N, 32), cdiv(M, 128)), 256, 0, s>>>(x, w, bias, y, M,
-                                                                              N, K, silu);
-  else
-    linear_ref_kernel<64, 64><<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, s>>>(x, w, bias, y, M, N,
-                                                                            K, silu);
+               int silu, cudaStream_t s, int ex_cfg = 1, int ex_S = 1) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15u) == 0;
+  if (ex_cfg <= 1 && aligned && N == 32 && (size_t)K * 32 * 4 <= kNarrowSmemMax &&
+      (K & 3) == 0 && M > 64) {
+    static bool attr = false;
+    const int smem = K * 32 * 4;
+    if (!attr) {
+      cudaFuncSetAttribute(linear_narrow_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kNarrowSmemMax);
+      attr = true;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = std::min(sms, cdiv(M, 128));
+    linear_narrow_kernel<<<grid, 1024, smem, s>>>(x, w, bias, y, M, K, silu);
+  } else if (ex_cfg <= 1 && aligned && M <= 64) {
+    const long long warps = (long long)M * cdiv(N, 32);
+    linear_rows_kernel<<<(unsigned)warps, 32, 0, s>>>(x, w, bias, y, M, N, K, silu);
+  } else
+    linear_ref_kernel<64, 64, 4, 4><<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, s>>>(
+        x, w, bias, y, M, N, K, silu, ex_cfg, ex_S);
   return check_launch();
 }
 
@@ -112,20 +224,6 @@ __global__ void timestep_embedding_kernel(const float* __restrict__ t_dev, float
   const float arg = __fmul_rn(t, freq);
   emb[i] = cosf(arg);
   emb[half + i] = sinf(arg);
-}
-
-// x[(r*cfg + c)*S + s] = p[r*S + s] for every CFG row c of request r.
-__global__ void expand_rows_kernel(const float* __restrict__ p, float* __restrict__ x, int R,
-                                   int cfg, int S, int D) {
-  const long long n = (long long)R * cfg * S * D;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / D;
-    const int d = (int)(i - row * D);
-    const long long s = row % S;
-    const long long r = row / ((long long)S * cfg);
-    x[i] = p[(r * S + s) * D + d];
-  }
 }
 
 // dit.c:1078 / ops.c:738-747: y = x * inv * w, inv = 1 / sqrt(mean(x^2) + eps),
@@ -156,13 +254,13 @@ __global__ void __launch_bounds__(256) rmsnorm_ref_kernel(const float* x,
   }
   if (t < kNR) inv_s[t] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, (float)D), eps)));
   __syncthreads();
-  for (int i = t; i < kNR * D; i += 256) {
-    const int rr = i / D, d = i % D;
+  for (int rr = 0; rr < kNR; rr++) {
     const int m = r0 + rr;
-    if (m < M) {
-      const size_t o = (size_t)m * D + d;
-      y[o] = __fmul_rn(__fmul_rn(x[o], inv_s[rr]), w[d]);
-    }
+    if (m >= M) break;
+    const float inv = inv_s[rr];
+    const float* xm = x + (size_t)m * D;
+    float* ym = y + (size_t)m * D;
+    for (int d = t; d < D; d += 256) ym[d] = __fmul_rn(__fmul_rn(xm[d], inv), w[d]);
   }
 }
 
@@ -254,13 +352,76 @@ int upload_rope(const StepBufs& b, int S, cudaStream_t s) {
   return IRO_OK;
 }
 
+// Conditioning of `n` timesteps at once (dit.c:502-530): cond [n, 3D] and
+// every layer's AdaLN parameters, params [2L sets][3][n][D].  The sampler
+// calls it once for all its steps; a single step calls it with n = 1.
+struct CondBufs {
+  float* t;       // [n] timesteps (device)
+  float* emb;     // [n, TD]
+  float* h0;      // [n, D]
+  float* h1;      // [n, D]
+  float* cond;    // [n, 3D]
+  float* params;  // [2L][3][n][D]
+  void* scratch;
+  int n;
+};
+
+size_t cond_bytes(const IroDiTModelDev* m, int n) {
+  const size_t D = (size_t)m->block[0].model_dim;
+  return al256(sizeof(float) * n) + al256(sizeof(float) * n * m->timestep_dim) +
+         2 * al256(sizeof(float) * n * D) + al256(sizeof(float) * n * 3 * D) +
+         al256(sizeof(float) * 6 * (size_t)m->layers * n * D) +
+         dit_adaln_scratch_bytes(2 * m->layers, n, (int)D, m->block[0].adaln_rank);
+}
+
+CondBufs carve_cond(const IroDiTModelDev* m, int n, uint8_t* ws) {
+  const size_t D = (size_t)m->block[0].model_dim;
+  CondBufs b;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* p = ws + off;
+    off += al256(bytes);
+    return p;
+  };
+  b.t = reinterpret_cast<float*>(take(sizeof(float) * n));
+  b.emb = reinterpret_cast<float*>(take(sizeof(float) * n * m->timestep_dim));
+  b.h0 = reinterpret_cast<float*>(take(sizeof(float) * n * D));
+  b.h1 = reinterpret_cast<float*>(take(sizeof(float) * n * D));
+  b.cond = reinterpret_cast<float*>(take(sizeof(float) * n * 3 * D));
+  b.params = reinterpret_cast<float*>(take(sizeof(float) * 6 * (size_t)m->layers * n * D));
+  b.scratch = ws + off;
+  b.n = n;
+  return b;
+}
+
+int condition_all(const IroDiTModelDev* m, const float* t_host, const CondBufs& b,
+                  cudaStream_t s) {
+  const int D = m->block[0].model_dim, TD = m->timestep_dim, n = b.n;
+  // Pageable source: staged before the call returns.
+  cudaError_t e = cudaMemcpyAsync(b.t, t_host, sizeof(float) * n, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return map_cuda(e);
+  }
+  timestep_embedding_kernel<<<dim3(cdiv(TD / 2, 128), n), 128, 0, s>>>(b.t, 0.0f, TD, b.emb);
+  int st = check_launch();
+  if (st) return st;
+  if ((st = linear_ref(b.emb, m->cond_w0, nullptr, b.h0, n, D, TD, 1, s))) return st;
+  if ((st = linear_ref(b.h0, m->cond_w1, nullptr, b.h1, n, D, D, 1, s))) return st;
+  if ((st = linear_ref(b.h1, m->cond_w2, nullptr, b.cond, n, 3 * D, D, 0, s))) return st;
+  const IroDiTBlockDev* blks[IRO_DIT_MAX_LAYERS];
+  for (int l = 0; l < m->layers; l++) blks[l] = &m->block[l];
+  return dit_adaln_params(blks, m->layers, b.cond, n, b.params, b.scratch, s);
+}
+
 // One step with `cfg` active rows per request, `mask` [R*cfg, C] for those
-// rows; `full_cfg` is the width the scratch was sized for.
+// rows; `full_cfg` is the width the scratch was sized for; the step's
+// conditioning is row `row` of `cb`.
 int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int full_cfg,
               int S, float t, float t_next, const float* scales, const float* const* ctx_k,
               const float* const* ctx_v, const uint8_t* mask, int C, const StepBufs& tb,
-              cudaStream_t s) {
-  const int D = m->block[0].model_dim, L = m->latent_dim, TD = m->timestep_dim;
+              const CondBufs& cb, int row, cudaStream_t s) {
+  const int D = m->block[0].model_dim, L = m->latent_dim;
   const int B = R * cfg, Bfull = R * full_cfg;
   uint8_t* ws = tb.rest;
   size_t off = 0;
@@ -269,35 +430,18 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
     off += al256(bytes);
     return p;
   };
-  float* emb = reinterpret_cast<float*>(take(sizeof(float) * TD));
-  float* h0 = reinterpret_cast<float*>(take(sizeof(float) * D));
-  float* h1 = reinterpret_cast<float*>(take(sizeof(float) * D));
-  float* cond = reinterpret_cast<float*>(take(sizeof(float) * 3 * (size_t)D));
-  float* proj = reinterpret_cast<float*>(take(sizeof(float) * (size_t)R * S * D));
   float* x = reinterpret_cast<float*>(take(sizeof(float) * (size_t)Bfull * S * D));
   float* vel = reinterpret_cast<float*>(take(sizeof(float) * (size_t)Bfull * S * L));
-  float* params = reinterpret_cast<float*>(take(sizeof(float) * 6 * (size_t)m->layers * D));
-  void* ada_scratch = take(dit_adaln_scratch_bytes(2 * m->layers, 1, D, m->block[0].adaln_rank));
   void* blk_ws = ws + off;
   int st;
-  // Conditioner, once: every row shares the timestep.
-  timestep_embedding_kernel<<<cdiv(TD / 2, 128), 128, 0, s>>>(nullptr, t, TD, emb);
-  if ((st = check_launch())) return st;
-  if ((st = linear_ref(emb, m->cond_w0, nullptr, h0, 1, D, TD, 1, s))) return st;
-  if ((st = linear_ref(h0, m->cond_w1, nullptr, h1, 1, D, D, 1, s))) return st;
-  if ((st = linear_ref(h1, m->cond_w2, nullptr, cond, 1, 3 * D, D, 0, s))) return st;
-  // Input projection per request, broadcast to its CFG rows.
-  if ((st = linear_ref(state, m->in_w, m->in_b, proj, R * S, D, L, 0, s))) return st;
-  const int eb = (int)std::min<long long>(((long long)B * S * D + 255) / 256, c->num_sms * 16LL);
-  expand_rows_kernel<<<eb, 256, 0, s>>>(proj, x, R, cfg, S, D);
-  if ((st = check_launch())) return st;
-  // Every layer's AdaLN parameters in one batch: the step's rows share cond.
-  const IroDiTBlockDev* blks[IRO_DIT_MAX_LAYERS];
-  for (int l = 0; l < m->layers; l++) blks[l] = &m->block[l];
-  if ((st = dit_adaln_params(blks, m->layers, cond, 1, params, ada_scratch, s))) return st;
+  // Input projection per request, each row stored to its CFG rows.
+  if ((st = linear_ref(state, m->in_w, m->in_b, x, R * S, D, L, 0, s, cfg, S))) return st;
   for (int l = 0; l < m->layers; l++) {
-    st = dit_block_run(c, &m->block[l], x, params + (size_t)l * 6 * D, 1, ctx_k[l], ctx_v[l],
-                       mask, R, B, S, C, tb.rcos, tb.rsin, blk_ws, s);
+    const float* ada[6];
+    for (int i = 0; i < 6; i++)
+      ada[i] = cb.params + (((size_t)(2 * l) * 3 + i) * cb.n + row) * D;
+    st = dit_block_run(c, &m->block[l], x, ada, 1, ctx_k[l], ctx_v[l], mask, R, B, S, C, tb.rcos,
+                       tb.rsin, blk_ws, s);
     if (st) return st;
   }
   // Output head (normalised in place: x is rebuilt from the state next
@@ -349,16 +493,16 @@ using namespace iro;
 extern "C" {
 
 size_t iro_dit_step_workspace_bytes(const IroDiTModelDev* m, int R, int cfg, int S, int C) {
-  if (!valid_model(m) || R <= 0 || cfg <= 0 || S <= 0 || C <= 0) return 0;
+  return iro_dit_sample_workspace_bytes(m, R, cfg, S, C, 1);
+}
+
+size_t iro_dit_sample_workspace_bytes(const IroDiTModelDev* m, int R, int cfg, int S, int C,
+                                      int steps) {
+  if (!valid_model(m) || R <= 0 || cfg <= 0 || S <= 0 || C <= 0 || steps <= 0) return 0;
   const int D = m->block[0].model_dim, B = R * cfg;
-  size_t t = head_bytes(R, S, C);
-  t += al256(sizeof(float) * (size_t)m->timestep_dim);                 // embedding
-  t += 2 * al256(sizeof(float) * (size_t)D) + al256(sizeof(float) * 3 * (size_t)D);  // cond
-  t += al256(sizeof(float) * (size_t)R * S * D);                       // projected
+  size_t t = head_bytes(R, S, C) + cond_bytes(m, steps);
   t += al256(sizeof(float) * (size_t)B * S * D);                       // x
   t += al256(sizeof(float) * (size_t)B * S * m->latent_dim);           // velocity
-  t += al256(sizeof(float) * 6 * (size_t)m->layers * D);               // AdaLN params
-  t += dit_adaln_scratch_bytes(2 * m->layers, 1, D, m->block[0].adaln_rank);
   return t + dit_block_body_bytes(&m->block[0], B, S, C, R);
 }
 
@@ -378,10 +522,12 @@ int iro_dit_euler_step_dev(const IroDiTModelDev* m, float* state, int R, int cfg
     if (!ws) return st;
   }
   StepBufs tb = carve(ws, S);
-  tb.rest = ws + head_bytes(R, S, C);
+  const CondBufs cb = carve_cond(m, 1, ws + head_bytes(R, S, C));
+  tb.rest = ws + head_bytes(R, S, C) + cond_bytes(m, 1);
   if ((st = upload_rope(tb, S, s))) return st;
+  if ((st = condition_all(m, &t, cb, s))) return st;
   return step_impl(c, m, state, R, cfg, cfg, S, t, t_next, cfg_scales, ctx_k, ctx_v, mask, C, tb,
-                   s);
+                   cb, 0, s);
 }
 
 int iro_dit_sample_euler_dev(const IroDiTModelDev* m, float* state, int R, int cfg, int S,
@@ -398,26 +544,34 @@ int iro_dit_sample_euler_dev(const IroDiTModelDev* m, float* state, int R, int c
   cudaStream_t s = pick_stream(c, stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (!ws) {
-    ws = static_cast<uint8_t*>(arena_get(c, iro_dit_step_workspace_bytes(m, R, cfg, S, C), &st));
+    ws = static_cast<uint8_t*>(
+        arena_get(c, iro_dit_sample_workspace_bytes(m, R, cfg, S, C, steps), &st));
     if (!ws) return st;
   }
+  // sampler.c:244-249: the timestep schedule, in the reference's float
+  // arithmetic; all steps' conditioning is computed up front.
+  std::vector<float> ts(steps), tn(steps);
+  for (int step = 0; step < steps; step++) {
+    const float u = (float)step / (float)steps;
+    const float u_next = (float)(step + 1) / (float)steps;
+    ts[step] = (1.0f - u) * init_scale;
+    tn[step] = (1.0f - u_next) * init_scale;
+  }
   StepBufs tb = carve(ws, S);
-  tb.rest = ws + head_bytes(R, S, C);
+  const CondBufs cb = carve_cond(m, steps, ws + head_bytes(R, S, C));
+  tb.rest = ws + head_bytes(R, S, C) + cond_bytes(m, steps);
   if ((st = upload_rope(tb, S, s))) return st;
+  if ((st = condition_all(m, ts.data(), cb, s))) return st;
   if (cfg > 1) {
     const int mb = (int)std::min<long long>(((long long)R * C + 255) / 256, c->num_sms * 4LL);
     cond_mask_kernel<<<mb, 256, 0, s>>>(mask, tb.cond_mask, R, cfg, C);
     if ((st = check_launch())) return st;
   }
   for (int step = 0; step < steps; step++) {
-    // sampler.c:244-249, in the reference's float arithmetic.
-    const float u = (float)step / (float)steps;
-    const float u_next = (float)(step + 1) / (float)steps;
-    const float t = (1.0f - u) * init_scale;
-    const float t_next = (1.0f - u_next) * init_scale;
+    const float t = ts[step];
     const bool use_cfg = cfg > 1 && t >= cfg_min_t && t <= cfg_max_t;
-    st = step_impl(c, m, state, R, use_cfg ? cfg : 1, cfg, S, t, t_next, cfg_scales, ctx_k, ctx_v,
-                   use_cfg ? mask : (cfg > 1 ? tb.cond_mask : mask), C, tb, s);
+    st = step_impl(c, m, state, R, use_cfg ? cfg : 1, cfg, S, t, tn[step], cfg_scales, ctx_k,
+                   ctx_v, use_cfg ? mask : (cfg > 1 ? tb.cond_mask : mask), C, tb, cb, step, s);
     if (st) return st;
   }
   return IRO_OK;

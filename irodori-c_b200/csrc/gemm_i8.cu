@@ -66,6 +66,7 @@ struct Cfg {
 
 struct GemmParams {
   int M, N, K, num_kb, tiles_m, tiles_n, num_tiles;
+  int n_fast;  // tile order: N blocks fastest (A reused through L2) or M blocks fastest
   const float* sx;
   const int32_t* zp;
   const float* sx2;
@@ -78,6 +79,8 @@ struct GemmParams {
   int32_t* work;
   int ldw;
   int accumulate;
+  const float* rgate;
+  int rgate_rows;
   int tma_out;  // outputs written by TMA tile stores (else direct stores)
   float* outs[4];
   int seg;
@@ -95,6 +98,20 @@ struct GemmParams {
 // exit, tiles processed.
 enum { TR_ENTRY = 0, TR_TMA0, TR_FULL0, TR_MMA_END0, TR_EPI0, TR_EPI_END0, TR_EXIT, TR_TILES,
        TR_SLOTS = 8 };
+
+// Tile -> (row block, column block).  N-fastest when the activation operand
+// is the larger one: the CTAs in flight then share a few row blocks of A
+// (read once from DRAM, the rest from L2) instead of streaming all of A once
+// per column block.
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& mb, int& nb) {
+  if (p.n_fast) {
+    mb = t / p.tiles_n;
+    nb = t - mb * p.tiles_n;
+  } else {
+    nb = t / p.tiles_m;
+    mb = t - nb * p.tiles_m;
+  }
+}
 
 __device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
   if (p.trace) p.trace[blockIdx.x * TR_SLOTS + slot] = globaltimer_ns();
@@ -164,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
         for (int kb = 0; kb < p.num_kb; kb++) {
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 1, abort_flag, p.limit_ns)) {
             ok = false;
@@ -250,7 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int zp, zp2;
     } pf;
     auto fetch = [&](int t) {
-      const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+      int mb, nb;
+      tile_coords(p, t, mb, nb);
       const int n = nb * BN + et;
       const bool ok = et < BN && n < p.N;
       pf.cs = ok ? __ldg(p.wcolsum + n) : 0;
@@ -265,7 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if ((int)blockIdx.x < p.num_tiles) fetch(blockIdx.x);
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      const int mb = tile % p.tiles_m, nb = tile / p.tiles_m;
+      int mb, nb;
+      tile_coords(p, tile, mb, nb);
       // Stage this tile's per-column parameters (the buffer was last read by
       // the tile before the previous one, which every warp has finished).
       float* pc = prm + pbuf * 3 * BN;
@@ -354,10 +374,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* drow = base + (size_t)row * ld + col0;
           const int valid = ncols - col0;
           float v[kChunk];
-          if ((EPI == EPI_LINEAR || EPI == EPI_DUAL) && p.accumulate) {
+          const bool gated_res = (EPI == EPI_LINEAR || EPI == EPI_DUAL) && p.rgate != nullptr;
+          if ((EPI == EPI_LINEAR || EPI == EPI_DUAL) && (p.accumulate || gated_res)) {
+            if (p.tma_out && valid >= kChunk) {
+              // 16-byte aligned rows (the TMA store path requires it): four
+              // vector loads per lane instead of sixteen scalar ones.
 #pragma unroll
-            for (int j = 0; j < kChunk; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
+              for (int j = 0; j < kChunk / 4; j++) {
+                const float4 o4 = row_ok ? reinterpret_cast<const float4*>(drow)[j]
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[4 * j] = o4.x;
+                v[4 * j + 1] = o4.y;
+                v[4 * j + 2] = o4.z;
+                v[4 * j + 3] = o4.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kChunk; j++) v[j] = (row_ok && j < valid) ? drow[j] : 0.0f;
+            }
           }
+          const float* grow =
+              (gated_res && row_ok) ? p.rgate + (size_t)(row / p.rgate_rows) * p.N + n0 : nullptr;
 #pragma unroll
           for (int i = 0; i < kChunk / 4; i++) {
             const int c = c0 + 4 * i;
@@ -383,6 +420,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (EPI == EPI_LINEAR && p.accumulate) {
               lo = add2_rn(make_float2(v[4 * i], v[4 * i + 1]), lo);
               hi = add2_rn(make_float2(v[4 * i + 2], v[4 * i + 3]), hi);
+            }
+            if (gated_res) {
+              const float4 gv = grow ? *reinterpret_cast<const float4*>(grow + 4 * i)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+              lo = make_float2(__fadd_rn(v[4 * i], __fmul_rn(gv.x, lo.x)),
+                               __fadd_rn(v[4 * i + 1], __fmul_rn(gv.y, lo.y)));
+              hi = make_float2(__fadd_rn(v[4 * i + 2], __fmul_rn(gv.z, hi.x)),
+                               __fadd_rn(v[4 * i + 3], __fmul_rn(gv.w, hi.y)));
             }
             v[4 * i] = lo.x;
             v[4 * i + 1] = lo.y;
@@ -510,6 +555,11 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
   p.tiles_m = cdiv(r.M, BM);
   p.tiles_n = cdiv(w->N, BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
+  {
+    const size_t a_bytes = (size_t)r.M * w->K * (r.epi == EPI_DUAL ? 2 : 1);
+    const size_t b_bytes = (size_t)w->N * w->K;
+    p.n_fast = a_bytes > b_bytes ? 1 : 0;
+  }
   const int grid = p.num_tiles < c->num_sms ? p.num_tiles : c->num_sms;
   unsigned long long* tr = nullptr;
   if (trace_enabled() && !r.no_alloc) {
@@ -553,6 +603,10 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   if (r.M == 0) return IRO_OK;
   if (r.M < 0 || !w || !w->data || !r.a || !r.sx || !r.zp) return IRO_ERR_INVALID;
   if ((r.lda & 15) != 0 || r.lda < w->K) return IRO_ERR_UNSUPPORTED;
+  if (r.rgate && ((r.epi != EPI_LINEAR && r.epi != EPI_DUAL) || r.accumulate || !r.y ||
+                  r.rgate_rows <= 0 || (w->N & 15) != 0 ||
+                  (reinterpret_cast<uintptr_t>(r.rgate) & 15u) != 0))
+    return IRO_ERR_INVALID;
   GemmParams p{};
   p.M = r.M;
   p.N = w->N;
@@ -570,6 +624,8 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   p.work = r.work;
   p.ldw = r.ldw;
   p.accumulate = r.accumulate;
+  p.rgate = r.rgate;
+  p.rgate_rows = r.rgate_rows;
   for (int i = 0; i < 4; i++) p.outs[i] = r.outs[i];
   p.seg = r.seg;
   p.hidden = r.hidden;

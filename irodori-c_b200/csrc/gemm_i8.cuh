@@ -36,11 +36,27 @@ struct GemmRequest {
   int nout = 0, seg = 0;
   float* hidden = nullptr;  // GATED: [M, w->hidden], row pitch ldh
   int ldh = 0;
+  // EPI_LINEAR / EPI_DUAL: y += rgate[row / rgate_rows][n] * result (the
+  // DiT's gated residual, dit.c:1013-1020, in its order: the result rounded,
+  // times the gate, then added); `accumulate` must be 0.
+  const float* rgate = nullptr;
+  int rgate_rows = 0;
   int force_bn = 0;         // 0 = heuristic
   int no_alloc = 0;         // never allocate (skips the IRO_GEMM_TRACE buffer)
 };
 
 int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
+
+// iro_int8_swiglu_dev with an optional gated residual in the W2 epilogue:
+// out += rgate[row / rgate_rows] * swiglu(x) when rgate is set (out then
+// holds the residual stream), out = swiglu(x) otherwise.  With qx set, x is
+// already quantised (codes qx [M, K], row scale sx and zero point zx) and
+// x itself is not read.
+int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
+               const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2,
+               void* workspace, cudaStream_t s, const float* rgate, int rgate_rows,
+               const uint8_t* qx = nullptr, const float* sx = nullptr,
+               const int32_t* zx = nullptr);
 
 // Split-K over a two-CTA cluster for plain linears with few, long tiles
 // (gemm_splitk.cu); gemm_launch picks it when eligible and IRO_GEMM_SPLITK=1.

@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
 }  // namespace
 
 bool splitk_eligible(const GemmRequest& r, int num_sms) {
-  if (r.epi != EPI_LINEAR || r.work || r.force_bn) return false;
+  if (r.epi != EPI_LINEAR || r.work || r.force_bn || r.rgate) return false;
   const IroInt8DevWeight* w = r.w;
   const int num_kb = cdiv(w->K, SBK);
   const int tiles = cdiv(r.M, SBM) * cdiv(w->N, SBN);

@@ -134,6 +134,7 @@ SIGNATURES = {
     "iro_dit_euler_step_dev": (_i, [_vp, _vp, _i, _i, _i, C.c_float, C.c_float, _vp, _vp, _vp,
                                     _vp, _i, _vp, _vp]),
     "iro_dit_stage_workspace_bytes": (_sz, [_vp, _i]),
+    "iro_dit_sample_workspace_bytes": (_sz, [_vp, _i, _i, _i, _i, _i]),
     "iro_dit_condition_dev": (_i, [_vp, _vp, _i, _vp, _vp, _vp]),
     "iro_dit_input_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "iro_dit_output_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
@@ -679,8 +680,11 @@ class DiTModel:
         check(lib().iro_dit_output_dev(C.byref(self.st), _p(x), B, S, _p(velocity), None, None),
               "dit_output_dev")
 
-    def workspace_bytes(self, R, cfg, S, n_ctx):
-        return lib().iro_dit_step_workspace_bytes(C.byref(self.st), R, cfg, S, n_ctx)
+    def workspace_bytes(self, R, cfg, S, n_ctx, steps=None):
+        """Workspace of one euler_step, or of sample_euler over `steps`."""
+        if steps is None:
+            return lib().iro_dit_step_workspace_bytes(C.byref(self.st), R, cfg, S, n_ctx)
+        return lib().iro_dit_sample_workspace_bytes(C.byref(self.st), R, cfg, S, n_ctx, steps)
 
 
 class StFile:
