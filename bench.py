@@ -524,7 +524,7 @@ def run_profile_case(args):
         print(f"profile case conv7: {args.warmup + args.steps} launches ok")
         return
 
-    if args.profile in ("dit_qkvg", "dit_w2"):
+    if args.profile in ("dit_qkvg", "dit_w2", "dit_w13"):
         # The config-3 DiT's GEMMs at full size, M = 24000 rows: the fused
         # QKVG projection (N = 4 x 1024, K = 1024, four fp32 outputs) or the
         # two-term W2 (N = 1024, K = 2816) with the gated residual epilogue.
@@ -541,6 +541,16 @@ def run_profile_case(args):
             outs = [iro.DevBuf((Mq, Dm), np.float32) for _ in range(4)]
             for _ in range(args.warmup + args.steps):
                 iro.linear_split_dev(q, s_, z, dw, outs, Dm, Mq)
+        elif args.profile == "dit_w13":
+            w13 = iro.DevWeight.gated_pair(iro.HostWeight(f(Hm, Dm, sc=0.03)),
+                                           iro.HostWeight(f(Hm, Dm, sc=0.03)))
+            xq = iro.DevBuf.from_host(f(Mq, Dm))
+            q, s_, z = (iro.DevBuf((Mq, Dm), np.uint8), iro.DevBuf(Mq, np.float32),
+                        iro.DevBuf(Mq, np.int32))
+            iro.quantize_rows_dev(xq, Mq, Dm, q, s_, z)
+            hid = iro.DevBuf((Mq, Hm), np.float32)
+            for _ in range(args.warmup + args.steps):
+                iro.gated_dev(q, s_, z, w13, hid, Mq)
         else:
             w2 = iro.DevWeight.upload(iro.HostWeight(f(Dm, Hm, sc=0.02)))
             hq = iro.DevBuf.from_host(f(Mq, Hm))
@@ -865,7 +875,7 @@ def main():
     ap.add_argument("--workload", choices=["swiglu", "conv7", "init", "dit"], default="swiglu",
                     help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
     ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7", "ditblock",
-                                          "dit_qkvg", "dit_w2"],
+                                          "dit_qkvg", "dit_w2", "dit_w13"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
     ap.add_argument("--dit-dims", choices=["cfg3", "reference"], default="cfg3",
                     help="dit workload: config 3's d1024/16 heads/2816, or the reference "

@@ -54,12 +54,11 @@ constexpr int kMaxCtxWords = 256;       // context mask bits in shared memory (C
 constexpr int kSmem = 1024 + kBarOff + 256 + 4 * kMaxCtxWords;
 // Two CTAs per SM: 2 x 99 KB of shared memory, 2 x 256 TMEM columns.
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColO = 2 * kKT;     // S/P buffers at columns 0 and kKT
+constexpr int kSBufs = 3;               // S/P buffers in TMEM
+constexpr uint32_t kColO = kSBufs * kKT;  // S/P buffers at columns 0, 64, 128; O at 192
 // Scores are kept in the log2 domain: t = s_raw * (1/8) * log2(e), p = 2^(t - m).
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
 constexpr float kRescaleGap = 8.0f * 1.4426950408889634f;  // e^8 in the log2 domain
-constexpr uint32_t kIdescS = idesc_tf32(kQ, kKT, 0);
-constexpr uint32_t kIdescPV = idesc_tf32(kQ, kDH, 0);
 
 // vt[((b * heads + h) * 64 + d) * ld + s] = v[(b * S + s) * D + h * 64 + d],
 // zero for s in [S, ld).  One block per (32 tokens, head, row block).
@@ -100,11 +99,110 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// CTA pairs (a two-CTA cluster sharing one tcgen05 MMA of M = 256).
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Bounded wait with cluster-scope acquire: for phases completed by arrivals
+// from the peer CTA's threads (their TMEM writes must be visible here).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, DevError* err,
+                                                  int where, volatile int* abort_flag,
+                                                  uint64_t limit_ns) {
+  auto poll = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+  };
+  if (poll()) return true;
+  const long long t0 = clock64();
+  const long long limit_cycles = (long long)(limit_ns * 2ull);
+  while (!poll()) {
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (clock64() - t0 > limit_cycles) {
+      report_error(err, IRO_ERR_DEVICE_TIMEOUT, where);
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
+               : "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t mbar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_ss_pair(uint32_t d, uint64_t a, uint64_t b,
+                                                 uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_ts_pair(uint32_t d, uint32_t a, uint64_t b,
+                                                 uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive on the same barrier in both CTAs of the pair once the pair's MMAs
+// issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
 template <int N>
 __device__ __forceinline__ uint32_t (&sub32(uint32_t (&r)[N], int c))[32] {
   return *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]);
 }
 
+// PAIR: a two-CTA cluster computes 256 query rows with M = 256 MMAs issued
+// by the leader (rank 0); each CTA loads its own Q rows, half of each K tile
+// (32 of 64 keys) and half of each V^T tile (32 of 64 dimensions), and the
+// TMA completions, P hand-offs and MMA commits meet on the leader's barriers
+// (commits multicast to both CTAs).  Otherwise one CTA runs M = 128.
+template <bool PAIR>
 __global__ void __launch_bounds__(kThreads, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -118,30 +216,41 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* sK = smem + kQBytes;         // two stages
   uint8_t* sV = sK + 2 * kKBytes;       // two stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 3;
-  uint64_t* kv_empty = bars + 5;
-  uint64_t* s_full = bars + 7;
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 11;
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* q_full = bars;         // 1
+  uint64_t* k_full = bars + 1;     // 2 stages
+  uint64_t* v_full = bars + 3;     // 2 stages
+  uint64_t* k_empty = bars + 5;    // 2 stages (after S)
+  uint64_t* v_empty = bars + 7;    // 2 stages (after PV)
+  uint64_t* s_full = bars + 9;     // 3 S/P buffers
+  uint64_t* p_full = bars + 12;    // 3
+  uint64_t* pv_done = bars + 15;   // 3
+  uint64_t* drain = bars + 18;     // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* ctx_bits = reinterpret_cast<uint32_t*>(smem + kBarOff + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, hd = blockIdx.y, q0 = blockIdx.x * kQ;
   const int T = a.n_self + a.n_ctx;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  // Per-CTA shares of the K and V^T tiles (bytes of one 32-wide slice).
+  constexpr int KH = (PAIR ? kKT / 2 : kKT) * 128;   // K rows x 128 B
+  constexpr int VC = (PAIR ? kDH / 2 : kDH) * 128;   // V^T rows x 128 B
+  constexpr uint32_t IDS = idesc_tf32(PAIR ? 2 * kQ : kQ, kKT, 0);
+  constexpr uint32_t IDPV = idesc_tf32(PAIR ? 2 * kQ : kQ, kDH, 0);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; i++) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < kSBufs; i++) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], PAIR ? 256 : 128);
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -156,105 +265,173 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&tmCV);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // the leader's barriers exist before the peer uses them
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   grid_dep_wait();
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      const int qrow0 = b * a.S + q0;
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      tma_load_2d(sQ, &tmQ, q_full, hd * kDH, qrow0);
-      tma_load_2d(sQ + kQHalf, &tmQ, q_full, hd * kDH + 32, qrow0);
+    // ---------------- TMA producers: lane 0 Q and K, lane 1 V^T ----------------
+    if (lane < 2) {
       const int cb = b / a.ctx_group;
       int issued = 0;
+      if (lane == 0) {
+        const int qrow0 = b * a.S + q0;
+        if (PAIR) {
+          // The leader's MMAs read both CTAs' Q rows: both loads count on the
+          // leader's q_full.
+          const uint32_t qb = cluster_addr(q_full, 0);
+          if (leader) mbar_arrive_expect_tx(q_full, 2 * kQBytes);
+          tma_load_2d_pair(sQ, &tmQ, qb, hd * kDH, qrow0);
+          tma_load_2d_pair(sQ + kQHalf, &tmQ, qb, hd * kDH + 32, qrow0);
+        } else {
+          mbar_arrive_expect_tx(q_full, kQBytes);
+          tma_load_2d(sQ, &tmQ, q_full, hd * kDH, qrow0);
+          tma_load_2d(sQ + kQHalf, &tmQ, q_full, hd * kDH + 32, qrow0);
+        }
+      }
+      uint64_t* full = lane == 0 ? k_full : v_full;
+      uint64_t* empty = lane == 0 ? k_empty : v_empty;
       for (int j = 0; j < T; j++) {
         const int st = j & 1;
-        if (j >= 2 &&
-            !mbar_wait_bounded(&kv_empty[st], ((j - 2) >> 1) & 1, a.err, 1, abort_flag,
-                               a.limit_ns))
+        if (j >= 2 && !mbar_wait_bounded(&empty[st], ((j - 2) >> 1) & 1, a.err, 1, abort_flag,
+                                         a.limit_ns))
           break;
         const bool self = j < a.n_self;
-        const CUtensorMap* mk = self ? &tmK : &tmCK;
-        const CUtensorMap* mv = self ? &tmV : &tmCV;
-        const int y = self ? b * a.S + j * kKT : cb * a.C + (j - a.n_self) * kKT;
-        const int x0 = (self ? j : j - a.n_self) * kKT;           // first key of the tile
-        const int vrow = ((self ? b : cb) * a.heads + hd) * kDH;  // first V^T row
-        uint8_t* dk = sK + st * kKBytes;
-        uint8_t* dv = sV + st * kVBytes;
-        mbar_arrive_expect_tx(&k_full[st], kKBytes);
-        tma_load_2d(dk, mk, &k_full[st], hd * kDH, y);
-        tma_load_2d(dk + kKHalf, mk, &k_full[st], hd * kDH + 32, y);
-        mbar_arrive_expect_tx(&v_full[st], kVBytes);
+        const uint32_t fb = PAIR ? cluster_addr(&full[st], 0) : 0u;
+        if (lane == 0) {
+          // This CTA's key rows of tile j.
+          const CUtensorMap* mk = self ? &tmK : &tmCK;
+          const int y = (self ? b * a.S + j * kKT : cb * a.C + (j - a.n_self) * kKT) +
+                        (int)rank * (KH / 128);
+          uint8_t* dk = sK + st * kKBytes;
+          if (PAIR) {
+            // Both CTAs' halves complete on the leader's barrier, which
+            // expects the pair's bytes (one CTA's full-tile total).
+            if (leader) mbar_arrive_expect_tx(&full[st], kKBytes);
+            tma_load_2d_pair(dk, mk, fb, hd * kDH, y);
+            tma_load_2d_pair(dk + KH, mk, fb, hd * kDH + 32, y);
+          } else {
+            mbar_arrive_expect_tx(&full[st], kKBytes);
+            tma_load_2d(dk, mk, &full[st], hd * kDH, y);
+            tma_load_2d(dk + KH, mk, &full[st], hd * kDH + 32, y);
+          }
+        } else {
+          // This CTA's V^T rows (head dimensions) of tile j.
+          const CUtensorMap* mv = self ? &tmV : &tmCV;
+          const int x0 = (self ? j : j - a.n_self) * kKT;
+          const int vrow = ((self ? b : cb) * a.heads + hd) * kDH + (int)rank * (VC / 128);
+          uint8_t* dv = sV + st * kVBytes;
+          if (PAIR) {
+            if (leader) mbar_arrive_expect_tx(&full[st], kVBytes);
 #pragma unroll
-        for (int c = 0; c < kKT / 32; c++)
-          tma_load_2d(dv + c * kVtChunk, mv, &v_full[st], x0 + 32 * c, vrow);
+            for (int c = 0; c < kKT / 32; c++) tma_load_2d_pair(dv + c * VC, mv, fb, x0 + 32 * c, vrow);
+          } else {
+            mbar_arrive_expect_tx(&full[st], kVBytes);
+#pragma unroll
+            for (int c = 0; c < kKT / 32; c++)
+              tma_load_2d(dv + c * VC, mv, &full[st], x0 + 32 * c, vrow);
+          }
+        }
         issued = j + 1;
       }
       // Drain: every load issued has landed before the CTA may exit (on the
       // normal path these phases completed long ago).
-      mbar_wait_bounded(q_full, 0, a.err, 9, nullptr, a.limit_ns);
-      for (int j = issued - 1; j >= 0 && j >= issued - 2; j--) {
-        mbar_wait_bounded(&k_full[j & 1], (j >> 1) & 1, a.err, 9, nullptr, a.limit_ns);
-        mbar_wait_bounded(&v_full[j & 1], (j >> 1) & 1, a.err, 9, nullptr, a.limit_ns);
-      }
+      if (leader && lane == 0) mbar_wait_bounded(q_full, 0, a.err, 9, nullptr, a.limit_ns);
+      for (int j = issued - 1; leader && j >= 0 && j >= issued - 2; j--)
+        mbar_wait_bounded(&full[j & 1], (j >> 1) & 1, a.err, 9, nullptr, a.limit_ns);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (the leader's, for a pair) ----------------
+    // Order: S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | ... | PV_{T-1}.  With three
+    // S/P buffers, S_{j+3} only waits for PV_j, so the softmax of tile j+1
+    // never waits for the PV of tile j.
+    if (lane == 0 && leader) {
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait_bounded(q_full, 0, a.err, 2, abort_flag, a.limit_ns);
-      for (int j = 0; ok && j <= T; j++) {
-        if (j < T) {
-          const int st = j & 1;
-          if (!mbar_wait_bounded(&k_full[st], (j >> 1) & 1, a.err, 3, abort_flag, a.limit_ns) ||
-              (j >= 2 && !mbar_wait_bounded(&pv_done[st], ((j - 2) >> 1) & 1, a.err, 4,
-                                            abort_flag, a.limit_ns))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * kKBytes);
-          const uint32_t d = tmem + (uint32_t)(st * kKT);
+      auto commit = [&](uint64_t* bar) {
+        if (PAIR) mma_commit_pair(bar);
+        else mma_commit(bar);
+      };
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1, sb = j % kSBufs;
+        if (!mbar_wait_bounded(&k_full[st], (j >> 1) & 1, a.err, 3, abort_flag, a.limit_ns))
+          return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * kKBytes);
+        const uint32_t d = tmem + (uint32_t)(sb * kKT);
 #pragma unroll
-          for (int ks = 0; ks < kDH / 8; ks++) {
-            const uint32_t qo = (uint32_t)((ks >> 2) * kQHalf + (ks & 3) * 32);
-            const uint32_t ko = (uint32_t)((ks >> 2) * kKHalf + (ks & 3) * 32);
-            mma_tf32_ss(d, sw128_desc(q_addr + qo), sw128_desc(k_addr + ko), kIdescS,
+        for (int ks = 0; ks < kDH / 8; ks++) {
+          const uint32_t qo = (uint32_t)((ks >> 2) * kQHalf + (ks & 3) * 32);
+          const uint32_t ko = (uint32_t)((ks >> 2) * KH + (ks & 3) * 32);
+          if (PAIR)
+            mma_tf32_ss_pair(d, sw128_desc(q_addr + qo), sw128_desc(k_addr + ko), IDS,
+                             ks > 0 ? 1u : 0u);
+          else
+            mma_tf32_ss(d, sw128_desc(q_addr + qo), sw128_desc(k_addr + ko), IDS,
                         ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[st]);
         }
-        if (j >= 1) {
-          const int pj = j - 1, pst = pj & 1;
-          if (!mbar_wait_bounded(&p_full[pst], (pj >> 1) & 1, a.err, 5, abort_flag,
-                                 a.limit_ns) ||
-              !mbar_wait_bounded(&v_full[pst], (pj >> 1) & 1, a.err, 6, abort_flag,
-                                 a.limit_ns)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + pst * kVBytes);
-          const uint32_t p_tmem = tmem + (uint32_t)(pst * kKT);
+        commit(&s_full[sb]);
+        commit(&k_empty[st]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j & 1, sb = j % kSBufs;
+        if (!(PAIR ? mbar_wait_cluster(&p_full[sb], (j / kSBufs) & 1, a.err, 5, abort_flag,
+                                       a.limit_ns)
+                   : mbar_wait_bounded(&p_full[sb], (j / kSBufs) & 1, a.err, 5, abort_flag,
+                                       a.limit_ns)) ||
+            !mbar_wait_bounded(&v_full[st], (j >> 1) & 1, a.err, 6, abort_flag, a.limit_ns))
+          return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + st * kVBytes);
+        const uint32_t p_tmem = tmem + (uint32_t)(sb * kKT);
 #pragma unroll
-          for (int ks = 0; ks < kKT / 8; ks++)
-            mma_tf32_ts(tmem + kColO, p_tmem + (uint32_t)(ks * 8),
-                        sw128_desc(v_addr + (uint32_t)((ks >> 2) * kVtChunk + (ks & 3) * 32)),
-                        kIdescPV, (pj > 0 || ks > 0) ? 1u : 0u);
-          mma_commit(&pv_done[pst]);
-          mma_commit(&kv_empty[pst]);
+        for (int ks = 0; ks < kKT / 8; ks++) {
+          const uint64_t vd = sw128_desc(v_addr + (uint32_t)((ks >> 2) * VC + (ks & 3) * 32));
+          if (PAIR)
+            mma_tf32_ts_pair(tmem + kColO, p_tmem + (uint32_t)(ks * 8), vd, IDPV,
+                             (j > 0 || ks > 0) ? 1u : 0u);
+          else
+            mma_tf32_ts(tmem + kColO, p_tmem + (uint32_t)(ks * 8), vd, IDPV,
+                        (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        commit(&pv_done[sb]);
+        commit(&v_empty[st]);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, a.err, 2, abort_flag, a.limit_ns);
+      for (int j = 0; ok && j < kSBufs && j < T; j++) ok = issue_s(j);
+      for (int j = 0; ok && j < T; j++) {
+        ok = issue_pv(j);
+        if (ok && j + kSBufs < T) {
+          // Buffer j % 3 is free once PV_j has read P_j.
+          ok = mbar_wait_bounded(&pv_done[j % kSBufs], (j / kSBufs) & 1, a.err, 4, abort_flag,
+                                 a.limit_ns) &&
+               issue_s(j + kSBufs);
         }
       }
       // Drain: all MMAs issued by this thread have completed.
-      mma_commit(drain);
+      if (PAIR)
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                smem_u32(drain))
+            : "memory");
+      else
+        mma_commit(drain);
       mbar_wait_bounded(drain, 0, a.err, 10, nullptr, a.limit_ns);
     }
     __syncwarp();
@@ -282,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     float m = -INFINITY, l = 0.0f;  // running max (log2 domain) and sum
     bool ok = true;
     for (int j = 0; j < T; j++) {
-      const int st = j & 1;
-      ok = mbar_wait_bounded(&s_full[st], (j >> 1) & 1, a.err, 7, abort_flag, a.limit_ns);
+      const int st = j % kSBufs;  // S/P buffer
+      ok = mbar_wait_bounded(&s_full[st], (j / kSBufs) & 1, a.err, 7, abort_flag, a.limit_ns);
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
@@ -325,8 +502,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float f = need ? ex2_approx(m - mnew) : 1.0f;
         if (j > 0) {
           // O is quiescent once PV_{j-1} is done (PV_j waits for this tile's P).
-          ok = mbar_wait_bounded(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err, 8, abort_flag,
-                                 a.limit_ns);
+          ok = mbar_wait_bounded(&pv_done[(j - 1) % kSBufs], ((j - 1) / kSBufs) & 1, a.err, 8,
+                                 abort_flag, a.limit_ns);
           if (!__all_sync(0xffffffffu, ok)) {
             ok = false;
             break;
@@ -361,11 +538,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_st_32x32b_x32(lane_base + (uint32_t)(st * kKT + 32 * c), sub32(r, c));
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[st]);
+      if (PAIR) mbar_arrive_cluster(cluster_addr(&p_full[st], 0));
+      else mbar_arrive(&p_full[st]);
     }
     if (ok) {
-      ok = mbar_wait_bounded(&pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, a.err, 11, abort_flag,
-                             a.limit_ns);
+      ok = mbar_wait_bounded(&pv_done[(T - 1) % kSBufs], ((T - 1) / kSBufs) & 1, a.err, 11,
+                             abort_flag, a.limit_ns);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
@@ -404,9 +582,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // the leader's MMAs no longer read this CTA
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(kTmemCols)
+                   : "memory");
+    else
+      tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -444,15 +628,18 @@ bool attention_tc_supported(const AttnTcRequest& r) {
 
 int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
   if (!attention_tc_supported(r)) return IRO_ERR_UNSUPPORTED;
-  static bool attr_done[64] = {false};
-  if (!attr_done[c->device]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  const bool pair = !r.single_cta;
+  static bool attr_done[64][2] = {{false}};
+  if (!attr_done[c->device][pair]) {
+    cudaError_t e = pair ? cudaFuncSetAttribute(attention_tc_kernel<true>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem)
+                         : cudaFuncSetAttribute(attention_tc_kernel<false>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return map_cuda(e);
     }
-    attr_done[c->device] = true;
+    attr_done[c->device][pair] = true;
   }
   // V^T of the self tokens and of the context block.
   const int lds = vt_ld(r.S), ldc = vt_ld(r.C);
@@ -471,11 +658,14 @@ int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
   if ((st = check_launch())) return st;
   CUtensorMap mq, mk, mv, mck, mcv;
   const long long rows = (long long)r.B * r.S, crows = (long long)r.context_batch * r.C;
+  // A CTA of a pair loads half of each K tile (32 keys) and of each V^T tile
+  // (32 dimensions).
+  const int krows = pair ? kKT / 2 : kKT, vrows = pair ? kDH / 2 : kDH;
   st = map2d(&mq, r.q, r.D, rows, kQ);
-  if (!st) st = map2d(&mk, r.k, r.D, rows, kKT);
-  if (!st) st = map2d(&mv, vt, lds, (long long)r.B * r.D, kDH);
-  if (!st) st = map2d(&mck, r.ck, r.D, crows, kKT);
-  if (!st) st = map2d(&mcv, cvt, ldc, (long long)r.context_batch * r.D, kDH);
+  if (!st) st = map2d(&mk, r.k, r.D, rows, krows);
+  if (!st) st = map2d(&mv, vt, lds, (long long)r.B * r.D, vrows);
+  if (!st) st = map2d(&mck, r.ck, r.D, crows, krows);
+  if (!st) st = map2d(&mcv, cvt, ldc, (long long)r.context_batch * r.D, vrows);
   if (st) return st;
   Args a;
   a.S = r.S;
@@ -491,9 +681,30 @@ int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
   a.err = c->err;
   a.limit_ns = kWaitLimitNs;
   a.dbg = nullptr;
-  const dim3 grid(cdiv(r.S, kQ), r.heads, r.B);
-  cudaError_t e = launch_pdl(attention_tc_kernel, grid, dim3(kThreads), (size_t)kSmem, s, mq, mk,
-                             mv, mck, mcv, a);
+  cudaError_t e;
+  if (pair) {
+    // Pairs of CTAs (a two-CTA cluster) over 256 query rows.
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(2 * cdiv(r.S, 2 * kQ), r.heads, r.B);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, attention_tc_kernel<true>, mq, mk, mv, mck, mcv, a);
+  } else {
+    const dim3 grid(cdiv(r.S, kQ), r.heads, r.B);
+    e = launch_pdl(attention_tc_kernel<false>, grid, dim3(kThreads), (size_t)kSmem, s, mq, mk, mv,
+                   mck, mcv, a);
+  }
   if (e != cudaSuccess) {
     cudaGetLastError();
     return map_cuda(e);

@@ -24,6 +24,8 @@ struct AttnTcRequest {
   // (vt[((b * heads + h) * 64 + d) * attention_tc_vt_ld(S) + s], zero past S),
   // so the launch only transposes the context V.
   const float* vt_self;
+  // One CTA per 128 query rows (M = 128 MMAs) instead of CTA pairs (M = 256).
+  int single_cta;
 };
 
 // Row pitch (floats) of the V^T rows for n tokens.

@@ -289,47 +289,68 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
   const int s0 = blockIdx.x * 32, hd = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
   const int d = 2 * lane;
+  // V loads first (8 per thread), so their latency overlaps the q/k work.
+  float vv[8];
+#pragma unroll
+  for (int r = 0; r < 8; r++) {
+    const int i = t + r * 256;
+    const int ss = i / kHD, dd = i % kHD;
+    const int s = s0 + ss;
+    vv[r] = s < S ? v[((size_t)b * S + s) * D + (size_t)hd * kHD + dd] : 0.0f;
+  }
+  // q and k of this warp's four tokens, loaded together.
+  float2 qv[4], kv[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int s = min(s0 + warp * 4 + i, S - 1);
+    const size_t off = ((size_t)b * S + s) * D + hd * kHD + d;
+    qv[i] = *reinterpret_cast<const float2*>(q + off);
+    kv[i] = *reinterpret_cast<const float2*>(k + off);
+  }
   const float* qwh = qw + hd * kHD;
   const float* kwh = kw + hd * kHD;
   const float qw0 = qwh[d], qw1 = qwh[d + 1], kw0 = kwh[d], kw1 = kwh[d + 1];
+  float qms[4], kms[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    qms[i] = __fmaf_rn(qv[i].y, qv[i].y, __fmul_rn(qv[i].x, qv[i].x));
+    kms[i] = __fmaf_rn(kv[i].y, kv[i].y, __fmul_rn(kv[i].x, kv[i].x));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      qms[i] += __shfl_xor_sync(0xffffffffu, qms[i], o);
+      kms[i] += __shfl_xor_sync(0xffffffffu, kms[i], o);
+    }
+#pragma unroll
   for (int i = 0; i < 4; i++) {
     const int s = s0 + warp * 4 + i;
     if (s >= S) break;  // warp-uniform
-    const size_t row = (size_t)b * S + s;
-    float* qr = q + row * D + hd * kHD;
-    float* kr = k + row * D + hd * kHD;
-    float2 qv = *reinterpret_cast<float2*>(qr + d);
-    float2 kv = *reinterpret_cast<float2*>(kr + d);
-    float qms = __fmaf_rn(qv.y, qv.y, __fmul_rn(qv.x, qv.x));
-    float kms = __fmaf_rn(kv.y, kv.y, __fmul_rn(kv.x, kv.x));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      qms += __shfl_xor_sync(0xffffffffu, qms, o);
-      kms += __shfl_xor_sync(0xffffffffu, kms, o);
-    }
-    const float qinv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(qms, (float)kHD), eps)));
-    const float kinv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(kms, (float)kHD), eps)));
-    const float q0 = __fmul_rn(qv.x, __fmul_rn(qinv, qw0));
-    const float q1 = __fmul_rn(qv.y, __fmul_rn(qinv, qw1));
-    const float k0 = __fmul_rn(kv.x, __fmul_rn(kinv, kw0));
-    const float k1 = __fmul_rn(kv.y, __fmul_rn(kinv, kw1));
+    const float qinv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(qms[i], (float)kHD), eps)));
+    const float kinv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(kms[i], (float)kHD), eps)));
+    const float q0 = __fmul_rn(qv[i].x, __fmul_rn(qinv, qw0));
+    const float q1 = __fmul_rn(qv[i].y, __fmul_rn(qinv, qw1));
+    const float k0 = __fmul_rn(kv[i].x, __fmul_rn(kinv, kw0));
+    const float k1 = __fmul_rn(kv[i].y, __fmul_rn(kinv, kw1));
+    const size_t off = ((size_t)b * S + s) * D + hd * kHD + d;
     if (hd >= heads / 2) {
-      *reinterpret_cast<float2*>(qr + d) = make_float2(q0, q1);
-      *reinterpret_cast<float2*>(kr + d) = make_float2(k0, k1);
+      *reinterpret_cast<float2*>(q + off) = make_float2(q0, q1);
+      *reinterpret_cast<float2*>(k + off) = make_float2(k0, k1);
     } else {
       const float c = rcos[(size_t)s * (kHD / 2) + lane], sn = rsin[(size_t)s * (kHD / 2) + lane];
-      *reinterpret_cast<float2*>(qr + d) =
+      *reinterpret_cast<float2*>(q + off) =
           make_float2(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, sn)),
                       __fadd_rn(__fmul_rn(q0, sn), __fmul_rn(q1, c)));
-      *reinterpret_cast<float2*>(kr + d) =
+      *reinterpret_cast<float2*>(k + off) =
           make_float2(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, sn)),
                       __fadd_rn(__fmul_rn(k0, sn), __fmul_rn(k1, c)));
     }
   }
-  for (int i = t; i < 32 * kHD; i += 256) {
-    const int ss = i / kHD, dd = i % kHD;
-    const int s = s0 + ss;
-    tile[dd][ss] = s < S ? v[((size_t)b * S + s) * D + (size_t)hd * kHD + dd] : 0.0f;
+#pragma unroll
+  for (int r = 0; r < 8; r++) {
+    const int i = t + r * 256;
+    tile[i % kHD][i / kHD] = vv[r];
   }
   __syncthreads();
   for (int i = t; i < 32 * kHD; i += 256) {
@@ -485,11 +506,16 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(AttnArgs a) {
 size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
 // IRO_DIT_ATTENTION=simt selects the fp32 CUDA-core attention kernel above
-// (exact fp32 products) instead of the tensor-core one; it also serves
-// requests the tensor-core kernel does not take (unaligned context buffers).
+// (exact fp32 products) instead of the tensor-core one, =pair the
+// tensor-core kernel on CTA pairs (M = 256 MMAs; at config 3 it measured
+// 423 us per layer against 351 for one CTA per 128 queries); the CUDA-core
+// kernel also serves requests the tensor-core one does not take (unaligned
+// context buffers).
 int attention_mode() {
   const char* e = getenv("IRO_DIT_ATTENTION");
-  return (e && strcmp(e, "simt") == 0) ? 1 : 0;
+  if (e && strcmp(e, "simt") == 0) return 1;
+  if (e && strcmp(e, "pair") == 0) return 2;  // CTA pairs, M = 256 MMAs
+  return 0;
 }
 
 }  // namespace
@@ -653,8 +679,8 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       r.outs[3] = g;
       if ((st = gemm_launch(c, r, s))) return st;
       AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
-                       sw_ws, nullptr};
-      if (attention_mode() == 0 && attention_tc_supported(ar)) {
+                       sw_ws, nullptr, attention_mode() == 2 ? 0 : 1};
+      if (attention_mode() != 1 && attention_tc_supported(ar)) {
         // Head norm + RoPE with the self V^T rows the attention kernel reads.
         float* vt = static_cast<float*>(sw_ws);
         const int ld = attention_tc_vt_ld(S);
