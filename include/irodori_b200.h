@@ -334,8 +334,10 @@ int iro_int8_codec_conv1_dev(const float *hidden, int rows, const IroInt8DevWeig
    shift_bias [D], scale_down, scale_up, scale_bias, gate_down, gate_up,
    gate_bias}; q_norm, k_norm [D].  qkvg is wq|wk|wv|gate concatenated
    (iro_int8_dev_weight_concat), w13 the gated pair of w1, w3.
-   residual_mask follows IRO_INT8_RESIDUAL (dit.c:429-436; 8 = two-term W2,
-   the reference default); other bits are IRO_ERR_UNSUPPORTED. */
+   residual_mask follows IRO_INT8_RESIDUAL (dit.c:429-436): the groups whose
+   activations are quantised with a second residual term, 1 = Q/K/V/gate,
+   2 = Wo, 4 = W1/W3, 8 = W2 (the reference default), any combination; other
+   bits are IRO_ERR_INVALID. */
 typedef struct {
     const float *adaln[2][9];
     const float *q_norm;
@@ -345,6 +347,23 @@ typedef struct {
     float norm_eps;
     int residual_mask;
 } IroDiTBlockDev;
+
+/* The reference's int8 policy switches, read from the same environment
+   variables with the same parsing (strtol base 0, masked to 4 bits) and
+   defaults, for engines that configure the device path as the reference's
+   own code would (read on every call, not cached):
+     IRO_INT8_RESIDUAL               dit.c:429-436, default 8 (W2)
+     IRO_CODEC_INT8_MASK             dacvae.c:43-50, default 15
+     IRO_CODEC_INT8_RESIDUAL         dacvae.c:52-60, default 4|8 (Conv7 + Conv1)
+     IRO_CODEC_INT8_RESIDUAL_STAGES  dacvae.c:63-71, default 8 (last stage)
+   iro_policy_codec_residual(stage, group) is the reference's per-layer
+   decision: the group's residual bit and, for the residual-unit convolutions
+   (groups 4 and 8), the stage's bit. */
+int iro_policy_dit_residual_mask(void);
+int iro_policy_codec_int8_mask(void);
+int iro_policy_codec_residual_mask(void);
+int iro_policy_codec_residual_stages(void);
+int iro_policy_codec_residual(int stage, int group);
 
 /* dit.c:644-705: RoPE cos/sin tables [S, head_dim/2] as the reference builds
    them (double-precision rotation recurrence, rounded to float); host

@@ -735,10 +735,37 @@ int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
 
 namespace iro {
 
+// silu(w1) * w3 from the W1|W3 pair-block layout (pair W1 columns, then the
+// matching pair W3 columns): the reference's iro_silu_mul_inplace
+// (ops.c:781-784), x / (1 + expf(-x)) * gate.
+__global__ void silu_mul_pairs_kernel(const float* __restrict__ o13, int ld, int pair, int M,
+                                      int H, float* __restrict__ hid) {
+  const long long n = (long long)M * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / H;
+    const int h = (int)(i - m * H);
+    const int blk = h / pair, j = h - blk * pair;
+    const float* row = o13 + (size_t)m * ld + (size_t)blk * 2 * pair;
+    const float a = row[j], g = row[pair + j];
+    hid[i] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), g);
+  }
+}
+
+size_t swiglu_workspace_bytes_ex(int M, int D, int H, int residual_w2, int residual_w13) {
+  size_t t = iro_int8_swiglu_workspace_bytes(M, D, H, residual_w2);
+  if (t == 0 || !residual_w13) return t;
+  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+  return t + al((size_t)M * round_up(D, 16)) + 2 * al(sizeof(float) * M) +
+         al(sizeof(float) * (size_t)M * 2 * round_up(H, 128));
+}
+
 int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
                const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2,
                void* workspace, cudaStream_t s, const float* rgate, int rgate_rows,
-               const uint8_t* qx_in, const float* sx_in, const int32_t* zx_in) {
+               const uint8_t* qx_in, const float* sx_in, const int32_t* zx_in,
+               int residual_w13) {
+  if (residual_w13 && !x) return IRO_ERR_INVALID;
   if ((!x && !(qx_in && sx_in && zx_in)) || !out || !w13 || !w2 ||
       w13->layout != IRO_LAYOUT_GATED_PAIR ||
       w2->layout != IRO_LAYOUT_PLAIN || w2->K != w13->hidden || M < 0)
@@ -748,7 +775,7 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
   if (D % 16 != 0 || H % 16 != 0) return IRO_ERR_UNSUPPORTED;
   if (M == 0) return IRO_OK;
   int st;
-  const size_t need = iro_int8_swiglu_workspace_bytes(M, D, H, residual_w2);
+  const size_t need = swiglu_workspace_bytes_ex(M, D, H, residual_w2, residual_w13);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (!ws) {
     ws = static_cast<uint8_t*>(arena_get(c, need, &st));
@@ -776,7 +803,8 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
     sh2 = reinterpret_cast<float*>(take(sizeof(float) * M));
     zh2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
   }
-  if (!rgate && !qx_in && swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
+  if (!rgate && !qx_in && !residual_w13 &&
+      swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
     SwigluBuffers b;
     b.qx = qx;
     b.sx = sx;
@@ -790,6 +818,42 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
     b.ctr = reinterpret_cast<int*>(ws + off);
     return swiglu_fused_launch(c, x, M, w13, w2, b2 ? b2 : w2->bias, out, b, s);
   }
+  if (residual_w13) {
+    // Two-term W1/W3: both activation terms through the pair-block weight
+    // as one two-term linear (y = lin(q1) + lin(q2), dit.c:479-486), then
+    // the gate.  The extra buffers follow the single-term workspace.
+    const size_t base = iro_int8_swiglu_workspace_bytes(M, D, H, residual_w2);
+    size_t off2 = base;
+    auto take2 = [&](size_t bytes) {
+      uint8_t* p = ws + off2;
+      off2 += al(bytes);
+      return p;
+    };
+    uint8_t* qx2 = take2((size_t)M * D);
+    float* sx2 = reinterpret_cast<float*>(take2(sizeof(float) * M));
+    int32_t* zx2 = reinterpret_cast<int32_t*>(take2(sizeof(float) * M));
+    float* o13 = reinterpret_cast<float*>(take2(sizeof(float) * (size_t)M * w13->N));
+    st = quantize_rows_residual_launch(x, M, D, qx, sx, zx, nullptr, qx2, sx2, zx2, s);
+    if (st) return st;
+    GemmRequest r13;
+    r13.epi = EPI_DUAL;
+    r13.M = M;
+    r13.a = qx;
+    r13.lda = D;
+    r13.sx = sx;
+    r13.zp = zx;
+    r13.a2 = qx2;
+    r13.sx2 = sx2;
+    r13.zp2 = zx2;
+    r13.w = w13;
+    r13.y = o13;
+    r13.ldy = w13->N;
+    if ((st = gemm_launch(c, r13, s))) return st;
+    const long long n = (long long)M * H;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, (long long)c->num_sms * 16);
+    silu_mul_pairs_kernel<<<blocks, 256, 0, s>>>(o13, w13->N, w13->pair, M, H, hid);
+    if ((st = check_launch())) return st;
+  } else {
   if (qx_in) {
     qx = const_cast<uint8_t*>(qx_in);
     sx = const_cast<float*>(sx_in);
@@ -810,6 +874,7 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
   g.ldh = H;
   st = gemm_launch(c, g, s);
   if (st) return st;
+  }
   if (residual_w2)
     st = quantize_rows_residual_launch(hid, M, H, qh, sh, zh, nullptr, qh2, sh2, zh2, s);
   else

@@ -583,12 +583,13 @@ size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int 
   const size_t M = (size_t)B * S, D = (size_t)blk->model_dim;
   size_t t = 0;
   t += 6 * al256(sizeof(float) * M * D);                           // h, q, k, v, g, mix
-  t += al256(M * D) + 2 * al256(sizeof(float) * M);                // codes + row params
+  t += 2 * (al256(M * D) + 2 * al256(sizeof(float) * M));          // codes (two terms) + row params
   t += al256(sizeof(int) * (size_t)B * C) + al256(sizeof(int) * B);
   // The SwiGLU scratch is only live in the MLP half, the V^T copies only in
   // the attention half: they share the tail of the workspace.
-  return t + std::max(iro_int8_swiglu_workspace_bytes((int)M, blk->model_dim, blk->mlp_dim,
-                                                      (blk->residual_mask & 8) != 0),
+  return t + std::max(swiglu_workspace_bytes_ex((int)M, blk->model_dim, blk->mlp_dim,
+                                                (blk->residual_mask & 8) != 0,
+                                                (blk->residual_mask & 4) != 0),
                       attention_tc_workspace_bytes(B, S, C, context_batch, blk->model_dim));
 }
 
@@ -603,9 +604,9 @@ int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, co
   if (blk->head_dim != kHD || NH * kHD != D || R <= 0 || H <= 0 || D % 16 != 0 ||
       (reinterpret_cast<uintptr_t>(x) & 15u) != 0)
     return IRO_ERR_UNSUPPORTED;
-  // Residual (two-term) policy: the reference's default, W2 only (dit.c:
-  // 429-436), or none; the QKVG, Wo and W1/W3 two-term forms are not built.
-  if ((blk->residual_mask & ~8) != 0) return IRO_ERR_UNSUPPORTED;
+  // Two-term activation policy: any combination of the four groups
+  // (dit.c:429-436); the reference's default is W2 only (8).
+  if ((blk->residual_mask & ~15) != 0) return IRO_ERR_INVALID;
   if (blk->qkvg.N != 4 * D || blk->qkvg.K != D || blk->wo.N != D || blk->wo.K != D ||
       blk->w13.layout != IRO_LAYOUT_GATED_PAIR || blk->w13.K != D || blk->w13.hidden != H ||
       blk->w2.N != D || blk->w2.K != H)
@@ -637,10 +638,18 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
   uint8_t* codes = take(M * D);
   float* rs = reinterpret_cast<float*>(take(sizeof(float) * M));
   int32_t* rz = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
+  // Second activation term of the two-term QKVG / Wo policies.
+  uint8_t* codes2 = take(M * D);
+  float* rs2 = reinterpret_cast<float*>(take(sizeof(float) * M));
+  int32_t* rz2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
   int* clist = reinterpret_cast<int*>(take(sizeof(int) * (size_t)B * C));
   int* ccount = reinterpret_cast<int*>(take(sizeof(int) * B));
   void* sw_ws = ws + off;
   int st;
+  // Two-term activation policy per projection group (dit.c:429-436,
+  // IRO_INT8_RESIDUAL bits: 1 QKVG, 2 Wo, 4 W1/W3, 8 W2).
+  const bool res_qkvg = (blk->residual_mask & 1) != 0, res_wo = (blk->residual_mask & 2) != 0;
+  const bool res_w13 = (blk->residual_mask & 4) != 0, res_w2 = (blk->residual_mask & 8) != 0;
 
   const int prow = B / cond_rows;  // batch rows per AdaLN parameter row
   for (int half = 0; half < 2; half++) {
@@ -648,27 +657,40 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
     const float* scale = ada[half * 3 + 1];
     const float* gate = ada[half * 3 + 2];
     // AdaLN apply and the row quantiser of its consumer (QKVG, or W1/W3 of
-    // the SwiGLU) in one pass; h is only materialised for shapes the fused
-    // kernel does not take.
-    st = adaln_quant_launch(x, (int)M, S, D, blk->norm_eps, prow, shift, scale, codes, rs, rz, s);
+    // the SwiGLU) in one pass; h is materialised for the two-term policies
+    // and for shapes the fused kernel does not take.
+    const bool two_term = half == 0 ? res_qkvg : res_w13;
+    st = two_term ? (int)IRO_ERR_UNSUPPORTED
+                  : adaln_quant_launch(x, (int)M, S, D, blk->norm_eps, prow, shift, scale, codes,
+                                       rs, rz, s);
     const bool fused = st == IRO_OK;
     if (st == IRO_ERR_UNSUPPORTED) {
       adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
                                                          shift, scale, h);
       if ((st = check_launch())) return st;
-      if ((st = quantize_rows_launch(h, (int)M, D, codes, rs, rz, 0, s))) return st;
+      if (half == 0 && res_qkvg)
+        st = quantize_rows_residual_launch(h, (int)M, D, codes, rs, rz, nullptr, codes2, rs2,
+                                           rz2, s);
+      else if (!(half == 1 && res_w13))
+        st = quantize_rows_launch(h, (int)M, D, codes, rs, rz, 0, s);
+      if (st) return st;
     } else if (st) {
       return st;
     }
     if (half == 0) {
       // QKVG on one quantised copy of h (dit.c:785-792).
       GemmRequest r;
-      r.epi = EPI_SPLIT;
+      r.epi = res_qkvg ? EPI_DUAL : EPI_SPLIT;
       r.M = (int)M;
       r.a = codes;
       r.lda = D;
       r.sx = rs;
       r.zp = rz;
+      if (res_qkvg) {
+        r.a2 = codes2;
+        r.sx2 = rs2;
+        r.zp2 = rz2;
+      }
       r.w = &blk->qkvg;
       r.bias = nullptr;
       r.nout = 4;
@@ -701,15 +723,22 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       }
       // Wo on the quantised gated mix (dit.c:876-884), with the gated
       // residual x += gate * Wo(mix) (dit.c:1013-1020) in its epilogue.
-      st = quantize_rows_launch(mix, (int)M, D, codes, rs, rz, 0, s);
+      st = res_wo ? quantize_rows_residual_launch(mix, (int)M, D, codes, rs, rz, nullptr, codes2,
+                                                  rs2, rz2, s)
+                  : quantize_rows_launch(mix, (int)M, D, codes, rs, rz, 0, s);
       if (st) return st;
       GemmRequest o;
-      o.epi = EPI_LINEAR;
+      o.epi = res_wo ? EPI_DUAL : EPI_LINEAR;
       o.M = (int)M;
       o.a = codes;
       o.lda = D;
       o.sx = rs;
       o.zp = rz;
+      if (res_wo) {
+        o.a2 = codes2;
+        o.sx2 = rs2;
+        o.zp2 = rz2;
+      }
       o.w = &blk->wo;
       o.y = x;
       o.ldy = D;
@@ -718,8 +747,12 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       if ((st = gemm_launch(c, o, s))) return st;
     } else {
       // SwiGLU (dit.c:913-969), x += gate * W2(...) in the W2 epilogue.
-      st = swiglu_run(c, fused ? nullptr : h, (int)M, &blk->w13, &blk->w2, nullptr, x,
-                      (blk->residual_mask & 8) != 0, sw_ws, s, gate, S * prow, codes, rs, rz);
+      if (res_w13)
+        st = swiglu_run(c, h, (int)M, &blk->w13, &blk->w2, nullptr, x, res_w2, sw_ws, s, gate,
+                        S * prow, nullptr, nullptr, nullptr, 1);
+      else
+        st = swiglu_run(c, fused ? nullptr : h, (int)M, &blk->w13, &blk->w2, nullptr, x, res_w2,
+                        sw_ws, s, gate, S * prow, codes, rs, rz);
       if (st) return st;
     }
   }

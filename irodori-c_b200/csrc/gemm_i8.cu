@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           int g = 0, col0 = n0, ncols = p.N, ld = p.ldy;
           float* base = p.y;
-          if (EPI == EPI_SPLIT) {
+          if (EPI == EPI_SPLIT || (EPI == EPI_DUAL && p.seg > 0)) {
             g = n0 / p.seg;
             col0 = n0 - g * p.seg;
             ncols = p.seg;
@@ -539,7 +539,7 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
     if (tma)
       st = make_tmap_f32_sw128(&om.m[0], r.hidden, (uint64_t)w->hidden, (uint64_t)r.M,
                                (uint64_t)r.ldh * 4);
-  } else if (EPI == EPI_SPLIT) {
+  } else if (EPI == EPI_SPLIT || (EPI == EPI_DUAL && r.nout > 0)) {
     for (int i = 0; i < r.nout && tma; i++) tma = out_tma_ok(r.outs[i], r.seg);
     for (int i = 0; tma && i < r.nout && st == IRO_OK; i++)
       st = make_tmap_f32_sw128(&om.m[i], r.outs[i], (uint64_t)r.seg, (uint64_t)r.M,
@@ -665,7 +665,18 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       if (w->pair == 64) return launch_t<128, EPI_GATED>(c, r, p, s);
       return IRO_ERR_UNSUPPORTED;
     case EPI_DUAL: {
-      if (!r.a2 || !r.sx2 || !r.zp2 || !r.y) return IRO_ERR_INVALID;
+      // With nout > 0 the columns go to nout buffers of `seg` columns each
+      // (the QKVG split, for the two-term QKVG policy); y is then unused.
+      if (!r.a2 || !r.sx2 || !r.zp2) return IRO_ERR_INVALID;
+      if (r.nout > 0) {
+        if (r.nout > 4 || r.seg <= 0 || r.seg % 128 != 0 || r.seg * r.nout != w->N ||
+            r.accumulate || r.rgate)
+          return IRO_ERR_UNSUPPORTED;
+        for (int i = 0; i < r.nout; i++)
+          if (!r.outs[i]) return IRO_ERR_INVALID;
+      } else if (!r.y) {
+        return IRO_ERR_INVALID;
+      }
       const int bn = r.force_bn ? r.force_bn : pick_bn(r.M, w->N, c->num_sms, 1);
       if (bn == 128) return launch_t<128, EPI_DUAL>(c, r, p, s);
       return launch_t<64, EPI_DUAL>(c, r, p, s);

@@ -52,11 +52,18 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
 // holds the residual stream), out = swiglu(x) otherwise.  With qx set, x is
 // already quantised (codes qx [M, K], row scale sx and zero point zx) and
 // x itself is not read.
+// residual_w13: the two-term activation path for W1/W3 too (dit.c:923-947
+// with IRO_INT8_RESIDUAL bit 4): x quantised with its residual term, both
+// terms through W1|W3, then silu(w1) * w3; needs x (not qx).
 int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
                const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2,
                void* workspace, cudaStream_t s, const float* rgate, int rgate_rows,
                const uint8_t* qx = nullptr, const float* sx = nullptr,
-               const int32_t* zx = nullptr);
+               const int32_t* zx = nullptr, int residual_w13 = 0);
+
+// Workspace of swiglu_run (iro_int8_swiglu_workspace_bytes plus the two-term
+// W1/W3 buffers when residual_w13 is set).
+size_t swiglu_workspace_bytes_ex(int M, int D, int H, int residual_w2, int residual_w13);
 
 // Split-K over a two-CTA cluster for plain linears with few, long tiles
 // (gemm_splitk.cu); gemm_launch picks it when eligible and IRO_GEMM_SPLITK=1.

@@ -134,6 +134,11 @@ SIGNATURES = {
     "iro_dit_euler_step_dev": (_i, [_vp, _vp, _i, _i, _i, C.c_float, C.c_float, _vp, _vp, _vp,
                                     _vp, _i, _vp, _vp]),
     "iro_dit_stage_workspace_bytes": (_sz, [_vp, _i]),
+    "iro_policy_dit_residual_mask": (_i, []),
+    "iro_policy_codec_int8_mask": (_i, []),
+    "iro_policy_codec_residual_mask": (_i, []),
+    "iro_policy_codec_residual_stages": (_i, []),
+    "iro_policy_codec_residual": (_i, [_i, _i]),
     "iro_dit_sample_workspace_bytes": (_sz, [_vp, _i, _i, _i, _i, _i]),
     "iro_dit_condition_dev": (_i, [_vp, _vp, _i, _vp, _vp, _vp]),
     "iro_dit_input_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),

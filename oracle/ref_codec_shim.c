@@ -89,3 +89,11 @@ int ref_convtranspose1d_output_length(int input_length, int kernel,
 int ref_codec_upsample_residual(void) {
     return (codec_int8_residual_mask() & IRO_CODEC_GROUP_UPSAMPLE) != 0;
 }
+
+/* The reference codec's int8 policy switches as it reads them
+   (dacvae.c:43-71); cached per process by the reference. */
+void ref_codec_policy(int *mask, int *residual, int *stages) {
+    *mask = codec_int8_mask();
+    *residual = codec_int8_residual_mask();
+    *stages = codec_int8_residual_stages();
+}

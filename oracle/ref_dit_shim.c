@@ -120,3 +120,7 @@ int ref_dit_output_w(const float *out_norm, const float *out_w, const float *out
     free(d);
     return rc;
 }
+
+/* The reference's residual-policy switch as it reads it (dit.c:429-436);
+   cached per process by the reference. */
+int ref_dit_residual_mask(void) { return dit_int8_residual_mask(); }

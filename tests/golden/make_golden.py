@@ -180,6 +180,38 @@ def dit_block_child():
     np.savez(os.path.join(HERE, "_tmp_dit_block.npz"), **res)
 
 
+DIT_BLOCK_RESID_CASES = [(31, 2, 40, 12, 1, 7), (32, 1, 70, 9, 1, 15), (33, 2, 36, 20, 2, 2)]
+# seed, B, S, C, context_batch, IRO_INT8_RESIDUAL
+
+
+def dit_block_resid_child(idx):
+    """Child process with IRO_INT8_RESIDUAL set for one case (the reference
+    reads it once per process)."""
+    seed, B, S, C, cb, mask = DIT_BLOCK_RESID_CASES[idx]
+    x, cond, ck, cv, mask_, adaln, qn, kn, ws = inputs.dit_block_case(seed, B, S, C, cb)
+    W = [oracle.ref_weight_quantize(w) for w in ws]
+    out = oracle.ref_dit_block(x, cond, ck, cv, mask_, cb, B, S, C, adaln, qn, kn, W)
+    np.savez(os.path.join(HERE, f"_tmp_dit_block_resid_{idx}.npz"), out=out,
+             case=np.array([seed, B, S, C, cb, mask], np.int32),
+             inputs_sha=np.frombuffer(inputs.sha(x, cond, ck, cv, mask_, *adaln, qn, kn, *ws),
+                                      np.uint8))
+
+
+def dit_block_resid():
+    res = {}
+    for i, case in enumerate(DIT_BLOCK_RESID_CASES):
+        e = dict(os.environ)
+        e["IRO_INT8_RESIDUAL"] = str(case[5])
+        subprocess.run([sys.executable, __file__, "--dit-block-resid-child", str(i)], check=True,
+                       env=e)
+        path = os.path.join(HERE, f"_tmp_dit_block_resid_{i}.npz")
+        g = dict(np.load(path))
+        os.remove(path)
+        for k, v in g.items():
+            res[f"c{i}_{k}"] = v
+    return res
+
+
 def dit_block():
     e = dict(os.environ)
     e.pop("IRO_INT8_RESIDUAL", None)
@@ -226,6 +258,9 @@ def dit_step():
 
 
 def main():
+    if len(sys.argv) > 2 and sys.argv[1] == "--dit-block-resid-child":
+        dit_block_resid_child(int(sys.argv[2]))
+        return
     if len(sys.argv) > 2 and sys.argv[1] == "--dit-step-child":
         dit_step_child()
         return
@@ -242,7 +277,7 @@ def main():
     for name, fn in (("int8_ops", int8_ops), ("residual", residual), ("conv7", conv7),
                      ("sym_quant", sym), ("dit_swiglu", dit_swiglu), ("convt", convt),
                      ("conv1", conv1), ("dit_block", dit_block),
-                     ("dit_step", dit_step)):
+                     ("dit_step", dit_step), ("dit_block_resid", dit_block_resid)):
         if only and name not in only:
             continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())
