@@ -365,6 +365,22 @@ int iro_policy_codec_residual_mask(void);
 int iro_policy_codec_residual_stages(void);
 int iro_policy_codec_residual(int stage, int group);
 
+/* Activation diagnostics (dit.c:340-412), recorded by the sampler entry
+   points (iro_dit_euler_step_dev, iro_dit_sample_euler_dev: layer index known)
+   at the reference's four points, group 0 Q/K/V/gate input, 1 Wo input, 2
+   W1/W3 input, 3 W2 input, when IRO_INT8_STATS is set (not "0"):
+   per (layer, group) the row count, the sum over rows of max|x| / rms(x) and
+   the histogram of each row's first max-|x| channel (8192 channels).
+   IRO_INT8_DUMP=dir writes the first three activations per (layer, group) to
+   dir/act_L%02d_G%d_%d_M%d_K%d.f32 as the reference does.  Recording takes the
+   unfused AdaLN path (h is materialised) and costs a pass per record.
+   iro_dit_stats_report prints the reference's summary line per cell to
+   stderr (also at process exit once recording has started). */
+int iro_dit_stats_read(int layer, int group, double *rows, double *ratio_sum,
+                       unsigned int *hist, int hist_len);
+void iro_dit_stats_reset(void);
+void iro_dit_stats_report(void);
+
 /* dit.c:644-705: RoPE cos/sin tables [S, head_dim/2] as the reference builds
    them (double-precision rotation recurrence, rounded to float); host
    buffers. */

@@ -10,6 +10,7 @@
 
 #include <vector>
 
+#include "diag.cuh"
 #include "gemm_i8.cuh"
 #include "swiglu_fused.cuh"
 #include "quantize.cuh"
@@ -764,7 +765,7 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
                const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2,
                void* workspace, cudaStream_t s, const float* rgate, int rgate_rows,
                const uint8_t* qx_in, const float* sx_in, const int32_t* zx_in,
-               int residual_w13) {
+               int residual_w13, int stats_layer) {
   if (residual_w13 && !x) return IRO_ERR_INVALID;
   if ((!x && !(qx_in && sx_in && zx_in)) || !out || !w13 || !w2 ||
       w13->layout != IRO_LAYOUT_GATED_PAIR ||
@@ -803,7 +804,7 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
     sh2 = reinterpret_cast<float*>(take(sizeof(float) * M));
     zh2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
   }
-  if (!rgate && !qx_in && !residual_w13 &&
+  if (!rgate && !qx_in && !residual_w13 && stats_layer < 0 &&
       swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
     SwigluBuffers b;
     b.qx = qx;
@@ -875,6 +876,8 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
   st = gemm_launch(c, g, s);
   if (st) return st;
   }
+  // W2 input diagnostics (dit.c:964).
+  if (stats_layer >= 0 && (st = diag_record(stats_layer, 3, hid, M, H, s))) return st;
   if (residual_w2)
     st = quantize_rows_residual_launch(hid, M, H, qh, sh, zh, nullptr, qh2, sh2, zh2, s);
   else

@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "diag.cuh"
 #include "dit_attention.cuh"
 #include "dit_block.cuh"
 #include "gemm_i8.cuh"
@@ -619,7 +620,8 @@ int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, co
 int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* const* ada,
                   int cond_rows, const float* ctx_k, const float* ctx_v,
                   const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
-                  const float* rcos, const float* rsin, void* workspace, cudaStream_t s) {
+                  const float* rcos, const float* rsin, void* workspace, cudaStream_t s,
+                  int stats_layer) {
   const int D = blk->model_dim, NH = blk->heads;
   const size_t M = (size_t)B * S;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -650,6 +652,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
   // IRO_INT8_RESIDUAL bits: 1 QKVG, 2 Wo, 4 W1/W3, 8 W2).
   const bool res_qkvg = (blk->residual_mask & 1) != 0, res_wo = (blk->residual_mask & 2) != 0;
   const bool res_w13 = (blk->residual_mask & 4) != 0, res_w2 = (blk->residual_mask & 8) != 0;
+  const int diag_layer = (stats_layer >= 0 && diag_enabled()) ? stats_layer : -1;
 
   const int prow = B / cond_rows;  // batch rows per AdaLN parameter row
   for (int half = 0; half < 2; half++) {
@@ -660,7 +663,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
     // the SwiGLU) in one pass; h is materialised for the two-term policies
     // and for shapes the fused kernel does not take.
     const bool two_term = half == 0 ? res_qkvg : res_w13;
-    st = two_term ? (int)IRO_ERR_UNSUPPORTED
+    st = (two_term || diag_layer >= 0) ? (int)IRO_ERR_UNSUPPORTED
                   : adaln_quant_launch(x, (int)M, S, D, blk->norm_eps, prow, shift, scale, codes,
                                        rs, rz, s);
     const bool fused = st == IRO_OK;
@@ -668,6 +671,9 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
                                                          shift, scale, h);
       if ((st = check_launch())) return st;
+      // Q/K/V/gate or W1/W3 input diagnostics (dit.c:787, 944).
+      if (diag_layer >= 0 && (st = diag_record(diag_layer, half == 0 ? 0 : 2, h, (int)M, D, s)))
+        return st;
       if (half == 0 && res_qkvg)
         st = quantize_rows_residual_launch(h, (int)M, D, codes, rs, rz, nullptr, codes2, rs2,
                                            rz2, s);
@@ -723,6 +729,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       }
       // Wo on the quantised gated mix (dit.c:876-884), with the gated
       // residual x += gate * Wo(mix) (dit.c:1013-1020) in its epilogue.
+      if (diag_layer >= 0 && (st = diag_record(diag_layer, 1, mix, (int)M, D, s))) return st;
       st = res_wo ? quantize_rows_residual_launch(mix, (int)M, D, codes, rs, rz, nullptr, codes2,
                                                   rs2, rz2, s)
                   : quantize_rows_launch(mix, (int)M, D, codes, rs, rz, 0, s);
@@ -749,10 +756,10 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       // SwiGLU (dit.c:913-969), x += gate * W2(...) in the W2 epilogue.
       if (res_w13)
         st = swiglu_run(c, h, (int)M, &blk->w13, &blk->w2, nullptr, x, res_w2, sw_ws, s, gate,
-                        S * prow, nullptr, nullptr, nullptr, 1);
+                        S * prow, nullptr, nullptr, nullptr, 1, diag_layer);
       else
         st = swiglu_run(c, fused ? nullptr : h, (int)M, &blk->w13, &blk->w2, nullptr, x, res_w2,
-                        sw_ws, s, gate, S * prow, codes, rs, rz);
+                        sw_ws, s, gate, S * prow, codes, rs, rz, 0, diag_layer);
       if (st) return st;
     }
   }

@@ -29,6 +29,7 @@ size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int 
 int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* const* ada,
                   int cond_rows, const float* ctx_k, const float* ctx_v,
                   const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
-                  const float* rcos, const float* rsin, void* workspace, cudaStream_t s);
+                  const float* rcos, const float* rsin, void* workspace, cudaStream_t s,
+                  int stats_layer = -1);
 
 }  // namespace iro

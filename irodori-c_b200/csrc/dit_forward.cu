@@ -441,7 +441,7 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
     for (int i = 0; i < 6; i++)
       ada[i] = cb.params + (((size_t)(2 * l) * 3 + i) * cb.n + row) * D;
     st = dit_block_run(c, &m->block[l], x, ada, 1, ctx_k[l], ctx_v[l], mask, R, B, S, C, tb.rcos,
-                       tb.rsin, blk_ws, s);
+                       tb.rsin, blk_ws, s, l);
     if (st) return st;
   }
   // Output head (normalised in place: x is rebuilt from the state next

@@ -59,7 +59,7 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
                const IroInt8DevWeight* w2, const float* b2, float* out, int residual_w2,
                void* workspace, cudaStream_t s, const float* rgate, int rgate_rows,
                const uint8_t* qx = nullptr, const float* sx = nullptr,
-               const int32_t* zx = nullptr, int residual_w13 = 0);
+               const int32_t* zx = nullptr, int residual_w13 = 0, int stats_layer = -1);
 
 // Workspace of swiglu_run (iro_int8_swiglu_workspace_bytes plus the two-term
 // W1/W3 buffers when residual_w13 is set).

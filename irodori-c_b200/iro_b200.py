@@ -135,6 +135,9 @@ SIGNATURES = {
                                     _vp, _i, _vp, _vp]),
     "iro_dit_stage_workspace_bytes": (_sz, [_vp, _i]),
     "iro_policy_dit_residual_mask": (_i, []),
+    "iro_dit_stats_read": (_i, [_i, _i, C.POINTER(C.c_double), C.POINTER(C.c_double), _vp, _i]),
+    "iro_dit_stats_reset": (None, []),
+    "iro_dit_stats_report": (None, []),
     "iro_policy_codec_int8_mask": (_i, []),
     "iro_policy_codec_residual_mask": (_i, []),
     "iro_policy_codec_residual_stages": (_i, []),
@@ -690,6 +693,28 @@ class DiTModel:
         if steps is None:
             return lib().iro_dit_step_workspace_bytes(C.byref(self.st), R, cfg, S, n_ctx)
         return lib().iro_dit_sample_workspace_bytes(C.byref(self.st), R, cfg, S, n_ctx, steps)
+
+
+DIT_STAT_GROUPS = ("qkvg", "wo", "w13", "w2")
+
+
+def dit_stats(layer, group, channels=8192):
+    """IRO_INT8_STATS cell of (layer, group): rows, sum of max|x|/rms(x) over
+    rows, and the histogram of each row's first max-|x| channel (dit.c:340-400)."""
+    rows, ratio = C.c_double(), C.c_double()
+    hist = np.zeros(channels, np.uint32)
+    check(lib().iro_dit_stats_read(layer, group, C.byref(rows), C.byref(ratio), _p(hist),
+                                   channels), "iro_dit_stats_read")
+    return rows.value, ratio.value, hist
+
+
+def dit_stats_reset():
+    lib().iro_dit_stats_reset()
+
+
+def dit_stats_report():
+    """Print the reference's int8-stats summary lines to stderr."""
+    lib().iro_dit_stats_report()
 
 
 class StFile:
