@@ -361,6 +361,18 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
   }
 }
 
+// RoPE tables [S][32] -> pair-major [32][S] (cos block, then sin block), the
+// layout the QKVG epilogue reads (EPI_QKV).
+__global__ void rope_pair_major_kernel(const float* __restrict__ rcos,
+                                       const float* __restrict__ rsin, int S,
+                                       float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= S * 32) return;
+  const int tok = i >> 5, pair = i & 31;
+  out[(size_t)pair * S + tok] = rcos[i];
+  out[(size_t)(32 + pair) * S + tok] = rsin[i];
+}
+
 // Valid context positions per batch row (dit.c:811-813, 828-839); the mask
 // is [B, C] even when the context K/V are shared by the batch.
 __global__ void context_list_kernel(const uint8_t* __restrict__ mask, int rows, int C,
@@ -586,6 +598,7 @@ size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int 
   t += 6 * al256(sizeof(float) * M * D);                           // h, q, k, v, g, mix
   t += 2 * (al256(M * D) + 2 * al256(sizeof(float) * M));          // codes (two terms) + row params
   t += al256(sizeof(int) * (size_t)B * C) + al256(sizeof(int) * B);
+  t += al256(sizeof(float) * 2 * 32 * (size_t)S);                   // pair-major RoPE tables
   // The SwiGLU scratch is only live in the MLP half, the V^T copies only in
   // the attention half: they share the tail of the workspace.
   return t + std::max(swiglu_workspace_bytes_ex((int)M, blk->model_dim, blk->mlp_dim,
@@ -621,7 +634,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
                   int cond_rows, const float* ctx_k, const float* ctx_v,
                   const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
                   const float* rcos, const float* rsin, void* workspace, cudaStream_t s,
-                  int stats_layer) {
+                  int stats_layer, const float* rope_t) {
   const int D = blk->model_dim, NH = blk->heads;
   const size_t M = (size_t)B * S;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -646,6 +659,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
   int32_t* rz2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
   int* clist = reinterpret_cast<int*>(take(sizeof(int) * (size_t)B * C));
   int* ccount = reinterpret_cast<int*>(take(sizeof(int) * B));
+  float* rope_ws = reinterpret_cast<float*>(take(sizeof(float) * 2 * 32 * (size_t)S));
   void* sw_ws = ws + off;
   int st;
   // Two-term activation policy per projection group (dit.c:429-436,
@@ -684,9 +698,17 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       return st;
     }
     if (half == 0) {
-      // QKVG on one quantised copy of h (dit.c:785-792).
+      // QKVG on one quantised copy of h (dit.c:785-792).  With the
+      // tensor-core attention and the single-term policy, the head norm,
+      // RoPE and the V transpose run in the GEMM's epilogue (EPI_QKV).
+      AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
+                       sw_ws, nullptr, attention_mode() == 2 ? 0 : 1};
+      const bool tc = attention_mode() != 1 && attention_tc_supported(ar);
+      const bool fuse_heads = tc && !res_qkvg;
+      float* vt = static_cast<float*>(sw_ws);
+      const int vld = attention_tc_vt_ld(S);
       GemmRequest r;
-      r.epi = res_qkvg ? EPI_DUAL : EPI_SPLIT;
+      r.epi = res_qkvg ? EPI_DUAL : fuse_heads ? EPI_QKV : EPI_SPLIT;
       r.M = (int)M;
       r.a = codes;
       r.lda = D;
@@ -705,16 +727,30 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       r.outs[1] = k;
       r.outs[2] = v;
       r.outs[3] = g;
+      if (fuse_heads) {
+        if (!rope_t) {
+          rope_pair_major_kernel<<<cdiv(S * 32, 256), 256, 0, s>>>(rcos, rsin, S, rope_ws);
+          if ((st = check_launch())) return st;
+          rope_t = rope_ws;
+        }
+        r.outs[2] = nullptr;
+        r.hn_q = blk->q_norm;
+        r.hn_k = blk->k_norm;
+        r.rcos = rope_t;
+        r.rsin = rope_t + 32 * (size_t)S;
+        r.vt = vt;
+        r.vt_ld = vld;
+        r.tokens = S;
+        r.eps = blk->norm_eps;
+      }
       if ((st = gemm_launch(c, r, s))) return st;
-      AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
-                       sw_ws, nullptr, attention_mode() == 2 ? 0 : 1};
-      if (attention_mode() != 1 && attention_tc_supported(ar)) {
-        // Head norm + RoPE with the self V^T rows the attention kernel reads.
-        float* vt = static_cast<float*>(sw_ws);
-        const int ld = attention_tc_vt_ld(S);
-        qk_norm_rope_vt_kernel<<<dim3(cdiv(S, 32), NH, B), 256, 0, s>>>(
-            q, k, v, vt, S, D, NH, ld, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
-        if ((st = check_launch())) return st;
+      if (tc) {
+        if (!fuse_heads) {
+          // Head norm + RoPE with the self V^T rows the attention kernel reads.
+          qk_norm_rope_vt_kernel<<<dim3(cdiv(S, 32), NH, B), 256, 0, s>>>(
+              q, k, v, vt, S, D, NH, vld, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
+          if ((st = check_launch())) return st;
+        }
         ar.vt_self = vt;
         if ((st = attention_tc_launch(c, ar, s))) return st;
       } else {

@@ -30,6 +30,6 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
                   int cond_rows, const float* ctx_k, const float* ctx_v,
                   const uint8_t* ctx_mask, int context_batch, int B, int S, int C,
                   const float* rcos, const float* rsin, void* workspace, cudaStream_t s,
-                  int stats_layer = -1);
+                  int stats_layer = -1, const float* rope_t = nullptr);
 
 }  // namespace iro

@@ -301,12 +301,13 @@ size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 struct StepBufs {
   float* rcos;
   float* rsin;
+  float* rope_t;  // pair-major copy: cos [32][S], then sin [32][S]
   uint8_t* cond_mask;
   uint8_t* rest;
 };
 
 size_t head_bytes(int R, int S, int C) {
-  return 2 * al256(sizeof(float) * (size_t)S * 32) + al256((size_t)R * C);
+  return 4 * al256(sizeof(float) * (size_t)S * 32) + al256((size_t)R * C);
 }
 
 StepBufs carve(uint8_t* ws, int S) {
@@ -314,7 +315,8 @@ StepBufs carve(uint8_t* ws, int S) {
   const size_t tab = al256(sizeof(float) * (size_t)S * 32);
   b.rcos = reinterpret_cast<float*>(ws);
   b.rsin = reinterpret_cast<float*>(ws + tab);
-  b.cond_mask = ws + 2 * tab;
+  b.rope_t = reinterpret_cast<float*>(ws + 2 * tab);
+  b.cond_mask = ws + 4 * tab;
   b.rest = nullptr;
   return b;
 }
@@ -340,10 +342,18 @@ int upload_rope(const StepBufs& b, int S, cudaStream_t s) {
   std::vector<float> hc((size_t)S * 32), hs((size_t)S * 32);
   int st = iro_dit_rope_table(hc.data(), hs.data(), S, 64);
   if (st) return st;
+  std::vector<float> ht((size_t)S * 64);
+  for (int tok = 0; tok < S; tok++)
+    for (int j = 0; j < 32; j++) {
+      ht[(size_t)j * S + tok] = hc[(size_t)tok * 32 + j];
+      ht[(size_t)(32 + j) * S + tok] = hs[(size_t)tok * 32 + j];
+    }
   cudaError_t e = cudaMemcpyAsync(b.rcos, hc.data(), sizeof(float) * hc.size(),
                                   cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(b.rsin, hs.data(), sizeof(float) * hs.size(), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(b.rope_t, ht.data(), sizeof(float) * ht.size(), cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -441,7 +451,7 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
     for (int i = 0; i < 6; i++)
       ada[i] = cb.params + (((size_t)(2 * l) * 3 + i) * cb.n + row) * D;
     st = dit_block_run(c, &m->block[l], x, ada, 1, ctx_k[l], ctx_v[l], mask, R, B, S, C, tb.rcos,
-                       tb.rsin, blk_ws, s, l);
+                       tb.rsin, blk_ws, s, l, tb.rope_t);
     if (st) return st;
   }
   // Output head (normalised in place: x is rebuilt from the state next

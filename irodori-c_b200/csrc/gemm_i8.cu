@@ -87,6 +87,13 @@ struct GemmParams {
   float* hidden;
   int ldh;
   int H;
+  const float* hn_q;  // EPI_QKV
+  const float* hn_k;
+  const float* rcos;
+  const float* rsin;
+  float* vt;
+  int vt_ld, tokens, heads;
+  float eps;
   DevError* err;
   uint64_t limit_ns;
   unsigned long long* trace;  // optional per-CTA timestamps (IRO_GEMM_TRACE)
@@ -352,6 +359,101 @@ __global__ void __launch_bounds__(kThreads, 1)
           gated_chunk(r1, r3, c0, HALF + c0, p_cs, p_sw, p_b, zp, sx, v);
           emit(v, &tmO.m[0], h0, p.H, p.hidden + (size_t)row * p.ldh + h0);
         }
+      } else if constexpr (EPI == EPI_QKV) {
+        // One head (64 columns) per warp.  q and k: the head RMSNorm in the
+        // reference's order (sequential mean square, then x * (inv * w);
+        // dit.c:638-690) and, on the first half of the heads, the rotation
+        // of each (even, odd) pair by the token's RoPE angle.  v: stored
+        // transposed per head (the attention kernel's V^T rows; for a fixed
+        // dimension the warp's 32 rows are 32 consecutive tokens, so each
+        // store instruction writes 128 contiguous bytes).  gate: as is.
+        static_assert(BN / kParts == 64, "one head per epilogue warp");
+        const int c0 = part * 64;
+        const int n0 = nb * BN + c0;
+        if (n0 < p.N) {  // warp-uniform
+          const int g = n0 / p.seg;
+          const int col0 = n0 - g * p.seg;
+          const int head = col0 >> 6;
+          const int seq = row_ok ? row / p.tokens : 0;
+          const int tok = row_ok ? row - seq * p.tokens : 0;
+          auto deq = [&](int c, float (&v)[kChunk]) {
+            uint32_t r[kChunk];
+            tmem_ld_32x32b_x16(tbase + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < kChunk / 4; i++) {
+              const int4 cs = *reinterpret_cast<const int4*>(p_cs + c + 4 * i);
+              const float4 sw = *reinterpret_cast<const float4*>(p_sw + c + 4 * i);
+              float2 lo = dequant2(r[4 * i], r[4 * i + 1], zp, cs.x, cs.y, sx, sw.x, sw.y);
+              float2 hi = dequant2(r[4 * i + 2], r[4 * i + 3], zp, cs.z, cs.w, sx, sw.z, sw.w);
+              if (p.bias) {
+                const float4 b = *reinterpret_cast<const float4*>(p_b + c + 4 * i);
+                lo = add2_rn(lo, make_float2(b.x, b.y));
+                hi = add2_rn(hi, make_float2(b.z, b.w));
+              }
+              v[4 * i] = lo.x;
+              v[4 * i + 1] = lo.y;
+              v[4 * i + 2] = hi.x;
+              v[4 * i + 3] = hi.y;
+            }
+          };
+          if (g < 2) {
+            float ms = 0.0f;
+            for (int ch = 0; ch < 64; ch += kChunk) {
+              float v[kChunk];
+              deq(c0 + ch, v);
+#pragma unroll
+              for (int j = 0; j < kChunk; j++) ms = __fadd_rn(ms, __fmul_rn(v[j], v[j]));
+            }
+            const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, 64.0f), p.eps)));
+            const float* nw = (g == 0 ? p.hn_q : p.hn_k) + col0;
+            const bool rope = head < p.heads / 2;
+            const float* rc = p.rcos + tok;  // pair-major: pair j at rc[j * tokens]
+            const float* rs = p.rsin + tok;
+            float* drow = p.outs[g] + (size_t)row * p.seg + col0;
+            for (int ch = 0; ch < 64; ch += kChunk) {
+              float v[kChunk];
+              deq(c0 + ch, v);
+#pragma unroll
+              for (int j = 0; j < kChunk; j += 2) {
+                const float x0 = __fmul_rn(v[j], __fmul_rn(inv, __ldg(nw + ch + j)));
+                const float x1 = __fmul_rn(v[j + 1], __fmul_rn(inv, __ldg(nw + ch + j + 1)));
+                if (rope) {
+                  const size_t pj = (size_t)((ch + j) >> 1) * p.tokens;
+                  const float cr = __ldg(rc + pj), sr = __ldg(rs + pj);
+                  v[j] = __fsub_rn(__fmul_rn(x0, cr), __fmul_rn(x1, sr));
+                  v[j + 1] = __fadd_rn(__fmul_rn(x0, sr), __fmul_rn(x1, cr));
+                } else {
+                  v[j] = x0;
+                  v[j + 1] = x1;
+                }
+              }
+              emit(v, &tmO.m[g], col0 + ch, p.seg, drow + ch);
+            }
+          } else if (g == 2) {
+            float* vrow = p.vt + (size_t)(seq * p.heads + head) * 64 * p.vt_ld + tok;
+            const int pad = (row_ok && tok == p.tokens - 1) ? p.vt_ld - p.tokens : 0;
+            for (int ch = 0; ch < 64; ch += kChunk) {
+              float v[kChunk];
+              deq(c0 + ch, v);
+              if (row_ok) {
+#pragma unroll
+                for (int j = 0; j < kChunk; j++) {
+                  float* dst = vrow + (size_t)(ch + j) * p.vt_ld;
+                  dst[0] = v[j];
+                  for (int t = 1; t <= pad; t++) dst[t] = 0.0f;
+                }
+              }
+            }
+          } else {
+            float* drow = p.outs[3] + (size_t)row * p.seg + col0;
+            for (int ch = 0; ch < 64; ch += kChunk) {
+              float v[kChunk];
+              deq(c0 + ch, v);
+              emit(v, &tmO.m[3], col0 + ch, p.seg, drow + ch);
+            }
+          }
+        }
       } else {
         constexpr int PER = BN / kParts;
         for (int c0 = part * PER; c0 < (part + 1) * PER; c0 += kChunk) {
@@ -539,6 +641,13 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
     if (tma)
       st = make_tmap_f32_sw128(&om.m[0], r.hidden, (uint64_t)w->hidden, (uint64_t)r.M,
                                (uint64_t)r.ldh * 4);
+  } else if (EPI == EPI_QKV) {
+    // q, k and the gate through tile stores; v goes to V^T by direct stores.
+    for (int i : {0, 1, 3}) tma = tma && out_tma_ok(r.outs[i], r.seg);
+    for (int i : {0, 1, 3})
+      if (tma && st == IRO_OK)
+        st = make_tmap_f32_sw128(&om.m[i], r.outs[i], (uint64_t)r.seg, (uint64_t)r.M,
+                                 (uint64_t)r.seg * 4);
   } else if (EPI == EPI_SPLIT || (EPI == EPI_DUAL && r.nout > 0)) {
     for (int i = 0; i < r.nout && tma; i++) tma = out_tma_ok(r.outs[i], r.seg);
     for (int i = 0; tma && i < r.nout && st == IRO_OK; i++)
@@ -631,6 +740,15 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   p.hidden = r.hidden;
   p.ldh = r.ldh;
   p.H = w->hidden;
+  p.hn_q = r.hn_q;
+  p.hn_k = r.hn_k;
+  p.rcos = r.rcos;
+  p.rsin = r.rsin;
+  p.vt = r.vt;
+  p.vt_ld = r.vt_ld;
+  p.tokens = r.tokens;
+  p.heads = r.seg / 64;
+  p.eps = r.eps;
   p.err = c->err;
   p.limit_ns = kWaitLimitNs;
   switch (r.epi) {
@@ -657,6 +775,18 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       if (bn == 256) return launch_t<256, EPI_SPLIT>(c, r, p, s);
       if (bn == 128) return launch_t<128, EPI_SPLIT>(c, r, p, s);
       return launch_t<64, EPI_SPLIT>(c, r, p, s);
+    }
+    case EPI_QKV: {
+      // Four segments of whole 64-column heads; one head per epilogue warp
+      // needs 256-column tiles.
+      if (r.nout != 4 || r.seg <= 0 || r.seg % 64 != 0 || r.seg * 4 != w->N || r.accumulate ||
+          r.work || r.tokens <= 0 || r.M % r.tokens != 0 || r.vt_ld < r.tokens ||
+          r.vt_ld - r.tokens > 3)
+        return IRO_ERR_UNSUPPORTED;
+      if (!r.outs[0] || !r.outs[1] || !r.outs[3] || !r.vt || !r.hn_q || !r.hn_k || !r.rcos ||
+          !r.rsin)
+        return IRO_ERR_INVALID;
+      return launch_t<256, EPI_QKV>(c, r, p, s);
     }
     case EPI_GATED:
       // The tile holds one pair block: `pair` W1 rows then the matching W3 rows.

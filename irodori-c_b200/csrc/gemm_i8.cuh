@@ -9,8 +9,10 @@ enum EpiKind {
   EPI_LINEAR = 0,  // y (=|+=) dequant (+bias); optional raw s32 sums
   EPI_SPLIT = 1,   // as LINEAR, column block g written to outs[g]
   EPI_GATED = 2,   // hidden = silu(dequant W1 + b1) * (dequant W3 + b3)
-  EPI_DUAL = 3     // y = (dequant(q1) + bias) + dequant(q2); with accumulate
+  EPI_DUAL = 3,    // y = (dequant(q1) + bias) + dequant(q2); with accumulate
                    // y = (y + (dequant(q1) + bias)) + dequant(q2)
+  EPI_QKV = 4      // the QKVG split (outs = q, k, -, gate) with the DiT's head
+                   // RMSNorm + RoPE on q and k and v written as per-head V^T
 };
 
 // One GEMM request: A (u8 codes, rows of `lda` bytes, K valid) against the
@@ -41,6 +43,19 @@ struct GemmRequest {
   // times the gate, then added); `accumulate` must be 0.
   const float* rgate = nullptr;
   int rgate_rows = 0;
+  // EPI_QKV: head RMSNorm weights of q and k ([seg], head dim 64), the RoPE
+  // tables pair-major ([32][tokens] cos / sin, so that a warp's 32 rows read
+  // 32 consecutive tokens of one pair), the V^T destination ([rows / tokens]
+  // x heads x 64 rows of vt_ld floats; columns tokens..vt_ld-1 are zeroed)
+  // and the norm epsilon.  Row r is token r % tokens of sequence r / tokens.
+  const float* hn_q = nullptr;
+  const float* hn_k = nullptr;
+  const float* rcos = nullptr;
+  const float* rsin = nullptr;
+  float* vt = nullptr;
+  int vt_ld = 0;
+  int tokens = 0;
+  float eps = 0.0f;
   int force_bn = 0;         // 0 = heuristic
   int no_alloc = 0;         // never allocate (skips the IRO_GEMM_TRACE buffer)
 };
