@@ -12,7 +12,7 @@
 //   TMA warp    Q tile once, then K and V^T tiles through a two-stage ring,
 //               fp32 with the 128-byte swizzle (128 B rows of 32 floats)
 //   MMA warp    S_j = Q K_j^T    (tcgen05 kind::tf32, 128 x 64, K = 64,
-//                                 accumulator in TMEM, two S buffers)
+//                                 accumulator in TMEM, three S/P buffers)
 //               O  += P_j V_j    (A = P_j straight from TMEM, B = V_j^T
 //                                 K-major in shared memory, 128 x 64 in TMEM)
 //   4 warps     one query row per thread: scores from TMEM, scale 1/8, mask,
@@ -55,6 +55,7 @@ constexpr int kSmem = 1024 + kBarOff + 256 + 4 * kMaxCtxWords;
 // Two CTAs per SM: 2 x 99 KB of shared memory, 2 x 256 TMEM columns.
 constexpr uint32_t kTmemCols = 256;
 constexpr int kSBufs = 3;               // S/P buffers in TMEM
+constexpr int kPvLag = 1;               // PVs issued between PV_j and S_{j+3}
 constexpr uint32_t kColO = kSBufs * kKT;  // S/P buffers at columns 0, 64, 128; O at 192
 // Scores are kept in the log2 domain: t = s_raw * (1/8) * log2(e), p = 2^(t - m).
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
@@ -357,9 +358,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer (the leader's, for a pair) ----------------
-    // Order: S_0 S_1 S_2 | PV_0 S_3 | PV_1 S_4 | ... | PV_{T-1}.  With three
-    // S/P buffers, S_{j+3} only waits for PV_j, so the softmax of tile j+1
-    // never waits for the PV of tile j.
+    // Order (kPvLag = 1): S_0 S_1 S_2 | PV_0 | PV_1 S_3 | PV_2 S_4 | ... |
+    // PV_{T-1}.  With three S/P buffers S_{j+3} needs PV_j complete; issued
+    // after PV_{j+1}, its wait overlaps PV_{j+1} in the tensor pipe instead of
+    // draining it.  (Measured at config 3 it runs at the same speed as
+    // kPvLag = 0, S_{j+3} right after PV_j.)
     if (lane == 0 && leader) {
       const uint32_t q_addr = smem_u32(sQ);
       auto commit = [&](uint64_t* bar) {
@@ -417,13 +420,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; ok && j < kSBufs && j < T; j++) ok = issue_s(j);
       for (int j = 0; ok && j < T; j++) {
         ok = issue_pv(j);
-        if (ok && j + kSBufs < T) {
-          // Buffer j % 3 is free once PV_j has read P_j.
-          ok = mbar_wait_bounded(&pv_done[j % kSBufs], (j / kSBufs) & 1, a.err, 4, abort_flag,
+        const int i = j - kPvLag;  // buffer i % 3 is free once PV_i has read P_i
+        if (ok && i >= 0 && i + kSBufs < T) {
+          ok = mbar_wait_bounded(&pv_done[i % kSBufs], (i / kSBufs) & 1, a.err, 4, abort_flag,
                                  a.limit_ns) &&
-               issue_s(j + kSBufs);
+               issue_s(i + kSBufs);
         }
       }
+      // Every S_{i+3} (i + 3 < T) was issued at iteration i + kPvLag < T.
       // Drain: all MMAs issued by this thread have completed.
       if (PAIR)
         asm volatile(

@@ -361,16 +361,16 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
   }
 }
 
-// RoPE tables [S][32] -> pair-major [32][S] (cos block, then sin block), the
-// layout the QKVG epilogue reads (EPI_QKV).
-__global__ void rope_pair_major_kernel(const float* __restrict__ rcos,
-                                       const float* __restrict__ rsin, int S,
-                                       float* __restrict__ out) {
+// RoPE tables [S][32] -> groups of four pairs [8][S][4] (cos block, then the
+// sin block at 32 * S), the layout the QKVG epilogue reads (EPI_QKV).
+__global__ void rope_group4_kernel(const float* __restrict__ rcos, const float* __restrict__ rsin,
+                                   int S, float* __restrict__ out) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= S * 32) return;
   const int tok = i >> 5, pair = i & 31;
-  out[(size_t)pair * S + tok] = rcos[i];
-  out[(size_t)(32 + pair) * S + tok] = rsin[i];
+  const size_t o = ((size_t)(pair >> 2) * S + tok) * 4 + (pair & 3);
+  out[o] = rcos[i];
+  out[(size_t)32 * S + o] = rsin[i];
 }
 
 // Valid context positions per batch row (dit.c:811-813, 828-839); the mask
@@ -598,7 +598,7 @@ size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int 
   t += 6 * al256(sizeof(float) * M * D);                           // h, q, k, v, g, mix
   t += 2 * (al256(M * D) + 2 * al256(sizeof(float) * M));          // codes (two terms) + row params
   t += al256(sizeof(int) * (size_t)B * C) + al256(sizeof(int) * B);
-  t += al256(sizeof(float) * 2 * 32 * (size_t)S);                   // pair-major RoPE tables
+  t += al256(sizeof(float) * 2 * 32 * (size_t)S);                   // grouped RoPE tables
   // The SwiGLU scratch is only live in the MLP half, the V^T copies only in
   // the attention half: they share the tail of the workspace.
   return t + std::max(swiglu_workspace_bytes_ex((int)M, blk->model_dim, blk->mlp_dim,
@@ -704,7 +704,8 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
                        sw_ws, nullptr, attention_mode() == 2 ? 0 : 1};
       const bool tc = attention_mode() != 1 && attention_tc_supported(ar);
-      const bool fuse_heads = tc && !res_qkvg;
+      auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+      const bool fuse_heads = tc && !res_qkvg && al16(blk->q_norm) && al16(blk->k_norm);
       float* vt = static_cast<float*>(sw_ws);
       const int vld = attention_tc_vt_ld(S);
       GemmRequest r;
@@ -729,7 +730,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       r.outs[3] = g;
       if (fuse_heads) {
         if (!rope_t) {
-          rope_pair_major_kernel<<<cdiv(S * 32, 256), 256, 0, s>>>(rcos, rsin, S, rope_ws);
+          rope_group4_kernel<<<cdiv(S * 32, 256), 256, 0, s>>>(rcos, rsin, S, rope_ws);
           if ((st = check_launch())) return st;
           rope_t = rope_ws;
         }

@@ -301,7 +301,7 @@ size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 struct StepBufs {
   float* rcos;
   float* rsin;
-  float* rope_t;  // pair-major copy: cos [32][S], then sin [32][S]
+  float* rope_t;  // grouped copy for the QKVG epilogue: cos [8][S][4], then sin
   uint8_t* cond_mask;
   uint8_t* rest;
 };
@@ -345,8 +345,9 @@ int upload_rope(const StepBufs& b, int S, cudaStream_t s) {
   std::vector<float> ht((size_t)S * 64);
   for (int tok = 0; tok < S; tok++)
     for (int j = 0; j < 32; j++) {
-      ht[(size_t)j * S + tok] = hc[(size_t)tok * 32 + j];
-      ht[(size_t)(32 + j) * S + tok] = hs[(size_t)tok * 32 + j];
+      const size_t o = ((size_t)(j >> 2) * S + tok) * 4 + (j & 3);
+      ht[o] = hc[(size_t)tok * 32 + j];
+      ht[(size_t)32 * S + o] = hs[(size_t)tok * 32 + j];
     }
   cudaError_t e = cudaMemcpyAsync(b.rcos, hc.data(), sizeof(float) * hc.size(),
                                   cudaMemcpyHostToDevice, s);

@@ -406,26 +406,39 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < kChunk; j++) ms = __fadd_rn(ms, __fmul_rn(v[j], v[j]));
             }
             const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, 64.0f), p.eps)));
-            const float* nw = (g == 0 ? p.hn_q : p.hn_k) + col0;
+            const float4* nw4 = reinterpret_cast<const float4*>((g == 0 ? p.hn_q : p.hn_k) + col0);
             const bool rope = head < p.heads / 2;
-            const float* rc = p.rcos + tok;  // pair-major: pair j at rc[j * tokens]
-            const float* rs = p.rsin + tok;
+            // RoPE tables in groups of four pairs, [8][tokens][4]: one vector
+            // load gives a lane the four (cos, sin) of its token, and the
+            // warp's 32 consecutive tokens read 512 contiguous bytes.
+            const float4* rc4 = reinterpret_cast<const float4*>(p.rcos) + tok;
+            const float4* rs4 = reinterpret_cast<const float4*>(p.rsin) + tok;
             float* drow = p.outs[g] + (size_t)row * p.seg + col0;
             for (int ch = 0; ch < 64; ch += kChunk) {
               float v[kChunk];
               deq(c0 + ch, v);
 #pragma unroll
-              for (int j = 0; j < kChunk; j += 2) {
-                const float x0 = __fmul_rn(v[j], __fmul_rn(inv, __ldg(nw + ch + j)));
-                const float x1 = __fmul_rn(v[j + 1], __fmul_rn(inv, __ldg(nw + ch + j + 1)));
-                if (rope) {
-                  const size_t pj = (size_t)((ch + j) >> 1) * p.tokens;
-                  const float cr = __ldg(rc + pj), sr = __ldg(rs + pj);
-                  v[j] = __fsub_rn(__fmul_rn(x0, cr), __fmul_rn(x1, sr));
-                  v[j + 1] = __fadd_rn(__fmul_rn(x0, sr), __fmul_rn(x1, cr));
-                } else {
-                  v[j] = x0;
-                  v[j + 1] = x1;
+              for (int j = 0; j < kChunk; j += 4) {
+                const float4 w4 = __ldg(nw4 + ((ch + j) >> 2));
+                v[j] = __fmul_rn(v[j], __fmul_rn(inv, w4.x));
+                v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(inv, w4.y));
+                v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(inv, w4.z));
+                v[j + 3] = __fmul_rn(v[j + 3], __fmul_rn(inv, w4.w));
+              }
+              if (rope) {
+#pragma unroll
+                for (int j = 0; j < kChunk; j += 8) {
+                  // Pairs (ch + j) / 2 .. + 3 form group (ch + j) / 8.
+                  const size_t gi = (size_t)((ch + j) >> 3) * p.tokens;
+                  const float4 c4 = __ldg(rc4 + gi), s4 = __ldg(rs4 + gi);
+                  const float cr[4] = {c4.x, c4.y, c4.z, c4.w};
+                  const float sr[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                  for (int t = 0; t < 4; t++) {
+                    const float x0 = v[j + 2 * t], x1 = v[j + 2 * t + 1];
+                    v[j + 2 * t] = __fsub_rn(__fmul_rn(x0, cr[t]), __fmul_rn(x1, sr[t]));
+                    v[j + 2 * t + 1] = __fadd_rn(__fmul_rn(x0, sr[t]), __fmul_rn(x1, cr[t]));
+                  }
                 }
               }
               emit(v, &tmO.m[g], col0 + ch, p.seg, drow + ch);
@@ -786,6 +799,10 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       if (!r.outs[0] || !r.outs[1] || !r.outs[3] || !r.vt || !r.hn_q || !r.hn_k || !r.rcos ||
           !r.rsin)
         return IRO_ERR_INVALID;
+      // Vector loads of the norm weights and the grouped RoPE tables.
+      for (const void* q : {(const void*)r.hn_q, (const void*)r.hn_k, (const void*)r.rcos,
+                            (const void*)r.rsin})
+        if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0) return IRO_ERR_UNSUPPORTED;
       return launch_t<256, EPI_QKV>(c, r, p, s);
     }
     case EPI_GATED:

@@ -43,9 +43,10 @@ struct GemmRequest {
   // times the gate, then added); `accumulate` must be 0.
   const float* rgate = nullptr;
   int rgate_rows = 0;
-  // EPI_QKV: head RMSNorm weights of q and k ([seg], head dim 64), the RoPE
-  // tables pair-major ([32][tokens] cos / sin, so that a warp's 32 rows read
-  // 32 consecutive tokens of one pair), the V^T destination ([rows / tokens]
+  // EPI_QKV: head RMSNorm weights of q and k ([seg], head dim 64, 16-byte
+  // aligned), the RoPE tables in groups of four pairs ([8][tokens][4] cos /
+  // sin: element ((pair / 4) * tokens + token) * 4 + pair % 4, so a warp's 32
+  // rows read 32 consecutive tokens' groups), the V^T destination ([rows / tokens]
   // x heads x 64 rows of vt_ld floats; columns tokens..vt_ld-1 are zeroed)
   // and the norm epsilon.  Row r is token r % tokens of sequence r / tokens.
   const float* hn_q = nullptr;
