@@ -47,7 +47,7 @@ struct Cfg {
   static constexpr int STAGE = NA * A_BYTES + B_BYTES;
   static constexpr int STG = kEpiWarps * kStgBufs * kStgBytes;
   static constexpr int PARAMS = 2 * 3 * BN * 4;  // double-buffered colsum/scale/bias
-  static constexpr int BAR_BYTES = 256;
+  static constexpr int BAR_BYTES = 512;  // pipeline barriers, then 2 per epilogue warp
   static constexpr int FIXED = STG + PARAMS + BAR_BYTES + 1024;
   static constexpr int STAGES_RAW = (kSmemMax - FIXED) / STAGE;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Per epilogue warp and staging buffer: completion of the TMA load of the
+  // old output values (accumulate / gated residual epilogues).
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(stg_base + C::STG + C::PARAMS + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -160,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], kEpiWarps);
     }
+    for (int i = 0; i < 2 * kEpiWarps; i++) mbar_init(&xbar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -290,6 +294,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       pf.zp2 = (EPI == EPI_DUAL && rok) ? __ldg(p.zp2 + r) : 0;
     };
     if ((int)blockIdx.x < p.num_tiles) fetch(blockIdx.x);
+    // Old output values (y += ..., or the gated residual) come in by TMA
+    // tile loads into the staging buffer that the chunk's result then goes
+    // out from: one bulk copy per 32 x 16 chunk instead of per-lane row
+    // loads, and the next chunk's load is in flight while this one computes.
+    constexpr bool kMayLoadOld = (EPI == EPI_LINEAR || EPI == EPI_DUAL);
+    static_assert(kStgBufs == 2, "old-value loads alternate between two staging buffers");
+    const bool xload = kMayLoadOld && p.tma_out && (p.accumulate || p.rgate != nullptr);
+    uint32_t xph = 0;  // parity of each staging buffer's load barrier
+    auto x_issue = [&](int buf, int col, int r0) {
+      // Lane 0: the buffer's previous store has finished reading it.
+      if (lane == 0) {
+        bulk_wait_read<0>();
+        uint64_t* bar = &xbar[2 * e + buf];
+        mbar_arrive_expect_tx(bar, kStgBytes);
+        tma_load_2d(stg_mine + buf * kStgBytes, &tmO.m[0], bar, col, r0);
+      }
+    };
+    auto x_wait = [&](int buf) -> bool {
+      const bool ok = mbar_wait_bounded(&xbar[2 * e + buf], (xph >> buf) & 1u, p.err, 12,
+                                        abort_flag, p.limit_ns);
+      xph ^= 1u << buf;
+      return ok;
+    };
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(p, tile, mb, nb);
@@ -312,10 +339,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sx2 = pf.sx2;
       const int zp2 = pf.zp2;
       if (tile + (int)gridDim.x < p.num_tiles) fetch(tile + (int)gridDim.x);
+      // The first chunk's old values load while the accumulator fills.
+      // Quadrants wholly below the last row load nothing (and store nothing).
+      const bool xrow = xload && row0 < p.M;
+      const bool x_first = xrow && nb * BN + part * (BN / kParts) < p.N;
+      if (x_first) x_issue(sbuf, nb * BN + part * (BN / kParts), row0);
       // The vote doubles as the barrier that publishes the staged parameters;
       // if any warp's bounded wait gave up, all epilogue warps stop together.
       const bool got = mbar_wait_bounded(&tfull[acc], aph, p.err, 4, abort_flag, p.limit_ns);
-      if (named_bar_or(1, 32 * kEpiWarps, !got)) break;
+      if (named_bar_or(1, 32 * kEpiWarps, !got)) {
+        if (x_first) x_wait(sbuf);  // no load may still be landing at exit
+        break;
+      }
       tc_fence_after();
       if (e == 0 && lane == 0 && tile == (int)blockIdx.x) trace_mark(p, TR_EPI0);
       const uint32_t tbase =
@@ -490,7 +525,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int valid = ncols - col0;
           float v[kChunk];
           const bool gated_res = (EPI == EPI_LINEAR || EPI == EPI_DUAL) && p.rgate != nullptr;
-          if ((EPI == EPI_LINEAR || EPI == EPI_DUAL) && (p.accumulate || gated_res)) {
+          if (xload) {
+            // Next chunk's old values into the other buffer, then this one's.
+            const int c1 = c0 + kChunk;
+            if (xrow && c1 < (part + 1) * PER && nb * BN + c1 < p.N)
+              x_issue(sbuf ^ 1, nb * BN + c1, row0);
+            if (xrow) x_wait(sbuf);
+            // The old values are read from the staging buffer group by group
+            // below, as each is needed.
+          } else if ((EPI == EPI_LINEAR || EPI == EPI_DUAL) && (p.accumulate || gated_res)) {
             if (p.tma_out && valid >= kChunk) {
               // 16-byte aligned rows (the TMA store path requires it): four
               // vector loads per lane instead of sixteen scalar ones.
@@ -510,8 +553,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const float* grow =
               (gated_res && row_ok) ? p.rgate + (size_t)(row / p.rgate_rows) * p.N + n0 : nullptr;
+          const uint8_t* xs = stg_mine + sbuf * kStgBytes + lane * 64;
 #pragma unroll
           for (int i = 0; i < kChunk / 4; i++) {
+            if (xload) {
+              // 16-byte group i of this lane's row (64-byte swizzle).
+              const float4 o4 = *reinterpret_cast<const float4*>(xs + ((i ^ ((lane >> 1) & 3)) << 4));
+              v[4 * i] = o4.x;
+              v[4 * i + 1] = o4.y;
+              v[4 * i + 2] = o4.z;
+              v[4 * i + 3] = o4.w;
+            }
             const int c = c0 + 4 * i;
             const int4 cs = *reinterpret_cast<const int4*>(p_cs + c);
             const float4 sw = *reinterpret_cast<const float4*>(p_sw + c);
@@ -549,7 +601,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             v[4 * i + 2] = hi.x;
             v[4 * i + 3] = hi.y;
           }
-          emit(v, &tmO.m[g], col0, ncols, drow);
+          if (xload) {
+            // The result goes out from the buffer its old values came in by
+            // (each lane rewrites only its own row).
+            uint8_t* stg = stg_mine + sbuf * kStgBytes;
+            stage_row16(stg, lane, v);
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0 && row0 < p.M) {
+              tma_store_2d(&tmO.m[0], stg, n0, row0);
+              bulk_commit();
+            }
+            sbuf ^= 1;
+          } else {
+            emit(v, &tmO.m[g], col0, ncols, drow);
+          }
           if (EPI == EPI_LINEAR && p.work != nullptr && row_ok) {
             int32_t* wrow = p.work + (size_t)row * p.ldw + n0;
 #pragma unroll
