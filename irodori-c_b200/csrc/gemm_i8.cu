@@ -31,6 +31,7 @@
 namespace iro {
 
 constexpr int BM = 128;
+constexpr int kHalfM = 64;  // output rows per EPI_DUAL2 tile
 constexpr int BKB = 128;  // K bytes per pipeline stage (one swizzle row)
 constexpr int kEpiWarps = 16;      // 4 per TMEM lane quadrant / per scheduler
 constexpr int kParts = kEpiWarps / 4;  // column parts per quadrant
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (EPI == EPI_DUAL) tma_prefetch_desc(&tmA2);
+    if (EPI == EPI_DUAL || EPI == EPI_DUAL2) tma_prefetch_desc(&tmA2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -202,7 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * C::STAGE;
           uint8_t* sb = sa + C::NA * C::A_BYTES;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
-          tma_load_2d(sa, &tmA, &full[s], kb * BKB, mb * BM);
+          if (EPI == EPI_DUAL2) {
+            // Rows 0-63 of the A tile: term 1 of output rows mb*64..; rows
+            // 64-127: term 2 of the same rows (two 64-row boxes).
+            tma_load_2d(sa, &tmA, &full[s], kb * BKB, mb * kHalfM);
+            tma_load_2d(sa + kHalfM * BKB, &tmA2, &full[s], kb * BKB, mb * kHalfM);
+          } else {
+            tma_load_2d(sa, &tmA, &full[s], kb * BKB, mb * BM);
+          }
           if (EPI == EPI_DUAL) tma_load_2d(sa + C::A_BYTES, &tmA2, &full[s], kb * BKB, mb * BM);
           tma_load_2d(sb, &tmB, &full[s], kb * BKB, nb * BN);
           if (tile == (int)blockIdx.x && kb == 0) trace_mark(p, TR_TMA0);
@@ -286,10 +294,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       pf.cs = ok ? __ldg(p.wcolsum + n) : 0;
       pf.sw = ok ? __ldg(p.wscale + n) : 0.0f;
       pf.b = (ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
-      const int r = mb * BM + quad * 32 + lane;
+      const int r = (EPI == EPI_DUAL2 ? mb * kHalfM + (quad & 1) * 32 : mb * BM + quad * 32) + lane;
       const bool rok = r < p.M;
-      pf.sx = rok ? __ldg(p.sx + r) : 0.0f;
-      pf.zp = rok ? __ldg(p.zp + r) : 0;
+      // EPI_DUAL2: quadrants 2 and 3 hold the second term (its row scales).
+      const bool term2 = EPI == EPI_DUAL2 && quad >= 2;
+      pf.sx = rok ? __ldg((term2 ? p.sx2 : p.sx) + r) : 0.0f;
+      pf.zp = rok ? __ldg((term2 ? p.zp2 : p.zp) + r) : 0;
       pf.sx2 = (EPI == EPI_DUAL && rok) ? __ldg(p.sx2 + r) : 0.0f;
       pf.zp2 = (EPI == EPI_DUAL && rok) ? __ldg(p.zp2 + r) : 0;
     };
@@ -298,9 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile loads into the staging buffer that the chunk's result then goes
     // out from: one bulk copy per 32 x 16 chunk instead of per-lane row
     // loads, and the next chunk's load is in flight while this one computes.
-    constexpr bool kMayLoadOld = (EPI == EPI_LINEAR || EPI == EPI_DUAL);
+    constexpr bool kMayLoadOld = (EPI == EPI_LINEAR || EPI == EPI_DUAL || EPI == EPI_DUAL2);
     static_assert(kStgBufs == 2, "old-value loads alternate between two staging buffers");
-    const bool xload = kMayLoadOld && p.tma_out && (p.accumulate || p.rgate != nullptr);
+    // EPI_DUAL2: quadrants 2 and 3 only pass their dequantised second term
+    // to quadrants 0 and 1 (through their own staging buffers), which finish
+    // and store the rows.
+    const bool writer2 = EPI == EPI_DUAL2 && quad >= 2;
+    const bool xload = kMayLoadOld && !writer2 && p.tma_out && (p.accumulate || p.rgate != nullptr);
+    uint32_t xc = 0;  // EPI_DUAL2 hand-over buffer counter (same sequence in both warps)
     uint32_t xph = 0;  // parity of each staging buffer's load barrier
     auto x_issue = [&](int buf, int col, int r0) {
       // Lane 0: the buffer's previous store has finished reading it.
@@ -331,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p_sw[et] = pf.sw;
         p_b[et] = pf.b;
       }
-      const int row0 = mb * BM + quad * 32;
+      const int row0 = EPI == EPI_DUAL2 ? mb * kHalfM + (quad & 1) * 32 : mb * BM + quad * 32;
       const int row = row0 + lane;
       const bool row_ok = row < p.M;
       const float sx = pf.sx;
@@ -502,6 +517,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if (writer2) {
+        // EPI_DUAL2 second term: dequantise (no bias) and hand over.
+        constexpr int PER = BN / kParts;
+        const int bar_id = 2 + part * 2 + (quad & 1);
+        for (int c0 = part * PER; c0 < (part + 1) * PER; c0 += kChunk) {
+          const int n0 = nb * BN + c0;
+          if (n0 >= p.N) break;  // warp-uniform, the same in the partner warp
+          uint32_t r[kChunk];
+          tmem_ld_32x32b_x16(tbase + c0, r);
+          tmem_ld_wait();
+          float v[kChunk];
+#pragma unroll
+          for (int i = 0; i < kChunk / 4; i++) {
+            const int c = c0 + 4 * i;
+            const int4 cs = *reinterpret_cast<const int4*>(p_cs + c);
+            const float4 sw = *reinterpret_cast<const float4*>(p_sw + c);
+            const float2 lo = dequant2(r[4 * i], r[4 * i + 1], zp, cs.x, cs.y, sx, sw.x, sw.y);
+            const float2 hi = dequant2(r[4 * i + 2], r[4 * i + 3], zp, cs.z, cs.w, sx, sw.z, sw.w);
+            v[4 * i] = lo.x;
+            v[4 * i + 1] = lo.y;
+            v[4 * i + 2] = hi.x;
+            v[4 * i + 3] = hi.y;
+          }
+          // Buffers alternate, so this write never meets the partner's read
+          // of the previous chunk (which it finished before the last barrier).
+          stage_row16(stg_mine + (xc & 1) * kStgBytes, lane, v);
+          named_bar(bar_id, 64);
+          xc++;
+        }
       } else {
         constexpr int PER = BN / kParts;
         for (int c0 = part * PER; c0 < (part + 1) * PER; c0 += kChunk) {
@@ -524,7 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           float* drow = base + (size_t)row * ld + col0;
           const int valid = ncols - col0;
           float v[kChunk];
-          const bool gated_res = (EPI == EPI_LINEAR || EPI == EPI_DUAL) && p.rgate != nullptr;
+          const bool gated_res =
+              (EPI == EPI_LINEAR || EPI == EPI_DUAL || EPI == EPI_DUAL2) && p.rgate != nullptr;
           if (xload) {
             // Next chunk's old values into the other buffer, then this one's.
             const int c1 = c0 + kChunk;
@@ -533,7 +578,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (xrow) x_wait(sbuf);
             // The old values are read from the staging buffer group by group
             // below, as each is needed.
-          } else if ((EPI == EPI_LINEAR || EPI == EPI_DUAL) && (p.accumulate || gated_res)) {
+          } else if ((EPI == EPI_LINEAR || EPI == EPI_DUAL || EPI == EPI_DUAL2) &&
+                     (p.accumulate || gated_res)) {
             if (p.tma_out && valid >= kChunk) {
               // 16-byte aligned rows (the TMA store path requires it): four
               // vector loads per lane instead of sixteen scalar ones.
@@ -554,6 +600,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* grow =
               (gated_res && row_ok) ? p.rgate + (size_t)(row / p.rgate_rows) * p.N + n0 : nullptr;
           const uint8_t* xs = stg_mine + sbuf * kStgBytes + lane * 64;
+          // EPI_DUAL2: the partner warp (two quadrants up, e - 2) has staged
+          // this chunk's second term.
+          const uint8_t* t2 =
+              EPI == EPI_DUAL2
+                  ? stg_base + (e - 2) * kStgBufs * kStgBytes + (xc & 1) * kStgBytes + lane * 64
+                  : nullptr;
+          if (EPI == EPI_DUAL2) {
+            named_bar(2 + part * 2 + (quad & 1), 64);
+            xc++;
+          }
 #pragma unroll
           for (int i = 0; i < kChunk / 4; i++) {
             if (xload) {
@@ -583,6 +639,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               lo = add2_rn(lo, dequant2(r2[4 * i], r2[4 * i + 1], zp2, cs.x, cs.y, sx2, sw.x, sw.y));
               hi = add2_rn(hi, dequant2(r2[4 * i + 2], r2[4 * i + 3], zp2, cs.z, cs.w, sx2, sw.z, sw.w));
+            }
+            if (EPI == EPI_DUAL2) {
+              if (p.accumulate) {
+                lo = add2_rn(make_float2(v[4 * i], v[4 * i + 1]), lo);
+                hi = add2_rn(make_float2(v[4 * i + 2], v[4 * i + 3]), hi);
+              }
+              const float4 d2 =
+                  *reinterpret_cast<const float4*>(t2 + ((i ^ ((lane >> 1) & 3)) << 4));
+              lo = add2_rn(lo, make_float2(d2.x, d2.y));
+              hi = add2_rn(hi, make_float2(d2.z, d2.w));
             }
             if (EPI == EPI_LINEAR && p.accumulate) {
               lo = add2_rn(make_float2(v[4 * i], v[4 * i + 1]), lo);
@@ -699,12 +765,13 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
   }
   const IroInt8DevWeight* w = r.w;
   CUtensorMap ta, tb, ta2;
-  int st = make_tmap_u8(&ta, r.a, (uint64_t)w->K, (uint64_t)r.M, (uint64_t)r.lda, BKB, BM);
+  constexpr int ABOX = EPI == EPI_DUAL2 ? kHalfM : BM;  // A rows per TMA box
+  int st = make_tmap_u8(&ta, r.a, (uint64_t)w->K, (uint64_t)r.M, (uint64_t)r.lda, BKB, ABOX);
   if (st) return st;
   st = make_tmap_u8(&tb, w->data, (uint64_t)w->K, (uint64_t)w->N, (uint64_t)w->ld, BKB, BN);
   if (st) return st;
-  if (EPI == EPI_DUAL) {
-    st = make_tmap_u8(&ta2, r.a2, (uint64_t)w->K, (uint64_t)r.M, (uint64_t)r.lda, BKB, BM);
+  if (EPI == EPI_DUAL || EPI == EPI_DUAL2) {
+    st = make_tmap_u8(&ta2, r.a2, (uint64_t)w->K, (uint64_t)r.M, (uint64_t)r.lda, BKB, ABOX);
     if (st) return st;
   } else {
     ta2 = ta;
@@ -740,7 +807,7 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
   }
   if (st) return st;
   p.tma_out = tma ? 1 : 0;
-  p.tiles_m = cdiv(r.M, BM);
+  p.tiles_m = cdiv(r.M, EPI == EPI_DUAL2 ? kHalfM : BM);
   p.tiles_n = cdiv(w->N, BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   {
@@ -890,6 +957,8 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       } else if (!r.y) {
         return IRO_ERR_INVALID;
       }
+      // Into y: both terms stacked in one A tile, N = 256 MMAs.
+      if (r.nout == 0 && !r.force_bn) return launch_t<256, EPI_DUAL2>(c, r, p, s);
       const int bn = r.force_bn ? r.force_bn : pick_bn(r.M, w->N, c->num_sms, 1);
       if (bn == 128) return launch_t<128, EPI_DUAL>(c, r, p, s);
       return launch_t<64, EPI_DUAL>(c, r, p, s);

@@ -11,8 +11,11 @@ enum EpiKind {
   EPI_GATED = 2,   // hidden = silu(dequant W1 + b1) * (dequant W3 + b3)
   EPI_DUAL = 3,    // y = (dequant(q1) + bias) + dequant(q2); with accumulate
                    // y = (y + (dequant(q1) + bias)) + dequant(q2)
-  EPI_QKV = 4      // the QKVG split (outs = q, k, -, gate) with the DiT's head
+  EPI_QKV = 4,     // the QKVG split (outs = q, k, -, gate) with the DiT's head
                    // RMSNorm + RoPE on q and k and v written as per-head V^T
+  EPI_DUAL2 = 5    // EPI_DUAL into y (nout = 0) with both terms stacked in one
+                   // 128-row A tile: 64 output rows per tile, N = 256 MMAs
+                   // (chosen by gemm_launch for EPI_DUAL requests)
 };
 
 // One GEMM request: A (u8 codes, rows of `lda` bytes, K valid) against the
