@@ -293,7 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool ok = et < BN && n < p.N;
       pf.cs = ok ? __ldg(p.wcolsum + n) : 0;
       pf.sw = ok ? __ldg(p.wscale + n) : 0.0f;
-      pf.b = (ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      if (EPI == EPI_QKV) {
+        // The bias slot carries the head-norm weight of q / k columns (the
+        // QKVG projection has no bias).
+        const int gq = ok ? n / p.seg : 2;
+        pf.b = gq == 0 ? __ldg(p.hn_q + n) : gq == 1 ? __ldg(p.hn_k + (n - p.seg)) : 0.0f;
+      } else {
+        pf.b = (ok && p.bias) ? __ldg(p.bias + n) : 0.0f;
+      }
       const int r = (EPI == EPI_DUAL2 ? mb * kHalfM + (quad & 1) * 32 : mb * BM + quad * 32) + lane;
       const bool rok = r < p.M;
       // EPI_DUAL2: quadrants 2 and 3 hold the second term (its row scales).
@@ -456,7 +463,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < kChunk; j++) ms = __fadd_rn(ms, __fmul_rn(v[j], v[j]));
             }
             const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, 64.0f), p.eps)));
-            const float4* nw4 = reinterpret_cast<const float4*>((g == 0 ? p.hn_q : p.hn_k) + col0);
             const bool rope = head < p.heads / 2;
             // RoPE tables in groups of four pairs, [8][tokens][4]: one vector
             // load gives a lane the four (cos, sin) of its token, and the
@@ -465,11 +471,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4* rs4 = reinterpret_cast<const float4*>(p.rsin) + tok;
             float* drow = p.outs[g] + (size_t)row * p.seg + col0;
             for (int ch = 0; ch < 64; ch += kChunk) {
+              // This chunk's RoPE groups load before the TMEM read and the
+              // dequantisation, which then cover their latency.
+              float4 c4[2], s4[2];
+              if (rope) {
+#pragma unroll
+                for (int q2 = 0; q2 < 2; q2++) {
+                  const size_t gi = (size_t)((ch >> 3) + q2) * p.tokens;
+                  c4[q2] = __ldg(rc4 + gi);
+                  s4[q2] = __ldg(rs4 + gi);
+                }
+              }
               float v[kChunk];
               deq(c0 + ch, v);
 #pragma unroll
               for (int j = 0; j < kChunk; j += 4) {
-                const float4 w4 = __ldg(nw4 + ((ch + j) >> 2));
+                // Norm weights staged with the tile's column parameters.
+                const float4 w4 = *reinterpret_cast<const float4*>(p_b + c0 + ch + j);
                 v[j] = __fmul_rn(v[j], __fmul_rn(inv, w4.x));
                 v[j + 1] = __fmul_rn(v[j + 1], __fmul_rn(inv, w4.y));
                 v[j + 2] = __fmul_rn(v[j + 2], __fmul_rn(inv, w4.z));
@@ -479,10 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < kChunk; j += 8) {
                   // Pairs (ch + j) / 2 .. + 3 form group (ch + j) / 8.
-                  const size_t gi = (size_t)((ch + j) >> 3) * p.tokens;
-                  const float4 c4 = __ldg(rc4 + gi), s4 = __ldg(rs4 + gi);
-                  const float cr[4] = {c4.x, c4.y, c4.z, c4.w};
-                  const float sr[4] = {s4.x, s4.y, s4.z, s4.w};
+                  const float4 cg = c4[j >> 3], sg = s4[j >> 3];
+                  const float cr[4] = {cg.x, cg.y, cg.z, cg.w};
+                  const float sr[4] = {sg.x, sg.y, sg.z, sg.w};
 #pragma unroll
                   for (int t = 0; t < 4; t++) {
                     const float x0 = v[j + 2 * t], x1 = v[j + 2 * t + 1];
@@ -926,6 +943,7 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       // Four segments of whole 64-column heads; one head per epilogue warp
       // needs 256-column tiles.
       if (r.nout != 4 || r.seg <= 0 || r.seg % 64 != 0 || r.seg * 4 != w->N || r.accumulate ||
+          r.bias ||  // the bias slot carries the norm weights
           r.work || r.tokens <= 0 || r.M % r.tokens != 0 || r.vt_ld < r.tokens ||
           r.vt_ld - r.tokens > 3)
         return IRO_ERR_UNSUPPORTED;
