@@ -13,7 +13,16 @@
 //                of the tile's columns: tcgen05.ld 16 columns at a time, the
 //                exact reference float arithmetic (ops.c:468-490), 64-byte
 //                swizzled staging and TMA tile stores; runs while the MMA
-//                warp fills the other accumulator.
+//                warp fills the other accumulator.  Epilogues that read the
+//                old output (accumulate, gated residual) TMA-load it into
+//                the same staging buffers, one chunk ahead.
+//
+// Epilogue kinds: LINEAR, SPLIT (column blocks to separate outputs), GATED
+// (silu(W1) * W3 from the pair-interleaved weight), DUAL (two activation
+// terms, two accumulators), DUAL2 (two terms stacked in one A tile: rows
+// 0-63 term 1, rows 64-127 term 2 of the same 64 output rows; quadrants 2-3
+// hand their dequantised term to quadrants 0-1 through shared memory), QKV
+// (the DiT's QKVG split with head RMSNorm, RoPE and the V^T store).
 //
 // Parity: the integer sums are exact.  The epilogue uses explicitly rounded
 // intrinsics in the reference's order, so fp32 outputs are bit-identical to
