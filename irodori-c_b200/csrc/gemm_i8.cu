@@ -602,8 +602,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (xrow && c1 < (part + 1) * PER && nb * BN + c1 < p.N)
               x_issue(sbuf ^ 1, nb * BN + c1, row0);
             if (xrow) x_wait(sbuf);
-            // The old values are read from the staging buffer group by group
-            // below, as each is needed.
+            if (EPI == EPI_LINEAR) {
+              // All four groups now (fewer registers live than reading them
+              // group by group in this variant); the two-term variants read
+              // them group by group below.
+              const uint8_t* xr = stg_mine + sbuf * kStgBytes + lane * 64;
+#pragma unroll
+              for (int i = 0; i < 4; i++) {
+                const float4 o4 = *reinterpret_cast<const float4*>(xr + ((i ^ ((lane >> 1) & 3)) << 4));
+                v[4 * i] = o4.x;
+                v[4 * i + 1] = o4.y;
+                v[4 * i + 2] = o4.z;
+                v[4 * i + 3] = o4.w;
+              }
+            }
           } else if ((EPI == EPI_LINEAR || EPI == EPI_DUAL || EPI == EPI_DUAL2) &&
                      (p.accumulate || gated_res)) {
             if (p.tma_out && valid >= kChunk) {
@@ -638,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int i = 0; i < kChunk / 4; i++) {
-            if (xload) {
+            if (xload && EPI != EPI_LINEAR) {
               // 16-byte group i of this lane's row (64-byte swizzle).
               const float4 o4 = *reinterpret_cast<const float4*>(xs + ((i ^ ((lane >> 1) & 3)) << 4));
               v[4 * i] = o4.x;
