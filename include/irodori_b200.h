@@ -127,7 +127,10 @@ int iro_cuda_device_count(void);
 /* The library stream of the current device (cudaStream_t as void*). */
 void *iro_cuda_stream(void);
 /* Block until the library stream (or `stream`) is idle; returns status,
-   including a pending in-kernel timeout report. */
+   including a pending in-kernel timeout report.  Every entry point's kernels
+   report into one error word per device (static device memory); this call
+   reads and clears it.  With a non-NULL `stream` it creates no context and
+   allocates nothing. */
 int iro_cuda_synchronize(void *stream);
 
 /* Device memory helpers for callers without their own allocator. */
@@ -265,18 +268,23 @@ void iro_int8_swiglu_pipe_free(IroSwigluPipe *pipe);
 
 /* The SwiGLU block without allocation.  No counterpart in the reference.
    For callers that cannot allocate device memory where they run the block:
-   code recording it into a CUDA graph under global-mode stream capture,
-   engines that reserve all device memory at start-up, and latency-critical
-   loops (growing the library arena calls cudaFree, which waits for the
-   device).  Same arguments and results as iro_int8_swiglu_dev without the
-   workspace: the scratch is a 64 MiB array inside the library, reserved on
-   every GPU where the library's device code is loaded until the process
-   exits.  Calls whose scratch (iro_int8_swiglu_workspace_bytes) exceeds
-   64 MiB are rejected with IRO_ERR_UNSUPPORTED and a message on stderr; split
-   the rows.  It calls no cudaMalloc/cudaFree and does not touch the library
-   context.  The first call on a device resolves the scratch address, so make
-   it before any stream capture.  Calls share the scratch: calls that can
-   overlap on the GPU race.  `stream` NULL is the default stream. */
+   engines that reserve all device memory at start-up and treat a later
+   allocation as a failure, hosts whose device memory belongs to another
+   allocator, and latency-critical loops (growing the library arena calls
+   cudaFree, which waits for the whole device).  Same arguments and results
+   as iro_int8_swiglu_dev without the workspace (bit-identical outputs): the
+   scratch is a 64 MiB array inside the library, reserved on every GPU where
+   the library's device code is loaded until the process exits.  Calls whose
+   scratch (iro_int8_swiglu_workspace_bytes) exceeds 64 MiB are rejected with
+   IRO_ERR_UNSUPPORTED and a message on stderr; split the rows (about 4,400
+   rows at D 1024 / H 2816, single-term W2).  It calls no cudaMalloc or
+   cudaFree and does not touch the library context.  The first call on a
+   device resolves the scratch address, so make it before any stream capture.
+   Calls share the scratch, which keeps the last call's contents (every byte a
+   call reads it writes first): calls that can overlap on the GPU race.  The
+   return value covers the launches; a bounded device wait that gave up is
+   reported by the next iro_cuda_synchronize(stream) with the same stream.
+   `stream` NULL is the legacy default stream. */
 int iro_int8_swiglu_noalloc_dev(const float *x, int M, const IroInt8DevWeight *w13,
                                 const IroInt8DevWeight *w2, const float *b2, float *out,
                                 int residual_w2, void *stream);

@@ -157,6 +157,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Completion of every MMA issued, waited for before TMEM is freed when a
+  // bounded wait gave up mid-tile.
+  uint64_t* drain = tempty + 3;
   // Per epilogue warp and staging buffer: completion of the TMA load of the
   // old output values (accumulate / gated residual epilogues).
   uint64_t* xbar = reinterpret_cast<uint64_t*>(stg_base + C::STG + C::PARAMS + 256);
@@ -174,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[i], kEpiWarps);
     }
     for (int i = 0; i < 2 * kEpiWarps; i++) mbar_init(&xbar[i], 1);
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -201,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      long long armed = 0;  // stages armed so far (loads issued)
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         int mb, nb;
         tile_coords(p, tile, mb, nb);
@@ -209,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          armed++;
           uint8_t* sa = smem + s * C::STAGE;
           uint8_t* sb = sa + C::NA * C::A_BYTES;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
@@ -229,6 +235,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (!ok) {
+        // A wait gave up: no load may still be landing in shared memory when
+        // the CTA exits.  Wait (bounded, regardless of the abort flag) for
+        // the last armed phase of every stage; in the normal path the MMA
+        // warp has consumed them all.
+        for (int st = 0; st < C::STAGES && st < armed; st++) {
+          const long long uses = (armed - 1 - st) / C::STAGES + 1;
+          mbar_wait_bounded(&full[st], (uint32_t)((uses - 1) & 1), p.err, 13, nullptr,
+                            p.limit_ns);
+        }
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -240,7 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t aph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        if (!mbar_wait_bounded(&tempty[acc], aph ^ 1u, p.err, 2, abort_flag, p.limit_ns)) break;
+        if (!mbar_wait_bounded(&tempty[acc], aph ^ 1u, p.err, 2, abort_flag, p.limit_ns)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * C::ACC_COLS);
         for (int kb = 0; kb < p.num_kb; kb++) {
@@ -271,6 +291,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tile == (int)blockIdx.x) trace_mark(p, TR_MMA_END0);
         acc ^= 1;
         if (acc == 0) aph ^= 1u;
+      }
+      if (!ok) {
+        // MMAs of an unfinished tile may still run: wait (bounded) for all of
+        // them before TMEM is freed.
+        mma_commit(drain);
+        mbar_wait_bounded(drain, 0, p.err, 14, nullptr, p.limit_ns);
       }
     }
     __syncwarp();
@@ -333,20 +359,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool xload = kMayLoadOld && !writer2 && p.tma_out && (p.accumulate || p.rgate != nullptr);
     uint32_t xc = 0;  // EPI_DUAL2 hand-over buffer counter (same sequence in both warps)
     uint32_t xph = 0;  // parity of each staging buffer's load barrier
+    // An old-value load whose wait gave up: this warp issues no further loads
+    // and stores nothing more (it still joins every barrier, so no partner
+    // warp is left waiting); the abort flag winds the CTA down.
+    bool xfail = false;
     auto x_issue = [&](int buf, int col, int r0) {
       // Lane 0: the buffer's previous store has finished reading it.
-      if (lane == 0) {
+      if (lane == 0 && !xfail) {
         bulk_wait_read<0>();
         uint64_t* bar = &xbar[2 * e + buf];
         mbar_arrive_expect_tx(bar, kStgBytes);
         tma_load_2d(stg_mine + buf * kStgBytes, &tmO.m[0], bar, col, r0);
       }
     };
-    auto x_wait = [&](int buf) -> bool {
-      const bool ok = mbar_wait_bounded(&xbar[2 * e + buf], (xph >> buf) & 1u, p.err, 12,
-                                        abort_flag, p.limit_ns);
+    // `drain`: wait for the load to land even when the CTA is aborting.
+    auto x_wait = [&](int buf, bool drain) -> bool {
+      const bool ok = xfail ? false
+                            : mbar_wait_bounded(&xbar[2 * e + buf], (xph >> buf) & 1u, p.err,
+                                                12, drain ? nullptr : abort_flag, p.limit_ns);
       xph ^= 1u << buf;
-      return ok;
+      xfail = __any_sync(0xffffffffu, !ok);
+      return !xfail;
     };
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int mb, nb;
@@ -379,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // if any warp's bounded wait gave up, all epilogue warps stop together.
       const bool got = mbar_wait_bounded(&tfull[acc], aph, p.err, 4, abort_flag, p.limit_ns);
       if (named_bar_or(1, 32 * kEpiWarps, !got)) {
-        if (x_first) x_wait(sbuf);  // no load may still be landing at exit
+        if (x_first) x_wait(sbuf, true);  // no load may still be landing at exit
         break;
       }
       tc_fence_after();
@@ -601,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int c1 = c0 + kChunk;
             if (xrow && c1 < (part + 1) * PER && nb * BN + c1 < p.N)
               x_issue(sbuf ^ 1, nb * BN + c1, row0);
-            if (xrow) x_wait(sbuf);
+            if (xrow) x_wait(sbuf, false);  // a give-up sets xfail (no store below)
             if (EPI == EPI_LINEAR) {
               // All four groups now (fewer registers live than reading them
               // group by group in this variant); the two-term variants read
@@ -712,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stage_row16(stg, lane, v);
             fence_async_shared();
             __syncwarp();
-            if (lane == 0 && row0 < p.M) {
+            if (lane == 0 && row0 < p.M && !xfail) {
               tma_store_2d(&tmO.m[0], stg, n0, row0);
               bulk_commit();
             }

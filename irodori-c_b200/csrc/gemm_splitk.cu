@@ -408,7 +408,9 @@ int splitk_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   }
   const int grid = 2 * tiles;
   unsigned long long* tr = nullptr;
-  if (trace_on && cudaMalloc(&tr, sizeof(unsigned long long) * ST_SLOTS * grid) == cudaSuccess)
+  // The trace buffer is an allocation: never on the no-allocation path.
+  if (trace_on && !r.no_alloc &&
+      cudaMalloc(&tr, sizeof(unsigned long long) * ST_SLOTS * grid) == cudaSuccess)
     cudaMemsetAsync(tr, 0, sizeof(unsigned long long) * ST_SLOTS * grid, s);
   else
     cudaGetLastError();

@@ -6,11 +6,11 @@
 // from a caller workspace or from the library's arena, and the arena grows
 // with cudaMalloc.  Some callers cannot allow that on the path that runs the
 // block:
-//   - code that records the block into a CUDA graph under global-mode stream
-//     capture, where cudaMalloc is not permitted;
 //   - engines that reserve all their device memory at start-up and treat any
-//     later allocation as a failure (fixed-budget serving processes sharing a
-//     GPU);
+//     later allocation as a failure (serving processes that share a GPU
+//     under a fixed memory budget);
+//   - hosts whose device memory belongs to another allocator (a framework's
+//     caching pool) and that must not create allocations behind its back;
 //   - latency-critical loops, because growing an arena calls cudaFree, which
 //     waits for the whole device.
 // For them, iro_int8_swiglu_noalloc_dev() runs the same kernels on a scratch
@@ -25,19 +25,19 @@
 #include "quantize.cuh"
 
 namespace iro {
-namespace {
 
 constexpr size_t kNoAllocScratchBytes = 64ull << 20;
 
-// The scratch itself and this path's own device error word.  Host code must
-// not pass these names to a kernel: in host code they are stand-ins, not
-// device addresses.  The device addresses come from cudaGetSymbolAddress.
-__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-__device__ DevError g_noalloc_error;
+// The scratch.  Host code must not pass this name to a kernel: in host code
+// it is a stand-in, not a device address.  The device address comes from
+// cudaGetSymbolAddress (noalloc_setup).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
 
 struct NoAllocDevice {
   unsigned char* scratch;  // device address of g_noalloc_scratch
-  DevError* err;           // device address of g_noalloc_error
+  DevError* err;           // the device's error word (device_error_word)
   int num_sms;
   bool ready;
 };
@@ -46,7 +46,8 @@ NoAllocDevice g_noalloc_dev[64];
 std::mutex g_noalloc_mu;
 
 // Once per device, with that device current: resolve the device addresses
-// of the file-scope arrays.  This is the only set-up; it allocates nothing.
+// of the scratch array and of the library's device error word (both static
+// device memory).  This is the only set-up; it allocates nothing.
 int noalloc_setup(int dev, NoAllocDevice** out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   NoAllocDevice& d = g_noalloc_dev[dev];
@@ -59,16 +60,17 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
       return map_cuda(e);
     }
     if (major != 10) return IRO_ERR_NO_DEVICE;
-    void* scratch = nullptr;
-    void* err = nullptr;
-    e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
-    if (e == cudaSuccess) e = cudaGetSymbolAddress(&err, g_noalloc_error);
+    unsigned char* ptr = nullptr;
+    e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_scratch);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return map_cuda(e);
     }
-    d.scratch = static_cast<unsigned char*>(scratch);
-    d.err = static_cast<DevError*>(err);
+    DevError* err = nullptr;
+    const int st = device_error_word(dev, &err);
+    if (st != IRO_OK) return st;
+    d.scratch = ptr;
+    d.err = err;
     d.num_sms = sms;
     d.ready = true;
   }
@@ -86,7 +88,10 @@ using namespace iro;
 // this library's device code on that device if it has not done so yet; make
 // that first call before any stream capture.  Calls share the one scratch
 // array, so calls that can overlap on the GPU (different streams without
-// ordering between them, or different host threads) race on it.
+// ordering between them, or different host threads) race on it.  A bounded
+// device wait that gives up inside the kernels records its code in the
+// device's error word, which iro_cuda_synchronize() on the call's stream
+// reports and clears.
 extern "C" int iro_int8_swiglu_noalloc_dev(const float* x, int M, const IroInt8DevWeight* w13,
                                            const IroInt8DevWeight* w2, const float* b2,
                                            float* out, int residual_w2, void* stream) {
@@ -142,7 +147,7 @@ extern "C" int iro_int8_swiglu_noalloc_dev(const float* x, int M, const IroInt8D
   }
 
   // A launch environment that owns nothing: the device, its SM count and
-  // this path's error word (the library context, which allocates, is not
+  // the device's error word (the library context, which allocates, is not
   // touched).
   Ctx env;
   env.device = dev;

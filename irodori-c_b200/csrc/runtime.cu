@@ -10,9 +10,16 @@
 
 namespace iro {
 
+// The device error word: bounded device waits that give up record their
+// code here.  A __device__ variable has one instance per GPU, so every device
+// has its own word without an allocation.
+__device__ DevError g_device_error;
+
 namespace {
 
 std::mutex g_ctx_mu;
+std::mutex g_err_mu;
+DevError* g_err_word[64] = {nullptr};
 Ctx* g_ctx[64] = {nullptr};
 thread_local int t_last_error = 0;
 
@@ -64,13 +71,15 @@ static int create_ctx(int dev, Ctx** out) {
   Ctx* c = new Ctx();
   c->device = dev;
   c->num_sms = prop.multiProcessorCount;
+  int st = device_error_word(dev, &c->err);
+  if (st != IRO_OK) {
+    delete c;
+    return st;
+  }
   e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = cudaMalloc(&c->err, sizeof(DevError));
   if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(DevError));
-  if (e == cudaSuccess) e = cudaMallocHost(&c->err_host, sizeof(DevError));
   if (e != cudaSuccess) {
     if (c->stream) cudaStreamDestroy(c->stream);
-    if (c->err) cudaFree(c->err);
     delete c;
     return map_cuda(e);
   }
@@ -154,16 +163,52 @@ int ctx_copy_resources(Ctx* c, int n) {
   return IRO_OK;
 }
 
-int take_device_error(Ctx* c) {
-  if (cudaMemcpy(c->err_host, c->err, sizeof(DevError), cudaMemcpyDeviceToHost) != cudaSuccess)
-    return IRO_ERR_CUDA;
-  int code = c->err_host->code;
-  if (code != 0) {
-    fprintf(stderr, "irodori_b200: device reported error %d (wait site %d, block %d)\n", code,
-            c->err_host->where, c->err_host->block);
-    cudaMemset(c->err, 0, sizeof(DevError));
+int device_error_word(int dev, DevError** out) {
+  if (dev < 0 || dev >= 64) return IRO_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(g_err_mu);
+  if (!g_err_word[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_device_error);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return map_cuda(e);
+    }
+    g_err_word[dev] = static_cast<DevError*>(p);
   }
-  return code;
+  *out = g_err_word[dev];
+  return IRO_OK;
+}
+
+// Synchronous read of the word into host memory on the stack (no pinned
+// buffer), then a clear when a code was recorded.
+static int take_error_word(DevError* word) {
+  DevError h;
+  if (cudaMemcpy(&h, word, sizeof(DevError), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return IRO_ERR_CUDA;
+  }
+  if (h.code != 0) {
+    fprintf(stderr, "irodori_b200: device reported error %d (wait site %d, block %d)\n", h.code,
+            h.where, h.block);
+    if (cudaMemset(word, 0, sizeof(DevError)) != cudaSuccess) cudaGetLastError();
+  }
+  return h.code;
+}
+
+int take_device_error(Ctx* c) { return take_error_word(c->err); }
+
+int take_device_error_current() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return IRO_ERR_NO_DEVICE;
+  }
+  DevError* word = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_err_mu);
+    if (dev >= 0 && dev < 64) word = g_err_word[dev];
+  }
+  return word ? take_error_word(word) : IRO_OK;
 }
 
 static int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
@@ -286,12 +331,21 @@ void* iro_cuda_stream(void) {
 }
 
 int iro_cuda_synchronize(void* stream) {
-  int st;
-  Ctx* c = ctx_current(&st);
-  if (!c) return st;
-  cudaError_t e = cudaStreamSynchronize(pick_stream(c, stream));
-  if (e != cudaSuccess) return map_cuda(e);
-  int dev = take_device_error(c);
+  // With a caller stream no context is needed (nothing is allocated here);
+  // without one, the library stream of the current device's context.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!s) {
+    int st;
+    Ctx* c = ctx_current(&st);
+    if (!c) return st;
+    s = c->stream;
+  }
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return map_cuda(e);
+  }
+  int dev = take_device_error_current();
   return dev ? dev : IRO_OK;
 }
 

@@ -27,8 +27,7 @@ struct Ctx {
   int device = -1;
   int num_sms = 0;
   cudaStream_t stream = nullptr;
-  DevError* err = nullptr;       // device error word
-  DevError* err_host = nullptr;  // pinned mirror for reading after sync
+  DevError* err = nullptr;       // this device's error word (device_error_word)
   void* arena = nullptr;         // device scratch for the host-pointer API
   size_t arena_bytes = 0;
   std::mutex mu;
@@ -65,8 +64,18 @@ int check_launch();
 // context stream.
 void* arena_get(Ctx* c, size_t bytes, int* status);
 
+// Device address of the current device's error word: one static
+// __device__ word per GPU (no allocation), shared by every entry point,
+// resolved once per device with cudaGetSymbolAddress.  `dev` must be the
+// current device.
+int device_error_word(int dev, DevError** out);
+
 // Read (and clear) the device error word after the stream was synchronised.
 int take_device_error(Ctx* c);
+
+// The same for the current device without a context (allocates nothing);
+// returns IRO_OK when the word was never resolved on this device.
+int take_device_error_current();
 
 // 2-D u8/s8 tensor map for TMA: rows x inner bytes with the given row pitch
 // (multiple of 16), box = box_inner x box_rows, 128-byte swizzle.

@@ -319,16 +319,18 @@ def codec_conv1(hidden, w: Weight, bias, skip, residual=False):
 
 
 def ref_lib(kind="ieee"):
-    """kind: "ieee" (parity build), "codec", "dit", "vnni", or "fast" (product flags,
-    variant chosen for this host's ISA)."""
-    if kind == "fast":
-        kind = "fast_" + _host_isa_variant()
+    """kind: "ieee" (parity build), "codec", "dit", "vnni", "fast" (product flags,
+    variant chosen for this host's ISA), "dit_fast" / "codec_fast" (the DiT /
+    codec builds with the product flags, likewise) or "dit_vec" (the DiT build
+    with IEEE semantics at -O3 for the build host, fixture recording only)."""
+    if kind in ("fast", "dit_fast", "codec_fast"):
+        kind = kind + "_" + _host_isa_variant()
     if kind not in _ref_libs:
         path = os.path.join(REF_DIR, f"libiro_ref_{kind}.so")
         if not os.path.exists(path):
             raise RuntimeError(f"reference build {path} is missing")
         L = C.CDLL(path) if kind == "vnni" else _bind_ops(C.CDLL(path))
-        if kind == "codec":
+        if kind.startswith("codec"):
             L.ref_conv1d_int8_forward.argtypes = [_vp, C.c_int, C.c_int, _vp, _vp, _vp, C.c_int,
                                                   C.c_int, C.c_int, C.c_int, C.c_int, _vp,
                                                   C.c_int, _vp]
@@ -343,7 +345,7 @@ def ref_lib(kind="ieee"):
             L.ref_convtranspose1d_output_length.restype = C.c_int
             L.ref_codec_upsample_residual.argtypes = []
             L.ref_codec_upsample_residual.restype = C.c_int
-        if kind == "dit":
+        if kind.startswith("dit"):
             L.ref_dit_swiglu_int8.argtypes = [_vp, C.c_int] + [_vp] * 10
             L.ref_dit_swiglu_int8.restype = C.c_int
             L.ref_dit_block_int8.argtypes = [_vp] * 5 + [C.c_int] * 4 + [_vp] * 6
@@ -459,8 +461,8 @@ def ref_selfcheck(kind="ieee"):
 
 
 def ref_conv1d_int8(inp, w: Weight, kernel, stride=1, dilation=1, padding=0, bias=None,
-                    residual=False):
-    L = ref_lib("codec")
+                    residual=False, kind="codec"):
+    L = ref_lib(kind)
     inp = _c(inp, np.float32)
     T_in, Cin = inp.shape
     T_out = L.ref_conv1d_output_length(T_in, kernel, stride, dilation, padding)
@@ -498,11 +500,11 @@ def ref_codec_upsample_residual():
 
 
 def ref_dit_block(x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C_ctx, adaln, q_norm,
-                  k_norm, weights):
+                  k_norm, weights, kind="dit"):
     """The reference's dit_block (dit.c:983-1051) at layer 0 with int8
     projections.  weights: Weight objects wq, wk, wv, gate, wo, w1, w3, w2.
     Returns the updated x [B*S, D]."""
-    L = ref_lib("dit")
+    L = ref_lib(kind)
     x = _c(x, np.float32).copy()
     keep = [_c(a, np.float32) for a in adaln]
     ada = (_vp * 18)(*[a.ctypes.data for a in keep])
@@ -519,31 +521,31 @@ def ref_dit_block(x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C_ctx, adaln
     return x
 
 
-def ref_dit_condition(w0, w1, w2, t):
+def ref_dit_condition(w0, w1, w2, t, kind="dit"):
     """dit.c:502-530 for timesteps t [B] -> cond [B, 3*1280]."""
     t = _c(np.atleast_1d(t), np.float32)
     out = np.empty((t.size, w2.shape[0]), np.float32)
     ws = [_c(w, np.float32) for w in (w0, w1, w2)]
-    if ref_lib("dit").ref_dit_condition_w(*[_ptr(w) for w in ws], _ptr(t), t.size, _ptr(out)):
+    if ref_lib(kind).ref_dit_condition_w(*[_ptr(w) for w in ws], _ptr(t), t.size, _ptr(out)):
         raise RuntimeError("reference conditioner failed")
     return out
 
 
-def ref_dit_input(in_w, in_b, x, B, S):
+def ref_dit_input(in_w, in_b, x, B, S, kind="dit"):
     """dit.c:532-541: x [B*S, 32] -> [B*S, 1280]."""
     x = _c(x, np.float32)
     out = np.empty((B * S, in_w.shape[0]), np.float32)
-    if ref_lib("dit").ref_dit_input_w(_ptr(_c(in_w, np.float32)), _ptr(_c(in_b, np.float32)),
+    if ref_lib(kind).ref_dit_input_w(_ptr(_c(in_w, np.float32)), _ptr(_c(in_b, np.float32)),
                                       _ptr(x), B, S, _ptr(out)):
         raise RuntimeError("reference input projection failed")
     return out
 
 
-def ref_dit_output(out_norm, out_w, out_b, x, B, S):
+def ref_dit_output(out_norm, out_w, out_b, x, B, S, kind="dit"):
     """dit.c:1070-1090: RMSNorm + linear -> velocity [B*S, 32]."""
     x = _c(x, np.float32)
     out = np.empty((B * S, out_w.shape[0]), np.float32)
-    if ref_lib("dit").ref_dit_output_w(_ptr(_c(out_norm, np.float32)), _ptr(_c(out_w, np.float32)),
+    if ref_lib(kind).ref_dit_output_w(_ptr(_c(out_norm, np.float32)), _ptr(_c(out_w, np.float32)),
                                        _ptr(_c(out_b, np.float32)), _ptr(x), B, S, _ptr(out)):
         raise RuntimeError("reference output head failed")
     return out
@@ -596,6 +598,60 @@ def ref_dit_sample_euler(state, ctx_k, ctx_v, mask, blocks, head, R, cfg, S, C, 
         state = ref_dit_euler_step(state, ctx_k, ctx_v, mask if use else cond_rows, blocks, head,
                                    R, cfg if use else 1, S, C, t, tn, scales)
     return state
+
+
+def ref_dit_branch_velocity(state_r, ctx_k_r, ctx_v_r, mask_row, blocks, head, S, C, t,
+                            kind="dit"):
+    """The velocity of ONE CFG branch of one request at timestep t: the
+    conditioner (B=1), the input projection of the request's state
+    [S, 32], every layer's dit_block with batch 1 over that branch's
+    context mask row [C] (ctx_k_r / ctx_v_r: per layer [1, C, D]), then
+    the output head.  dit_block mixes rows only inside one batch row
+    (attention, dit.c:809-868) and applies its AdaLN per batch row, so a
+    batch of cfg branches equals cfg batch-1 calls
+    (tests/test_oracle.py checks this bit for bit).  Returns [S, 32]."""
+    cond = ref_dit_condition(head["cond_w0"], head["cond_w1"], head["cond_w2"], np.float32(t),
+                             kind=kind)
+    x = ref_dit_input(head["in_w"], head["in_b"], state_r, 1, S, kind=kind)
+    m = np.ascontiguousarray(mask_row, np.uint8).reshape(1, C)
+    for l, (adaln, qn, kn, W) in enumerate(blocks):
+        x = ref_dit_block(x, cond, ctx_k_r[l], ctx_v_r[l], m, 1, 1, S, C, adaln, qn, kn, W,
+                          kind=kind)
+    return ref_dit_output(head["out_norm"], head["out_w"], head["out_b"], x, 1, S, kind=kind)
+
+
+def ref_cfg_guided(v, scales):
+    """sampler.c:283-297: guided = v0, then += s_i * (v0 - v_i) for the
+    uncond rows in order, all in float32.  v: [cfg, S, 32]."""
+    g = v[0].copy()
+    for i in range(1, v.shape[0]):
+        g = g + np.float32(scales[i - 1]) * (v[0] - v[i])
+    return g
+
+
+def ref_dit_sample_request(state_r, ctx_k_r, ctx_v_r, mask_r, blocks, head, cfg, S, C, steps,
+                           init_scale, cfg_min_t, cfg_max_t, scales, kind="dit", pool=None):
+    """sampler.c:241-297 for one request, its CFG branches evaluated as
+    independent batch-1 forwards (in `pool`, a thread pool, when given: the
+    reference calls release the GIL).  Returns (final state [S, 32],
+    guided velocity per step [steps, S, 32], CFG rows used per step)."""
+    f = np.float32
+    state = np.array(state_r, np.float32, copy=True)
+    vels, rows = [], []
+    for step in range(steps):
+        u, un = f(step) / f(steps), f(step + 1) / f(steps)
+        t, tn = (f(1) - u) * f(init_scale), (f(1) - un) * f(init_scale)
+        use = cfg > 1 and f(cfg_min_t) <= t <= f(cfg_max_t)
+        nb = cfg if use else 1
+        run = lambda b, st=state, tt=t: ref_dit_branch_velocity(  # noqa: E731
+            st, ctx_k_r, ctx_v_r, mask_r[b], blocks, head, S, C, tt, kind=kind)
+        v = list(pool.map(run, range(nb))) if pool is not None else [run(b) for b in range(nb)]
+        g = ref_cfg_guided(np.stack(v), scales)
+        dt = f(tn - t)
+        state = state + g * dt
+        vels.append(g)
+        rows.append(nb)
+    return state, np.stack(vels), rows
 
 
 def ref_dit_block_dims():

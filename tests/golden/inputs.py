@@ -184,3 +184,25 @@ def dit_swiglu_inputs(D, H, rows=3):
     w3 = (rng.standard_normal((H, D)) * 0.02).astype(np.float32)
     w2 = (rng.standard_normal((D, H)) * 0.02).astype(np.float32)
     return x, w1, w3, w2
+
+
+def dit_sha(state, ck, cv, mask, blocks, head):
+    """SHA-256 over a DiT model case's inputs, in a fixed order."""
+    flat = [state, *ck, *cv, mask] + [a for b in blocks for a in (*b[0], b[1], b[2], *b[3])]
+    return sha(*flat, *head.values())
+
+
+# Config-3 row geometry at the reference's own dimensions: 12 layers, 8
+# requests x 4 CFG rows x 750 latent frames (24,000 rows per linear), 128
+# context tokens.  The reference fixes d_model 1280 / 20 heads / mlp 3680 as
+# compile-time constants (dit.c:11-20), so the full-geometry pin runs at
+# those dimensions.
+CFG3 = dict(seed=2026, layers=12, R=8, cfg=4, S=750, C=128)
+CFG3_SAMPLED = (0, 7)            # requests recorded by the fixture
+CFG3_SAMPLER = dict(steps=8, init_scale=0.999, cfg_min_t=0.5, cfg_max_t=1.0,
+                    scales=(2.0, 1.5, 1.0))  # generate.c:416-422 window
+
+
+def dit_cfg3_case():
+    c = CFG3
+    return dit_model_case(c["seed"], c["layers"], c["R"], c["cfg"], c["S"], c["C"])
