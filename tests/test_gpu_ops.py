@@ -183,6 +183,44 @@ def test_linear_dev_bit_exact(M, N, K, bias, accumulate):
     assert_same(yd.get(), oy, "outputs")
 
 
+@pytest.mark.parametrize("M", [64, 256, 4096, 65536])
+@pytest.mark.parametrize("N", [1024, 2816, 4096])
+def test_linear_sweep_shapes_bit_exact(M, N):
+    """Config 5's isolated GEMM sweep (K = 1024, config 1's distributions:
+    N(0,1) activations with 0.1% outliers x20, N(0,0.02) weights, N(0,0.01)
+    bias): the whole M on the device, every tile schedule up to 65536 rows;
+    the codes, raw int32 sums and outputs of a row sample (the first and last
+    96 rows and 128 random rows; rows are independent) bit-exact against
+    the oracle."""
+    K = 1024
+    rng = np.random.default_rng(M + N)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x[rng.random((M, K)) < 0.001] *= 20.0
+    b = (rng.standard_normal(N) * 0.01).astype(np.float32)
+    ow = oracle.weight_quantize(w)
+    dw = iro.DevWeight.upload((ow.data, ow.scale, ow.colsum))
+    xd = iro.DevBuf.from_host(x)
+    qd, sd, zd = iro.DevBuf((M, K), np.uint8), iro.DevBuf(M, np.float32), iro.DevBuf(M, np.int32)
+    iro.quantize_rows_dev(xd, M, K, qd, sd, zd)
+    bd = iro.DevBuf.from_host(b)
+    yd = iro.DevBuf((M, N), np.float32)
+    wk = iro.DevBuf((M, N), np.int32)
+    iro.linear_dev(qd, sd, zd, dw, bd, yd, M, work=wk)
+    iro.synchronize()
+    rows = np.unique(np.r_[0:min(96, M), max(0, M - 96):M, rng.integers(0, M, 128)])
+    q, s, z = oracle.quantize_rows(x[rows])
+    assert_same(qd.get()[rows], q, "codes")
+    oy, owork = oracle.linear_ex(q, s, z, ow, b)
+    assert_same(wk.get()[rows], owork, "int32 sums")
+    assert_same(yd.get()[rows], oy, "outputs")
+    # The no-raw-sum path (what the DiT and the sweep bench run) too.
+    yd2 = iro.DevBuf((M, N), np.float32)
+    iro.linear_dev(qd, sd, zd, dw, bd, yd2, M)
+    iro.synchronize()
+    assert_same(yd2.get()[rows], oy, "outputs without raw sums")
+
+
 @pytest.mark.parametrize("M,N,K", [(2048, 1024, 2816), (300, 512, 4096), (1000, 520, 2816),
                                    (129, 1024, 1030)])
 @pytest.mark.parametrize("bias,accumulate", [(True, False), (False, True)])

@@ -296,3 +296,35 @@ def test_fixture_generator_is_committed_and_runs_offline():
     """make_golden.py only needs oracle/_ref; it must not touch the network."""
     src = open(os.path.join(GOLDEN, "make_golden.py")).read()
     assert "oracle.ref_" in src and "urllib" not in src and "requests" not in src
+
+
+def test_dit_branch_split_and_vec_build_agree(ref_dit):
+    """The config-3 fixture (tests/golden/make_dit_cfg3.py) runs each CFG
+    branch as its own batch-1 forward, from the -O3 IEEE-semantics build
+    (libiro_ref_dit_vec.so) where it exists.  Both must give the reference
+    sampler's result bit for bit: batched (dit.c's B = cfg) from the -O2
+    parity build, on a two-step, one-layer case through the CFG window."""
+    R, cfg, S, C = 1, 4, 24, 12
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(71, 1, R, cfg, S, C)
+    bw = [(a, q, k, [oracle.weight_quantize(w) for w in w8]) for a, q, k, w8 in blocks]
+    scales = [2.0, 1.5, 1.0]
+    want = oracle.ref_dit_sample_euler(state, ck, cv, mask, bw, head, R, cfg, S, C, 2, 0.999,
+                                       0.6, 1.0, scales)
+    kinds = ["dit"] + (["dit_vec"] if oracle.ref_available("dit_vec") else [])
+    for kind in kinds:
+        fin, vel, rows = oracle.ref_dit_sample_request(
+            state[0], [k[0:1] for k in ck], [v[0:1] for v in cv], mask[:cfg], bw, head, cfg, S,
+            C, 2, 0.999, 0.6, 1.0, scales, kind=kind)
+        assert rows == [4, 1]
+        assert same(fin, want[0]), kind
+
+
+def test_cfg3_fixture_generator_is_committed():
+    src = open(os.path.join(GOLDEN, "make_dit_cfg3.py")).read()
+    assert "ref_dit_sample_request" in src and "urllib" not in src
+    g = load("dit_cfg3")
+    assert tuple(int(v) for v in g["case"]) == tuple(inputs.CFG3[k] for k in
+                                                     ("seed", "layers", "R", "cfg", "S", "C"))
+    assert list(g["rows_per_step"]) == [4, 4, 4, 4, 1, 1, 1, 1]
+    assert np.isfinite(g["velocity"]).all() and np.isfinite(g["final"]).all()
+    assert g["env_velocity_max"].shape == (8,) and (g["env_final"] > 0).all()
