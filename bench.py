@@ -1,25 +1,37 @@
 """Benchmark of the B200 int8 W8A8 path (one JSON line on rank 0).
 
-Workload (default): the int8 SwiGLU MLP block of the DiT,
-x fp32 [M=2048, D=1024] N(0,1); W1, W3 [2816, 1024] and W2 [1024, 2816]
-N(0,0.02) quantised per output channel; a seeded fp32 bias on every
-projection; per-row activation quantisation (the reference's asymmetric
-u8 + zero point, ops.c:321-348), silu(W1 x) * (W3 x), per-row
-requantisation, single-term W2 (IRO_INT8_RESIDUAL=0).  Synthetic data:
-there is no dataset or checkpoint for this path.
+Headline: the int8 SwiGLU MLP block of the DiT, x fp32
+[M=2048, D=1024] N(0,1); W1, W3 [2816, 1024] and W2 [1024, 2816] N(0,0.02)
+quantised per output channel; a seeded fp32 bias on every projection;
+per-row activation quantisation (the reference's asymmetric u8 + zero point,
+ops.c:321-348), silu(W1 x) * (W3 x), per-row requantisation, single-term W2
+(IRO_INT8_RESIDUAL=0).  A step is one pass of the block over one batch of M
+rows.  Metric: int8 TOPS = algorithmic ops (2*M*N*K per GEMM) / time.
+`value` has inputs resident in HBM; `e2e` goes through the host-buffer C-ABI
+pipeline (iro_int8_swiglu_pipe_*) with the step's x copied in from pinned
+host memory and the output copied back inside the timed region.  Both
+rotate through NSETS distinct input/weight sets whose total exceeds the
+126 MB L2.
 
-A step is one pass of the block over one batch of M rows.  Metric: int8
-TOPS = algorithmic ops (2*M*N*K per GEMM) / time.  `value` has inputs
-resident in HBM; `e2e` goes through the host-pointer C-ABI call
-iro_int8_swiglu() with the step's x copied in from pinned host memory and
-the output copied back inside the timed region.  Both rotate through
-NSETS distinct input/weight sets whose total exceeds the 126 MB L2.
+The same line carries the metric's second half and config 4 as nested
+objects, each with the reference's own CPU code timed beside it:
+  "dit"   BASELINE config 3: whole DiT Euler steps (12 blocks, d 1024, 16
+          heads, SwiGLU 2816; 8 requests x 4 CFG rows x 750 frames = 24,000
+          rows per linear per GPU), steps/s and rows/s;
+  "dit_ref_dims"  the same at the reference checkpoint's dimensions (d 1280,
+          20 heads, 3680; the only ones the reference's dit.c compiles to),
+          against the reference's dit.c forward on the host cores;
+  "conv7" BASELINE config 4: the codec's int8 kernel-7 conv, 4 x 48000
+          frames, 512 -> 512 channels.
+Synthetic seeded data throughout: there is no dataset or checkpoint for this
+path.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload sweep    # config 5: GEMM sweep + sampler sweep
 
-Multi-GPU: one process per GPU (torchrun); rows are sharded by whole
-batches, weights replicated, no collective on the data path (weak scaling).
-The device time is the max over ranks.
+Multi-GPU: one process per GPU (torchrun); whole requests (or whole blocks)
+per rank, weights replicated, no collective on the data path (weak
+scaling).  Device times are the max over ranks.
 """
 import argparse
 import json
@@ -30,6 +42,7 @@ import subprocess
 import sys
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
@@ -45,6 +58,15 @@ WORKLOAD = ("cfg2 int8 SwiGLU MLP block: x[2048,1024] -> quantise -> fused W1|W3
 OPS_W13 = 2.0 * M * D * (2 * H)
 OPS_W2 = 2.0 * M * H * D
 OPS_STEP = OPS_W13 + OPS_W2
+DTYPE = "int8 (u8 x s8 -> s32, fp32 dequant epilogue)"
+DATA = "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) biases)"
+ONEMKL = "oneMKL absent on this host: the reference's scalar exact int8 GEMM (ops.c:350-365)"
+
+# BASELINE config 3 and the reference checkpoint's dimensions.
+DIT_DIMS = {"cfg3": (1024, 16, 2816), "reference": (1280, 20, 3680)}
+DIT_RANK, DIT_LAYERS, DIT_CFG, DIT_S, DIT_C = 192, 12, 4, 750, 128
+DIT_REQUESTS = 8                   # per GPU
+DIT_SCALES = (2.0, 1.5, 1.0)
 
 
 def peaks():
@@ -63,10 +85,10 @@ def peaks():
                 "source": "fallback"}
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu
-    summary (profiles/), or None."""
-    path = os.path.join(ROOT, "profiles", "gemm_i8_gated_cfg2.md")
+def profile_traffic(name="gemm_i8_gated_cfg2.md"):
+    """DRAM bytes per launch of a kernel from its committed ncu summary
+    (profiles/), or None."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         txt = open(path).read()
     except OSError:
@@ -76,7 +98,7 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """nvidia-smi clock/throttle sampling during the timed regions."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -141,16 +163,19 @@ def dist_setup(n_gpus):
 
 
 def shard_requests(n_requests, world, rank):
-    """Contiguous block of whole requests for `rank` (every CFG row of a
-    request stays on one GPU: attention and the CFG combine mix rows only
-    within a request, SURVEY rows 8e / sampler.c:285-297)."""
+    """Contiguous block of whole requests for `rank`: every CFG row of a
+    request stays on one GPU, because attention (dit.c:809-868) and the CFG
+    combine (sampler.c:285-297) mix rows only within a request."""
     base, extra = divmod(n_requests, world)
     start = rank * base + min(rank, extra)
     return start, start + base + (1 if rank < extra else 0)
 
 
-def max_over_ranks_cpu(value, dist):
-    """Max of a host float over the process group (gloo or nccl)."""
+def max_over_ranks(value, dist=None):
+    """Max of a host float over the process group (nccl or gloo); the value
+    itself without one."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return value
     import torch
     dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
     t = torch.tensor([value], dtype=torch.float64, device=dev)
@@ -167,13 +192,57 @@ def physical_gpu(local):
     return local
 
 
-def make_sets(rng, iro, oracle_mod):
+def hold(stream, ms=3.0):
+    """Queue a short device-side wait on `stream` before a timed region, so
+    the host enqueues the region's launches while the device is busy and the
+    events then time the device work of exactly those launches back to
+    back.  The wait itself lies before the start event."""
+    import torch
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(ms * 2.0e6))
+
+
+def timed(stream, fn, n, hold_ms=3.0):
+    """Device time (ms) of fn(i) for i in range(n) on `stream`, measured with
+    CUDA events recorded on that stream."""
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    hold(stream, hold_ms)
+    e0.record(stream)
+    for i in range(n):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def _count_kernels(fn):
+    """Kernel launches of fn() seen by the CUDA activity profiler (untimed)."""
+    try:
+        import torch
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return sum(1 for e in prof.events()
+                   if getattr(e, "device_type", None) is not None
+                   and str(e.device_type).endswith("CUDA") and "emcpy" not in e.name
+                   and "emset" not in e.name)
+    except Exception:  # noqa: BLE001 - the count is informational
+        return None
+
+
+# ---------------------------------------------------------------------------
+# Config 2: the SwiGLU block.
+
+
+def make_sets(rng, iro, nsets=None):
     """NSETS synthetic (x, W1, W3, W2, biases) sets on the device."""
     sets = []
-    for i in range(NSETS):
+    for i in range(nsets or NSETS):
         x = rng.standard_normal((M, D), dtype=np.float32)
-        if i == 0:
-            x_host0 = x
         w1 = (rng.standard_normal((H, D), dtype=np.float32) * np.float32(0.02))
         w3 = (rng.standard_normal((H, D), dtype=np.float32) * np.float32(0.02))
         w2 = (rng.standard_normal((D, H), dtype=np.float32) * np.float32(0.02))
@@ -197,7 +266,7 @@ def make_sets(rng, iro, oracle_mod):
     return sets
 
 
-def check_parity(iro, oracle_mod, s0):
+def check_parity(oracle_mod, s0):
     """Spot check of set 0 against the oracle (not timed)."""
     w1, w3, w2 = s0["hw"]
     ow = [oracle_mod.Weight(h.data, h.scale, h.colsum) for h in (w1, w3, w2)]
@@ -207,110 +276,58 @@ def check_parity(iro, oracle_mod, s0):
     return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
 
 
-def run_ours(args):
+def leg_block(args, iro, stream, world, max_ranks, barrier):
+    """The headline: device-resident config-2 steps, the gated W1|W3 GEMM
+    alone (the roofline kernel) and the host-buffer pipeline (e2e)."""
     import torch
-    import torch.distributed as dist
-    import iro_b200 as iro
-
-    world, rank, local = dist_setup(args.gpus)
-    if world > 1:
-        from datetime import timedelta
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    iro.init(local)
-    torch.cuda.set_device(local)
-    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
-    rng = np.random.default_rng(1000 + rank)
-
     import oracle as oracle_mod
-    sets = make_sets(rng, iro, oracle_mod)
+
+    rng = np.random.default_rng(1000 + int(os.environ.get("RANK", "0")))
+    sets = make_sets(rng, iro)
+
     # A step is one iro_int8_swiglu_dev call: four kernels (quantise x,
-    # W1|W3 + silu, requantise, W2), each a programmatic dependent launch, so
-    # every kernel's launch and prologue overlap the previous one's tail,
-    # across steps too.  (A recorded graph per step, iro_int8_swiglu_plan,
-    # measured ~4 us slower per step: consecutive graph launches do not
-    # overlap.)
+    # W1|W3 + silu, requantise, W2), each a programmatic dependent launch.
     def step(i):
         s = sets[i % NSETS]
         iro.swiglu_dev(s["xd"], M, s["w13"], s["w2"], None, s["out"])
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---- device-resident throughput --------------------------------------
     for i in range(args.warmup):
         step(i)
     iro.synchronize()
-    rel_err = check_parity(iro, oracle_mod, sets[0]) if rank == 0 else 0.0
-
-    sampler = ClockSampler(physical_gpu(local)) if local == 0 else None
+    rel_err = check_parity(oracle_mod, sets[0])
     barrier()
-    torch.cuda.synchronize()
-    iro.synchronize()
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for i in range(args.steps):
+    # The warm-up steps again right before the timed region (no idle gap).
+    for i in range(args.warmup):
         step(i)
-    ev1.record(stream)
-    ev1.synchronize()
+    dev_ms = max_ranks(timed(stream, step, args.steps))
     iro.synchronize()
-    dev_ms = ev0.elapsed_time(ev1)
-    clocks = sampler.stop() if sampler else None
-    torch.cuda.synchronize()
     barrier()
-    dev_ms = max_over_ranks(dev_ms)
-    ms_per_step = dev_ms / args.steps
-    value = world * OPS_STEP * args.steps / (dev_ms * 1e-3) / 1e12
 
-    # ---- dominant kernel alone: fused W1|W3 GEMM + gate ------------------
-    kreps = max(50, min(args.steps, 2000))
+    # The dominant kernel alone: fused W1|W3 GEMM + silu gate.
+    kreps = max(50, min(args.steps * 10, 2000))
+
+    def gated(i):
+        s = sets[i % NSETS]
+        iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
+
     for i in range(5):
-        s = sets[i % NSETS]
-        iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
+        gated(i)
+    k_ms = max_ranks(timed(stream, gated, kreps) / kreps)
     iro.synchronize()
-    barrier()
-    k0 = torch.cuda.Event(enable_timing=True)
-    k1 = torch.cuda.Event(enable_timing=True)
-    k0.record(stream)
-    for i in range(kreps):
-        s = sets[i % NSETS]
-        iro.gated_dev(s["qx"], s["sx"], s["zx"], s["w13"], s["hid"], M)
-    k1.record(stream)
-    k1.synchronize()
-    iro.synchronize()
-    k_ms = max_over_ranks(k0.elapsed_time(k1) / kreps)
-    pk = peaks()
-    int8_peak = 2.0 * pk["bf16_tflops"]
-    k_tops = OPS_W13 / (k_ms * 1e-3) / 1e12
 
-    # ---- end to end through the host-buffer C ABI ---------------------------
-    # iro_int8_swiglu_pipe_*: each step copies its x in from page-locked host
-    # memory, runs the block and copies the output back to host memory; the
-    # ring of device slots lets one step's copy-in, the previous step's
-    # compute and the copy-out of the one before overlap.
+    # End to end through the host-buffer C ABI: iro_int8_swiglu_pipe_* copies
+    # each step's x in from page-locked host memory, runs the block and
+    # copies the output back; a ring of device slots overlaps one step's
+    # copy-in, the previous step's compute and the copy-out before it.
     NPIPE = 4
     pipes = [iro.SwigluPipe(M, sets[i]["w13"], sets[i]["w2"], depth=3) for i in range(NPIPE)]
-    xs_pinned = []
-    outs_pinned = []
+    xs_pinned, outs_pinned = [], []
     for s in sets[:NPIPE]:
         xp = torch.empty((M, D), dtype=torch.float32, pin_memory=True)
         xp.numpy()[:] = s["x"]
         xs_pinned.append(xp)
         outs_pinned.append(torch.empty((M, D), dtype=torch.float32, pin_memory=True))
-    e2e_steps = max(10, min(args.steps, 500))
+    e2e_steps = max(10, min(args.steps * 10, 500))
     for i in range(3):
         pipes[i % NPIPE].submit(xs_pinned[i % NPIPE].numpy(), outs_pinned[i % NPIPE].numpy())
     for pp in pipes:
@@ -322,67 +339,29 @@ def run_ours(args):
         pipes[j].submit(xs_pinned[j].numpy(), outs_pinned[j].numpy())
     for pp in pipes:
         pp.wait()
-    e2e_s = time.perf_counter() - t0
-    e2e_s = max_over_ranks(e2e_s)
-    e2e_tops = world * OPS_STEP * e2e_steps / e2e_s / 1e12
+    e2e_s = max_ranks(time.perf_counter() - t0)
     for pp in pipes:
         pp.free()
-
-    # ---- CPU baseline: the reference's own int8 path on the host cores ----
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_reference_sample(seconds=args.cpu_seconds)
-
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    line = {
-        "metric": METRIC,
-        "value": round(value, 3),
-        "unit": "TOPS",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "int8 (u8 x s8 -> s32, fp32 dequant epilogue)",
-        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) biases)",
-        "config": {"workload": WORKLOAD, "M": M, "D": D, "H": H, "ops_per_step": OPS_STEP,
-                   "global_batch_rows": M * world, "parallelism": f"replicas x{world}",
-                   "launch": "iro_int8_swiglu_dev per step: 4 programmatic dependent launches",
-                   "l2": f"rotating {NSETS} input+weight sets ({NSETS * 25} MB) > 126 MB L2",
-                   "pct_int8_peak": round(100.0 * value / world / int8_peak, 2),
-                   "parity_rel_err_vs_oracle": rel_err},
-        "e2e": {"value": round(e2e_tops, 3), "unit": "TOPS",
-                "h2d_bytes_per_step": M * D * 4, "d2h_bytes_per_step": M * D * 4,
-                "api": "iro_int8_swiglu_pipe_submit/wait (page-locked host buffers, 3-slot ring)"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel<256,EPI_GATED> (W1|W3 + silu)",
-                     "achieved": round(k_tops, 2), "peak": round(int8_peak, 1),
-                     "unit": "TFLOP/s",
-                     "peak_note": (f"int8 dense = 2 x {pk['source']} cuBLAS bf16 burst "
-                                   f"{pk['bf16_tflops']} TF/s (of {pk['source']})"),
-                     "frac": round(k_tops / int8_peak, 4), "traffic": profile_traffic(),
-                     "ms_per_launch": round(k_ms, 5), "ops_per_launch": OPS_W13},
-        "cpu_baseline": cpu,
-        "clocks": clocks,
-        "gpu_launches": 4 * args.steps,
-    }
-    print(json.dumps(line), flush=True)
+    e2e_tops = world * OPS_STEP * e2e_steps / e2e_s / 1e12
+    for s in sets:
+        for k in ("xd", "qx", "sx", "zx", "out", "hid"):
+            s[k].free()
+        s["w13"].free()
+        s["w2"].free()
+    return dict(dev_ms=dev_ms, k_ms=k_ms, rel_err=rel_err, e2e_tops=e2e_tops,
+                e2e_steps=e2e_steps, kreps=kreps)
 
 
 # ---------------------------------------------------------------------------
-# The reference's CPU path (oracle/_ref: ops.c built with the reference's
-# product flags -O3 -ffast-math for this host's ISA level), row slices over
-# all host threads (rows are independent: tests/test_int8_ops.c:87-97).
+# The reference's CPU paths (oracle/_ref: the reference's sources built with
+# its product flags -O3 -ffast-math for this host's ISA level), over all
+# host threads.
 
 
-def _ref_block(oracle_mod, L, x, ws, bs, threads):
+def _ref_block(oracle_mod, L, x, ws, bs, threads, pool):
+    """The reference's int8 SwiGLU (ops.c) over row slices: rows are
+    independent (tests/test_int8_ops.c:87-97)."""
     import ctypes as C
-    from concurrent.futures import ThreadPoolExecutor
 
     rows = x.shape[0]
     out = np.empty((rows, D), np.float32)
@@ -408,8 +387,7 @@ def _ref_block(oracle_mod, L, x, ws, bs, threads):
         out[lo:hi] = o
 
     bounds = [(rows * t // threads, rows * (t + 1) // threads) for t in range(threads)]
-    with ThreadPoolExecutor(threads) as ex:
-        list(ex.map(lambda b: part(*b), bounds))
+    list(pool.map(lambda b: part(*b), bounds))
     return out
 
 
@@ -424,81 +402,649 @@ def _ref_inputs(rows):
     return oracle_mod, x, ws, bs
 
 
-def _ref_lib():
+def _ref_kind(base):
+    """The product-flag build of `base` ("fast", "dit_fast", "codec_fast")
+    for this host, or None when the reference could not be compiled where
+    the build ran."""
     import oracle as oracle_mod
-    if oracle_mod.ref_available("fast_" + oracle_mod._host_isa_variant()):
-        return oracle_mod.ref_lib("fast"), "reference", "fast_" + oracle_mod._host_isa_variant()
-    return None, "port", None
+    try:
+        variant = base + "_" + oracle_mod._host_isa_variant()
+    except RuntimeError:
+        return None
+    return variant if oracle_mod.ref_available(variant) else None
 
 
-def cpu_reference_sample(seconds=10.0, rows=256):
-    L, kind, variant = _ref_lib()
+def cpu_block_steps(steps, warmup=1, seconds=None):
+    """The reference's config-2 block on all host threads, full M=2048 rows
+    per step.  Returns (seconds per step, cpu_baseline dict)."""
+    import oracle as oracle_mod
     threads = os.cpu_count() or 1
-    oracle_mod, x, ws, bs = _ref_inputs(rows)
-    if L is None:
-        # The C restatement (same algorithm, IEEE build), when the reference
-        # could not be compiled where the build ran.
-        def run():
-            oracle_mod.swiglu(x, *ws, *bs)
+    variant = _ref_kind("fast")
+    _, x, ws, bs = _ref_inputs(M)
+    pool = ThreadPoolExecutor(threads)
+    if variant is None:
+        run = lambda: oracle_mod.swiglu(x, *ws, *bs)  # noqa: E731 - the C restatement
+        kind = "port"
     else:
-        def run():
-            _ref_block(oracle_mod, L, x, ws, bs, threads)
-    run()
-    reps, t0 = 0, time.perf_counter()
-    while True:
+        L = oracle_mod.ref_lib(variant)
+        run = lambda: _ref_block(oracle_mod, L, x, ws, bs, threads, pool)  # noqa: E731
+        kind = "reference"
+    for _ in range(warmup):
         run()
+    times = []
+    t_all = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+        if len(times) >= steps and (not seconds or time.perf_counter() - t_all >= seconds):
+            break
+    pool.shutdown()
+    per = sum(times) / len(times)
+    return per, {"value": round(OPS_STEP / per / 1e12, 5), "unit": "TOPS", "cores": threads,
+                 "kind": kind, "build": variant or "oracle port (-O2 IEEE)", "onemkl": ONEMKL,
+                 "sample": f"the full cfg2 block ({M} rows) x {len(times)} steps, "
+                           f"{per * 1e3:.1f} ms per step, row slices over {threads} threads"}
+
+
+# ---------------------------------------------------------------------------
+# Config 3: whole DiT Euler steps.
+
+
+class DitCase:
+    """Random-init DiT weights, per-layer context K/V, a context mask and
+    N(0,1) latents for `requests` requests at dims (d, heads, mlp).  With
+    `iro` the weights are quantised on the device by the library's own
+    quantiser and uploaded; without it (the reference arm) the reference's
+    own iro_int8_weight_quantize (`ref_kind` build) quantises them and
+    nothing touches a GPU.  Both quantisers give identical bytes."""
+
+    def __init__(self, iro, dims, requests, seed=33, keep_host=False, ref_kind=None):
+        import oracle as oracle_mod
+        D_, NH, H_ = DIT_DIMS[dims]
+        self.D, self.NH, self.H, self.R = D_, NH, H_, requests
+        rng = np.random.default_rng(seed)
+        f = lambda *sh, s=1.0: (rng.standard_normal(sh, dtype=np.float32) * np.float32(s))  # noqa
+        self.blocks, self.host_blocks = [], []
+        for _ in range(DIT_LAYERS):
+            adaln = []
+            for _ in range(6):
+                adaln += [f(DIT_RANK, D_, s=0.03), f(D_, DIT_RANK, s=0.03), f(D_, s=0.02)]
+            qn, kn = 1.0 + f(D_, s=0.1), 1.0 + f(D_, s=0.1)
+            shapes = [(D_, D_, 0.03)] * 5 + [(H_, D_, 0.03), (H_, D_, 0.03), (D_, H_, 0.02)]
+            if iro is not None:
+                ws = [iro.HostWeight(f(n, k, s=sc)) for n, k, sc in shapes]
+                self.blocks.append(iro.DiTBlock(adaln, qn, kn, *ws, model_dim=D_, heads=NH,
+                                                rank=DIT_RANK, mlp_dim=H_))
+                hw = [oracle_mod.Weight(w.data, w.scale, w.colsum) for w in ws] \
+                    if keep_host else None
+            else:
+                hw = [oracle_mod.ref_weight_quantize(f(n, k, s=sc), kind=ref_kind)
+                      for n, k, sc in shapes]
+            if keep_host or iro is None:
+                self.host_blocks.append((adaln, qn, kn, hw))
+        self.head = {"cond_w0": f(D_, 512, s=0.04), "cond_w1": f(D_, D_, s=0.03),
+                     "cond_w2": f(3 * D_, D_, s=0.03), "in_w": f(D_, 32, s=0.15),
+                     "in_b": f(D_, s=0.02), "out_norm": 1.0 + f(D_, s=0.1),
+                     "out_w": f(32, D_, s=0.03), "out_b": f(32, s=0.02)}
+        self.ck = [f(requests, DIT_C, D_) for _ in range(DIT_LAYERS)]
+        self.cv = [f(requests, DIT_C, D_) for _ in range(DIT_LAYERS)]
+        mask = (rng.random((requests * DIT_CFG, DIT_C)) < 0.9).astype(np.uint8)
+        mask[:, 0] = 1
+        self.mask = mask
+        self.state0 = f(requests, DIT_S, 32)
+        if iro is not None:
+            self.model = iro.DiTModel(self.blocks, *self.head.values())
+            self.ckd = [iro.DevBuf.from_host(k) for k in self.ck]
+            self.cvd = [iro.DevBuf.from_host(v) for v in self.cv]
+            self.maskd = iro.DevBuf.from_host(mask)
+        self.rows = requests * DIT_CFG * DIT_S
+        # QKVG, Wo, W1|W3 and the two-term W2 (the default residual policy).
+        self.gemm_ops = 2.0 * self.rows * DIT_LAYERS * (4 * D_ * D_ + D_ * D_ + 2 * H_ * D_ +
+                                                       2 * H_ * D_)
+        self.attn_flops = 4.0 * self.rows * DIT_LAYERS * NH * 64 * (DIT_S + DIT_C)
+
+
+def leg_dit(args, iro, stream, dims, world, max_ranks, barrier, case=None):
+    """DiT Euler steps on this GPU's shard of requests (device-resident and
+    end to end), each step one iro_dit_sample_euler_dev step with the CFG
+    window open (four rows per request)."""
+    import torch
+
+    c = case or DitCase(iro, dims, DIT_REQUESTS, seed=33 + int(os.environ.get("RANK", "0")))
+    steps = args.steps
+    ws = iro.DevBuf(c.model.workspace_bytes(c.R, DIT_CFG, DIT_S, DIT_C, steps=max(steps, 8)),
+                    np.uint8)
+    state = torch.from_numpy(c.state0).cuda()
+    host_in = torch.from_numpy(c.state0).pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+
+    def sample(k):
+        c.model.sample_euler(state, c.R, DIT_CFG, DIT_S, k, 1.0, 0.0, 1.0, DIT_SCALES, c.ckd,
+                             c.cvd, c.maskd, DIT_C, workspace=ws)
+
+    sample(args.warmup)
+    iro.synchronize()
+    launches = None
+    if not args.no_count:
+        n1 = _count_kernels(lambda: sample(1))
+        n2 = _count_kernels(lambda: sample(2))
+        if n1 is not None and n2 is not None:
+            launches = (2 * n1 - n2) + steps * (n2 - n1)
+    barrier()
+    sample(1)
+    ms = max_ranks(timed(stream, lambda i: sample(steps), 1) / steps)
+    # End to end, every step: the latents in from pinned host memory, one
+    # Euler step, the new latents back to pinned host memory.
+    sd = torch.empty_like(state)
+
+    def e2e_step(i):
+        with torch.cuda.stream(stream):
+            sd.copy_(host_in, non_blocking=True)
+        c.model.euler_step(sd, c.R, DIT_CFG, DIT_S, 1.0 - i / (steps + 1),
+                           1.0 - (i + 1) / (steps + 1), DIT_SCALES, c.ckd, c.cvd, c.maskd, DIT_C,
+                           workspace=ws)
+        with torch.cuda.stream(stream):
+            host_out.copy_(sd, non_blocking=True)
+
+    e2e_step(0)
+    barrier()
+    ms_e2e = max_ranks(timed(stream, e2e_step, steps) / steps)
+    ws.free()
+    res = {"value": round(1000.0 / ms, 3), "unit": "steps/s", "ms_per_step": round(ms, 3),
+           "rows_per_s": round(world * c.rows * 1000.0 / ms, 1),
+           "requests_per_gpu": c.R, "rows_per_gpu": c.rows,
+           "int8_linear_tops": round(world * c.gemm_ops / ms / 1e9, 1),
+           "attention_tflop_per_step": round(world * c.attn_flops / 1e12, 3),
+           "e2e": {"value": round(1000.0 / ms_e2e, 3), "unit": "steps/s",
+                   "h2d_bytes_per_step": host_in.numel() * 4,
+                   "d2h_bytes_per_step": host_out.numel() * 4,
+                   "api": "iro_dit_euler_step_dev per step, latents copied in and out of "
+                          "pinned host memory inside the timed region"},
+           "gpu_launches": launches,
+           "dims": f"d{c.D}/h{c.NH}x64/mlp{c.H}/rank{DIT_RANK}",
+           "workload": f"{DIT_LAYERS} blocks, {c.R} requests x {DIT_CFG} CFG rows x {DIT_S} "
+                       f"frames ({c.rows} rows/linear) per GPU, {DIT_C} context tokens, CFG "
+                       f"window open every step"}
+    return res, c
+
+
+def leg_dit_gemm(args, iro, stream, dims, max_ranks):
+    """The config-3 W1|W3 gated GEMM (the DiT's largest int8 GEMM, M = 24000
+    rows) alone: the DiT line's roofline kernel."""
+    D_, _, H_ = DIT_DIMS[dims]
+    Mq = DIT_REQUESTS * DIT_CFG * DIT_S
+    rng = np.random.default_rng(10)
+    f = lambda *sh, s=1.0: rng.standard_normal(sh, dtype=np.float32) * np.float32(s)  # noqa
+    w13 = iro.DevWeight.gated_pair(iro.HostWeight(f(H_, D_, s=0.03)),
+                                   iro.HostWeight(f(H_, D_, s=0.03)))
+    xq = iro.DevBuf.from_host(f(Mq, D_))
+    q, s_, z = iro.DevBuf((Mq, D_), np.uint8), iro.DevBuf(Mq, np.float32), iro.DevBuf(Mq, np.int32)
+    iro.quantize_rows_dev(xq, Mq, D_, q, s_, z)
+    hid = iro.DevBuf((Mq, H_), np.float32)
+    run = lambda i: iro.gated_dev(q, s_, z, w13, hid, Mq)  # noqa: E731
+    for i in range(3):
+        run(i)
+    reps = max(10, min(args.steps * 5, 200))
+    k_ms = max_ranks(timed(stream, run, reps) / reps)
+    ops = 2.0 * Mq * D_ * 2 * H_
+    for b in (xq, q, s_, z, hid):
+        b.free()
+    w13.free()
+    return k_ms, ops
+
+
+def cpu_dit_sample(case, seconds=10.0):
+    """The reference's dit.c forward (conditioner, input projection, 12
+    dit_blocks, output head; dit.c:488-541, 983-1090) plus the CFG update
+    (sampler.c:283-297), product-flag build, on a sample of requests: every
+    CFG branch of every sampled request a batch-1 forward in its own host
+    thread (the reference is single-threaded per call; branches are
+    independent).  Returns a cpu_baseline dict (steps/s of the full
+    per-GPU request count)."""
+    import oracle as oracle_mod
+    variant = _ref_kind("dit_fast")
+    if variant is None:
+        return None
+    threads = os.cpu_count() or 1
+    n_req = max(1, min(case.R, threads // DIT_CFG))
+    pool = ThreadPoolExecutor(max(1, n_req * DIT_CFG))
+
+    def branch(job):
+        r, b = job
+        return oracle_mod.ref_dit_branch_velocity(
+            case.state0[r], [k[r:r + 1] for k in case.ck], [v[r:r + 1] for v in case.cv],
+            case.mask[r * DIT_CFG + b], case.host_blocks, case.head, DIT_S, DIT_C,
+            np.float32(0.875), kind=variant)
+
+    jobs = [(r, b) for r in range(n_req) for b in range(DIT_CFG)]
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        v = list(pool.map(branch, jobs))
+        for r in range(n_req):
+            g = oracle_mod.ref_cfg_guided(np.stack(v[r * DIT_CFG:(r + 1) * DIT_CFG]), DIT_SCALES)
+            _ = case.state0[r] + g * np.float32(-0.125)
         reps += 1
         el = time.perf_counter() - t0
-        if el >= seconds or reps >= 1000:
+        if el >= seconds:
             break
-    ops = OPS_STEP * rows / M * reps
-    return {"value": round(ops / el / 1e12, 5), "unit": "TOPS", "cores": threads, "kind": kind,
-            "build": variant or "oracle port (-O2 IEEE)",
-            "sample": f"{rows} of {M} rows of the cfg2 block x {reps} repetitions in {el:.1f} s"}
+    pool.shutdown()
+    per_sample_step = el / reps
+    step_s = per_sample_step * case.R / n_req   # the full request count, same threads
+    return {"value": round(1.0 / step_s, 5), "unit": "steps/s", "cores": threads,
+            "kind": "reference", "build": variant, "onemkl": ONEMKL,
+            "sample": f"{reps} Euler step(s) of {n_req} of {case.R} requests (all {DIT_CFG} CFG "
+                      f"branches, {n_req * DIT_CFG} host threads), {per_sample_step:.1f} s per "
+                      f"step; steps/s scaled to {case.R} requests"}
+
+
+# ---------------------------------------------------------------------------
+# Config 4: the codec's kernel-7 conv.
+
+CONV = dict(B=4, T=48000, C=512, N=512, KW=7)
+
+
+def _conv_inputs():
+    rng = np.random.default_rng(44)
+    inp = rng.standard_normal((CONV["B"], CONV["T"], CONV["C"]), dtype=np.float32) * np.float32(0.5)
+    w = rng.standard_normal((CONV["N"], CONV["KW"] * CONV["C"]), dtype=np.float32) * \
+        np.float32(0.02)
+    bias = rng.standard_normal(CONV["N"], dtype=np.float32) * np.float32(0.01)
+    return inp, w, bias
+
+
+def conv_ops():
+    return 2.0 * CONV["B"] * CONV["T"] * CONV["N"] * CONV["KW"] * CONV["C"]
+
+
+def leg_conv7(args, iro, stream, max_ranks):
+    inp, w, bias = _conv_inputs()
+    hw = iro.HostWeight(w)
+    dw = iro.DevWeight.upload(hw)
+    xd = iro.DevBuf.from_host(inp)
+    bd = iro.DevBuf.from_host(bias)
+    out = iro.DevBuf((CONV["B"], CONV["T"], CONV["N"]), np.float32)
+    run = lambda i: iro.conv1d_dev(xd, CONV["B"], CONV["T"], CONV["C"], dw, CONV["KW"], 1, 1, 3,  # noqa
+                                   bd, False, out)
+    for i in range(max(3, args.warmup)):
+        run(i)
+    ms = max_ranks(timed(stream, run, args.steps) / args.steps)
+    wq = (hw.data, hw.scale, hw.colsum)
+    for b in (xd, bd, out):
+        b.free()
+    dw.free()
+    hw.free()
+    return ms, wq, inp, bias
+
+
+def cpu_conv7_sample(wq, inp, bias, seconds=8.0):
+    """The reference's conv1d_int8_forward (dacvae.c:543-688), product-flag
+    build, over one of the four sequences split into time chunks (one host
+    thread each; a chunk takes its 3-frame halo so its rows see the same
+    inputs, and the rows next to a cut are dropped).  Returns a cpu_baseline
+    dict in TOPS."""
+    import oracle as oracle_mod
+    variant = _ref_kind("codec_fast")
+    if variant is None:
+        return None
+    threads = os.cpu_count() or 1
+    W = oracle_mod.Weight(*wq)
+    x = inp[0]
+    T = x.shape[0]
+    pad = CONV["KW"] // 2
+    bounds = [(T * t // threads, T * (t + 1) // threads) for t in range(threads)]
+
+    def chunk(b):
+        lo, hi = max(0, b[0] - pad), min(T, b[1] + pad)
+        return oracle_mod.ref_conv1d_int8(x[lo:hi], W, CONV["KW"], 1, 1, pad, bias, kind=variant)
+
+    pool = ThreadPoolExecutor(threads)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        list(pool.map(chunk, bounds))
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 20:
+            break
+    pool.shutdown()
+    ops = conv_ops() / CONV["B"] * reps
+    return {"value": round(ops / el / 1e12, 5), "unit": "TOPS", "cores": threads,
+            "kind": "reference", "build": variant, "onemkl": ONEMKL,
+            "sample": f"1 of {CONV['B']} sequences ({T} frames) x {reps}, time chunks over "
+                      f"{threads} threads"}
+
+
+# ---------------------------------------------------------------------------
+# The default run: the headline plus the nested config-3 / config-4 legs.
+
+
+def _gpu_setup(args):
+    import torch
+    import torch.distributed as dist
+    import iro_b200 as iro
+
+    world, rank, local = dist_setup(args.gpus)
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    iro.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_ranks(v):
+        return max_over_ranks(v, dist if world > 1 else None)
+
+    return iro, dist, stream, world, rank, local, barrier, max_ranks
+
+
+def run_ours(args):
+    iro, dist, stream, world, rank, local, barrier, max_ranks = _gpu_setup(args)
+    sampler = ClockSampler(physical_gpu(local)) if local == 0 else None
+    if sampler:
+        sampler.start()
+    blk = leg_block(args, iro, stream, world, max_ranks, barrier)
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]
+    ms_per_step = blk["dev_ms"] / args.steps
+    value = world * OPS_STEP * args.steps / (blk["dev_ms"] * 1e-3) / 1e12
+    k_tops = OPS_W13 / (blk["k_ms"] * 1e-3) / 1e12
+
+    nested = {}
+    case = None
+    if not args.headline_only:
+        dit, _ = leg_dit(args, iro, stream, "cfg3", world, max_ranks, barrier)
+        g_ms, g_ops = leg_dit_gemm(args, iro, stream, "cfg3", max_ranks)
+        g_tops = g_ops / (g_ms * 1e-3) / 1e12
+        dit["roofline"] = {"bound": "tensor", "kernel": "gemm_i8_kernel<256,EPI_GATED> (W1|W3 + "
+                           "silu) at M = 24000, the DiT's largest int8 GEMM",
+                           "achieved": round(g_tops, 1), "peak": round(int8_peak, 1),
+                           "unit": "TFLOP/s", "frac": round(g_tops / int8_peak, 4),
+                           "traffic": profile_traffic("gemm_i8_dit_m24000.md"),
+                           "ms_per_launch": round(g_ms, 4), "ops_per_launch": g_ops}
+        nested["dit"] = dit
+        case = DitCase(iro, "reference", DIT_REQUESTS, seed=35 + rank,
+                       keep_host=(rank == 0 and world == 1 and not args.no_cpu))
+        refd, _ = leg_dit(args, iro, stream, "reference", world, max_ranks, barrier, case=case)
+        nested["dit_ref_dims"] = refd
+        c_ms, wq, cinp, cbias = leg_conv7(args, iro, stream, max_ranks)
+        nested["conv7"] = {"value": round(world * conv_ops() / (c_ms * 1e-3) / 1e12, 2),
+                           "unit": "TOPS", "ms_per_step": round(c_ms, 4),
+                           "frac_int8_peak": round(conv_ops() / (c_ms * 1e-3) / 1e12 / int8_peak,
+                                                   4),
+                           "workload": "cfg4 DACVAE int8 conv1d k7 pad 3, [4,48000,512] -> "
+                                       "[4,48000,512] per GPU, seeded bias",
+                           "ops_per_step": conv_ops()}
+    clocks = sampler.stop() if sampler else None
+
+    # ---- CPU baselines: the reference's own code on this box's host cores ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        _, cpu = cpu_block_steps(steps=1, warmup=1, seconds=args.cpu_seconds)
+        if nested:
+            nested["dit_ref_dims"]["cpu_baseline"] = cpu_dit_sample(case, seconds=10.0)
+            nested["conv7"]["cpu_baseline"] = cpu_conv7_sample(wq, cinp, cbias, seconds=8.0)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": DTYPE,
+        "data": DATA,
+        "config": {"workload": WORKLOAD, "M": M, "D": D, "H": H, "ops_per_step": OPS_STEP,
+                   "global_batch_rows": M * world, "parallelism": f"replicas x{world}",
+                   "launch": "iro_int8_swiglu_dev per step: 4 programmatic dependent launches; "
+                             "the step launches are queued behind a 3 ms device-side hold "
+                             "before the start event",
+                   "l2": f"rotating {NSETS} input+weight sets ({NSETS * 25} MB) > 126 MB L2",
+                   "pct_int8_peak": round(100.0 * value / world / int8_peak, 2),
+                   "parity_rel_err_vs_oracle": blk["rel_err"]},
+        "e2e": {"value": round(blk["e2e_tops"], 3), "unit": "TOPS",
+                "h2d_bytes_per_step": M * D * 4, "d2h_bytes_per_step": M * D * 4,
+                "steps": blk["e2e_steps"],
+                "api": "iro_int8_swiglu_pipe_submit/wait (page-locked host buffers, 3-slot ring)"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_i8_kernel<256,EPI_GATED> (W1|W3 + silu)",
+                     "achieved": round(k_tops, 2), "peak": round(int8_peak, 1),
+                     "unit": "TFLOP/s",
+                     "peak_note": (f"int8 dense = 2 x cuBLAS bf16 burst {pk['bf16_tflops']} TF/s "
+                                   f"(of {pk['source']})"),
+                     "frac": round(k_tops / int8_peak, 4), "traffic": profile_traffic(),
+                     "ms_per_launch": round(blk["k_ms"], 5), "ops_per_launch": OPS_W13,
+                     "launches_timed": blk["kreps"]},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": 4 * args.steps,
+    }
+    line.update(nested)
+    print(json.dumps(line), flush=True)
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU code for this path on the
+    host cores (rank 0 only), on the headline's metric and config -- the full
+    2048-row config-2 block per step -- plus the same nested legs as our
+    line (the reference's dit.c step on a request sample, its conv7 on a
+    frame sample).  Nothing of this repository's library runs here."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    L, kind, variant = _ref_lib()
     threads = os.cpu_count() or 1
-    rows = 256
-    oracle_mod, x, ws, bs = _ref_inputs(rows)
-
-    def run():
-        if L is None:
-            oracle_mod.swiglu(x, *ws, *bs)
-        else:
-            _ref_block(oracle_mod, L, x, ws, bs, threads)
-
-    for _ in range(args.warmup):
-        run()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        run()
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = OPS_STEP * rows / M * args.steps / total / 1e12
+    per, cpu = cpu_block_steps(steps=args.steps, warmup=args.warmup)
+    value = OPS_STEP / per / 1e12
+    nested = {}
+    if not args.headline_only:
+        if _ref_kind("dit_fast"):
+            case = DitCase(None, "reference", DIT_REQUESTS, seed=35, ref_kind=_ref_kind("fast"))
+            d = cpu_dit_sample(case, seconds=10.0)
+            nested["dit_ref_dims"] = {"value": d["value"], "unit": "steps/s",
+                                      "cpu_baseline": d,
+                                      "dims": "d1280/h20x64/mlp3680/rank192"}
+        if _ref_kind("codec_fast"):
+            import oracle as oracle_mod
+            inp, w, bias = _conv_inputs()
+            W = oracle_mod.ref_weight_quantize(w, kind=_ref_kind("fast"))
+            cv = cpu_conv7_sample((W.data, W.scale, W.colsum), inp, bias, seconds=8.0)
+            nested["conv7"] = {"value": cv["value"], "unit": "TOPS", "cpu_baseline": cv}
     line = {
         "metric": METRIC, "value": round(value, 5), "unit": "TOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 (u8 x s8 -> s32, fp32 dequant epilogue)",
-        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) biases)",
-        "config": {"workload": WORKLOAD, "M": M, "D": D, "H": H, "sample_rows": rows,
+        "ms_per_step": round(1e3 * per, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": DATA,
+        "config": {"workload": WORKLOAD, "M": M, "D": D, "H": H, "ops_per_step": OPS_STEP,
                    "parallelism": f"{threads} host threads (row slices)"},
         "impl": "reference",
-        "cpu_baseline": {"value": round(value, 5), "unit": "TOPS", "cores": threads, "kind": kind,
-                         "build": variant or "oracle port (-O2 IEEE)",
-                         "sample": f"{rows} of {M} rows of the cfg2 block per step"},
+        "cpu_baseline": cpu,
         "e2e": {"value": round(value, 5), "unit": "TOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    line.update(nested)
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Standalone workloads.
+
+
+def run_dit(args):
+    """BASELINE config 3 alone (or --dit-dims reference): DiT Euler steps."""
+    iro, dist, stream, world, rank, local, barrier, max_ranks = _gpu_setup(args)
+    clocks = ClockSampler(physical_gpu(local))
+    clocks.start()
+    res, _ = leg_dit(args, iro, stream, args.dit_dims, world, max_ranks, barrier)
+    res["clocks"] = clocks.stop()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    res.update({"metric": "DiT Euler steps/sec", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "dtype": "int8 GEMMs, tf32 attention (fp32 accumulate)",
+                "data": "synthetic (random-init weights, N(0,1) latents)"})
+    print(json.dumps(res), flush=True)
+
+
+def run_conv7(args):
+    """BASELINE config 4 alone: the codec's int8 kernel-7 conv."""
+    iro, dist, stream, world, rank, local, barrier, max_ranks = _gpu_setup(args)
+    ms, wq, inp, bias = leg_conv7(args, iro, stream, max_ranks)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"metric": "int8 conv7 TOPS",
+                          "value": round(world * conv_ops() / ms / 1e9, 2),
+                          "unit": "TOPS", "ms_per_step": round(ms, 4), "steps": args.steps,
+                          "n_gpus": world,
+                          "config": {"workload": "cfg4 DACVAE int8 conv1d k7 [4,48000,512]->"
+                                                 "[4,48000,512] per GPU",
+                                     "ops_per_step": conv_ops()}}), flush=True)
+
+
+SWEEP_M = (64, 256, 4096, 65536)
+SWEEP_N = (1024, 2816, 4096)
+SWEEP_REQUESTS = (1, 8, 64, 512)
+
+
+def run_sweep(args):
+    """BASELINE config 5.  (ii) The isolated int8 linear (quantised x in,
+    fp32 y = dequant + bias out; iro_int8_linear_dev) at M in {64, 256, 4096,
+    65536} x N in {1024, 2816, 4096}, K = 1024, inputs with config 1's
+    distributions: TOPS, fraction of the int8 peak and HBM GB/s of the
+    algorithmic bytes (u8 A + s8 W + fp32 y) against the measured copy
+    bandwidth; plus config 1 through the host-pointer ops.h calls.  (i) The
+    8-step Euler sampler with the reference's CFG window (four rows while t
+    in [0.5, 1], the conditional row after; sampler.c:248-250,
+    generate.c:416-422) over 1, 8, 64 and 512 concurrent requests at config
+    3's dimensions, whole requests per GPU (shard_requests); each GPU runs
+    its requests in calls of at most 8 (one call's workspace), the whole
+    batch timed as a serving loop would run it.  One JSON line per point,
+    then a summary line."""
+    iro, dist, stream, world, rank, local, barrier, max_ranks = _gpu_setup(args)
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]
+    rng = np.random.default_rng(5)
+    K = 1024
+    out = []
+    for N in (SWEEP_N if rank == 0 else ()):
+        w = iro.DevWeight.upload(iro.HostWeight(rng.standard_normal((N, K), dtype=np.float32) *
+                                                np.float32(0.02)),
+                                 rng.standard_normal(N, dtype=np.float32) * np.float32(0.01))
+        for Mi in SWEEP_M:
+            x = rng.standard_normal((Mi, K), dtype=np.float32)
+            x[rng.random((Mi, K)) < 0.001] *= 20.0
+            xd = iro.DevBuf.from_host(x)
+            q, s_, z = iro.DevBuf((Mi, K), np.uint8), iro.DevBuf(Mi, np.float32), \
+                iro.DevBuf(Mi, np.int32)
+            iro.quantize_rows_dev(xd, Mi, K, q, s_, z)
+            # Several outputs in rotation so the timed launches write > 126 MB.
+            ybytes = Mi * N * 4
+            ncopy = max(1, min(8, (256 << 20) // max(ybytes, 1)))
+            ys = [iro.DevBuf((Mi, N), np.float32) for _ in range(ncopy)]
+            run = lambda i: iro.linear_dev(q, s_, z, w, None, ys[i % ncopy], Mi)  # noqa: E731
+            for i in range(5):
+                run(i)
+            reps = max(20, min(2000, int(2e11 / max(1.0, 2.0 * Mi * N * K))))
+            ms = timed(stream, run, reps) / reps
+            ops = 2.0 * Mi * N * K
+            byts = Mi * K + N * K + 4 * Mi * N + 8 * Mi + 12 * N
+            rec = {"point": "gemm", "M": Mi, "N": N, "K": K, "us": round(ms * 1e3, 2),
+                   "tops": round(ops / ms / 1e9, 1),
+                   "frac_int8_peak": round(ops / ms / 1e9 / int8_peak, 4),
+                   "hbm_gbs": round(byts / ms / 1e6, 1),
+                   "frac_hbm": round(byts / ms / 1e6 / pk["hbm_gbs"], 4),
+                   "bound": "tensor" if ops / int8_peak > byts / pk["hbm_gbs"] / 1e3 else "hbm"}
+            print(json.dumps(rec), flush=True)
+            out.append(rec)
+            for b in (xd, q, s_, z, *ys):
+                b.free()
+        w.free()
+    if rank == 0:
+        # Config 1 through the ops.h host-pointer calls an unchanged dit.c
+        # makes: iro_int8_quantize_rows then iro_int8_linear_ex, each copying
+        # its operands in and its result (y and the raw int32 sums) out.
+        M1, N1 = 512, 4096
+        x1 = rng.standard_normal((M1, K), dtype=np.float32)
+        x1[rng.random((M1, K)) < 0.001] *= 20.0
+        hw1 = iro.HostWeight(rng.standard_normal((N1, K), dtype=np.float32) * np.float32(0.02))
+        b1 = rng.standard_normal(N1, dtype=np.float32) * np.float32(0.01)
+        y1 = np.zeros((M1, N1), np.float32)
+        for _ in range(5):
+            q1, s1, z1 = iro.quantize_rows(x1)
+            iro.linear_ex(q1, s1, z1, hw1, b1, y=y1)
+        reps = 50
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            q1, s1, z1 = iro.quantize_rows(x1)
+            iro.linear_ex(q1, s1, z1, hw1, b1, y=y1)
+        per = (time.perf_counter() - t0) / reps
+        rec = {"point": "host_api_cfg1", "M": M1, "N": N1, "K": K,
+               "us_per_call": round(per * 1e6, 1),
+               "tops": round(2.0 * M1 * N1 * K / per / 1e12, 3),
+               "api": "iro_int8_quantize_rows + iro_int8_linear_ex (host pointers: x, q, y and "
+                      "the M x N int32 work cross PCIe each call)"}
+        print(json.dumps(rec), flush=True)
+        out.append(rec)
+        hw1.free()
+
+    # (i) the serving sweep of the 8-step sampler.
+    import torch
+    case = DitCase(iro, "cfg3", DIT_REQUESTS, seed=77)
+    ws = iro.DevBuf(case.model.workspace_bytes(case.R, DIT_CFG, DIT_S, DIT_C, steps=8), np.uint8)
+    for R in SWEEP_REQUESTS:
+        lo, hi = shard_requests(R, world, rank)
+        mine = hi - lo
+        chunks = [min(DIT_REQUESTS, mine - i) for i in range(0, mine, DIT_REQUESTS)]
+        states = [torch.from_numpy(np.ascontiguousarray(case.state0[:c])).cuda()
+                  for c in chunks]
+
+        def sample_all(_):
+            for c, st in zip(chunks, states):
+                case.model.sample_euler(st, c, DIT_CFG, DIT_S, 8, 0.999, 0.5, 1.0, DIT_SCALES,
+                                        case.ckd, case.cvd, case.maskd, DIT_C, workspace=ws)
+
+        sample_all(0)
+        barrier()
+        ms = max_ranks(timed(stream, sample_all, 1))
+        rows = sum(r * R * DIT_S for r in [4] * 4 + [1] * 4)
+        rec = {"point": "sampler", "requests": R, "gpus": world,
+               "ms_per_request_batch": round(ms, 2),
+               "steps_per_s": round(8 * 1000.0 / ms, 2),
+               "requests_per_s": round(R * 1000.0 / ms, 2),
+               "rows_per_s": round(rows * 1000.0 / ms, 1),
+               "rows_per_linear_per_gpu": [4 * mine * DIT_S, mine * DIT_S]}
+        if rank == 0:
+            print(json.dumps(rec), flush=True)
+        out.append(rec)
+    ws.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({"metric": "config-5 sweep", "points": len(out),
+                      "peaks": {"int8_tops": int8_peak, "hbm_gbs": pk["hbm_gbs"],
+                                "source": pk["source"]}}), flush=True)
 
 
 def run_profile_case(args):
@@ -593,10 +1139,8 @@ def run_profile_case(args):
         print(f"profile case ditblock: {args.warmup + args.steps} blocks ok")
         return
 
-    global NSETS
-    NSETS = 1
     iro.init(0)
-    s = make_sets(np.random.default_rng(5), iro, oracle_mod)[0]
+    s = make_sets(np.random.default_rng(5), iro, nsets=1)[0]
     ws = iro.DevBuf(iro.swiglu_workspace_bytes(M, D, H, False), np.uint8)
     qh = iro.DevBuf((M, H), np.uint8)
     sh = iro.DevBuf(M, np.float32)
@@ -617,42 +1161,6 @@ def run_profile_case(args):
     print(f"profile case {args.profile}: {args.warmup + args.steps} launches ok")
 
 
-def run_conv7(args):
-    """the codec's int8 kernel-7 conv over 4 x 48000 frames,
-    512 -> 512 channels (device-resident; one JSON line)."""
-    import torch
-    import iro_b200 as iro
-    import oracle as oracle_mod
-
-    B, T, C, N, KW = 4, 48000, 512, 512, 7
-    iro.init(0)
-    torch.cuda.set_device(0)
-    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
-    rng = np.random.default_rng(44)
-    inp = rng.standard_normal((B, T, C), dtype=np.float32) * np.float32(0.5)
-    w = rng.standard_normal((N, KW * C), dtype=np.float32) * np.float32(0.02)
-    bias = rng.standard_normal(N, dtype=np.float32) * np.float32(0.01)
-    hw = iro.HostWeight(w)
-    dw = iro.DevWeight.upload(hw)
-    xd = iro.DevBuf.from_host(inp)
-    bd = iro.DevBuf.from_host(bias)
-    out = iro.DevBuf((B, T, N), np.float32)
-    for _ in range(args.warmup):
-        iro.conv1d_dev(xd, B, T, C, dw, KW, 1, 1, 3, bd, False, out)
-    iro.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        iro.conv1d_dev(xd, B, T, C, dw, KW, 1, 1, 3, bd, False, out)
-    e1.record(stream)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    ops = 2.0 * B * T * N * KW * C
-    print(json.dumps({"metric": "int8 conv7 TOPS", "value": round(ops / ms / 1e9, 2),
-                      "unit": "TOPS", "ms_per_step": round(ms, 4), "steps": args.steps,
-                      "config": {"workload": "cfg4 DACVAE int8 conv1d k7 [4,48000,512]->[4,48000,512]",
-                                 "ops_per_step": ops}}), flush=True)
 
 
 def run_init(args):
@@ -740,140 +1248,22 @@ def run_init(args):
                                  "fp32_bytes": total_bytes}}), flush=True)
 
 
-def _count_kernels(fn):
-    """Kernel launches of fn() seen by the CUDA activity profiler (untimed)."""
-    try:
-        import torch
-        from torch.profiler import ProfilerActivity, profile
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fn()
-            torch.cuda.synchronize()
-        return sum(1 for e in prof.events()
-                   if getattr(e, "device_type", None) is not None
-                   and str(e.device_type).endswith("CUDA") and "emcpy" not in e.name
-                   and "emset" not in e.name)
-    except Exception:  # noqa: BLE001 - the count is informational
-        return None
-
-
-def run_dit(args):
-    """whole DiT Euler steps at the config's dimensions
-    (12 blocks, d_model 1024, 16 heads of 64, SwiGLU 2816, AdaLN rank 192),
-    8 requests x 4 CFG rows (cond, text, speaker and caption uncond) x 750
-    latent frames = 24000 rows per linear, 128 context tokens per request
-    (their per-layer K/V precomputed, as the sampler's KV-cache prep does
-    once per request, sampler.c:205-237).  A step is one Euler step through
-    iro_dit_sample_euler_dev: conditioner, input projection, 12 blocks,
-    output head, CFG-guided update.  Random-init weights quantised by the
-    library's own quantiser; N(0,1) latents; CFG window open for every step.
-    The weights (164 MB of int8) and every activation tensor (98 MB each)
-    exceed the 126 MB L2, so no flush is needed between steps."""
-    import torch
-    import iro_b200 as iro
-
-    D, NH, H, RK, L = 1024, 16, 2816, 192, 12
-    R, CFG, S, Cx = 8, 4, 750, 128
-    if args.dit_dims == "reference":
-        D, NH, H = 1280, 20, 3680
-    iro.init(0)
-    torch.cuda.set_device(0)
-    stream = torch.cuda.ExternalStream(iro.lib().iro_cuda_stream())
-    rng = np.random.default_rng(33)
-    f = lambda *sh, s=1.0: (rng.standard_normal(sh, dtype=np.float32) * np.float32(s))
-    blocks = []
-    for _ in range(L):
-        adaln = []
-        for _ in range(6):
-            adaln += [f(RK, D, s=0.03), f(D, RK, s=0.03), f(D, s=0.02)]
-        ws = [iro.HostWeight(f(D, D, s=0.03)) for _ in range(5)]
-        ws += [iro.HostWeight(f(H, D, s=0.03)), iro.HostWeight(f(H, D, s=0.03)),
-               iro.HostWeight(f(D, H, s=0.02))]
-        blocks.append(iro.DiTBlock(adaln, 1.0 + f(D, s=0.1), 1.0 + f(D, s=0.1), *ws,
-                                   model_dim=D, heads=NH, rank=RK, mlp_dim=H))
-    model = iro.DiTModel(blocks, f(D, 512, s=0.04), f(D, D, s=0.03), f(3 * D, D, s=0.03),
-                         f(D, 32, s=0.15), f(D, s=0.02), 1.0 + f(D, s=0.1), f(32, D, s=0.03),
-                         f(32, s=0.02))
-    ctx_k = [iro.DevBuf.from_host(f(R, Cx, D)) for _ in range(L)]
-    ctx_v = [iro.DevBuf.from_host(f(R, Cx, D)) for _ in range(L)]
-    mask = (rng.random((R * CFG, Cx)) < 0.9).astype(np.uint8)
-    mask[:, 0] = 1
-    maskd = iro.DevBuf.from_host(mask)
-    ws = iro.DevBuf(model.workspace_bytes(R, CFG, S, Cx, steps=max(args.steps, args.warmup, 2)),
-                    np.uint8)
-    state0 = f(R, S, 32)
-    host_in = torch.from_numpy(state0).pin_memory()
-    host_out = torch.empty_like(host_in).pin_memory()
-    state = torch.empty(host_in.shape, dtype=torch.float32, device="cuda")
-    scales = [2.0, 1.5, 1.0]
-
-    def sample(k):
-        model.sample_euler(state, R, CFG, S, k, 1.0, 0.0, 1.0, scales, ctx_k, ctx_v, maskd, Cx,
-                           workspace=ws)
-
-    with torch.cuda.stream(stream):
-        state.copy_(host_in, non_blocking=True)
-    sample(args.warmup)
-    iro.synchronize()
-    n1 = n2 = None
-    if not args.no_count:
-        n1 = _count_kernels(lambda: sample(1))
-        n2 = _count_kernels(lambda: sample(2))
-    clocks = ClockSampler(physical_gpu(0))
-    clocks.start()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    sample(args.steps)
-    e1.record(stream)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    # End to end: the latents in from pinned host memory, the sampled
-    # latents back, inside the timed region.
-    e0.record(stream)
-    with torch.cuda.stream(stream):
-        state.copy_(host_in, non_blocking=True)
-    sample(args.steps)
-    with torch.cuda.stream(stream):
-        host_out.copy_(state, non_blocking=True)
-    e1.record(stream)
-    e1.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
-    clk = clocks.stop()
-    M = R * CFG * S
-    gemm_ops = 2.0 * M * L * (4 * D * D + D * D + 2 * H * D + H * D)
-    attn_flops = 4.0 * M * L * NH * 64 * (S + Cx)
-    launches = None
-    if n1 is not None and n2 is not None:
-        launches = (2 * n1 - n2) + args.steps * (n2 - n1)
-    dims = f"d{D}/h{NH}x64/mlp{H}/rank{RK}"
-    print(json.dumps({
-        "metric": "DiT Euler steps/sec", "value": round(1000.0 / ms, 3), "unit": "steps/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMMs, tf32 attention (fp32 accumulate)",
-        "data": "synthetic (random-init weights, N(0,1) latents)",
-        "e2e": {"value": round(1000.0 / ms_e2e, 3), "unit": "steps/s",
-                "h2d_bytes_per_step": host_in.numel() * 4 / args.steps,
-                "d2h_bytes_per_step": host_out.numel() * 4 / args.steps},
-        "int8_linear_tops": round(gemm_ops / ms / 1e9, 1),
-        "attention_tflop_per_step": round(attn_flops / 1e12, 3),
-        "gpu_launches": launches, "launches_per_step": None if launches is None else n2 - n1,
-        "clocks": clk,
-        "config": {"workload": f"cfg3 DiT {L} blocks {dims}, {R} requests x {CFG} CFG rows x "
-                               f"{S} frames ({M} rows/linear), {Cx} context tokens",
-                   "l2": "working set > L2 (164 MB int8 weights, 98 MB activations)",
-                   "int8_ops_per_step": gemm_ops}}), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["swiglu", "conv7", "init", "dit"], default="swiglu",
-                    help="swiglu = BASELINE config 2 (the bench line); conv7 = config 4")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="only the config-2 headline (no nested DiT / conv7 legs)")
+    ap.add_argument("--workload", choices=["default", "conv7", "init", "dit", "sweep"],
+                    default="default",
+                    help="default = the headline line (config 2 + nested configs 3 and 4); "
+                         "dit = config 3 alone; conv7 = config 4 alone; sweep = config 5")
     ap.add_argument("--profile", choices=["gated", "w2", "quant", "block", "conv7", "ditblock",
                                           "dit_qkvg", "dit_w2", "dit_w13"],
                     help="run a short fixed launch sequence for ncu instead of the benchmark")
@@ -881,20 +1271,22 @@ def main():
                     help="dit workload: config 3's d1024/16 heads/2816, or the reference "
                          "checkpoint's d1280/20 heads/3680")
     ap.add_argument("--no-count", action="store_true",
-                    help="dit workload: skip the profiler-based launch count (for ncu runs)")
+                    help="skip the profiler-based DiT launch count (for ncu runs)")
     args = ap.parse_args()
     if args.warmup < 3 and not args.profile:
         raise SystemExit("--warmup must be >= 3")
     if args.profile:
         run_profile_case(args)
-    elif args.workload == "init" and args.impl == "ours":
-        run_init(args)
-    elif args.workload == "dit" and args.impl == "ours":
-        run_dit(args)
-    elif args.workload == "conv7" and args.impl == "ours":
-        run_conv7(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.workload == "init":
+        run_init(args)
+    elif args.workload == "dit":
+        run_dit(args)
+    elif args.workload == "conv7":
+        run_conv7(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 

@@ -45,7 +45,7 @@ def _worker(rank, world, port, out_dir):
         dist.all_gather_object(sizes, (lo, hi))
         parts = [None] * world
         dist.all_gather_object(parts, y)
-        t = bench.max_over_ranks_cpu(float(rank + 1) * 0.5, dist)
+        t = bench.max_over_ranks(float(rank + 1) * 0.5, dist)
         if rank == 0:
             np.savez(os.path.join(out_dir, "r.npz"), y=np.concatenate(parts), t=t,
                      cover=np.array([v for (a, b) in sizes for v in range(a, b)]))
