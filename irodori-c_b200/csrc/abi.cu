@@ -536,13 +536,7 @@ int iro_int8_dev_weight_gated_pair(IroInt8DevWeight* dst, const IroInt8Weight* w
   if (!dst || !w1 || !w3 || !w1->data || !w3->data || w1->N != w3->N || w1->K != w3->K ||
       w1->N <= 0 || w1->K <= 0)
     return IRO_ERR_INVALID;
-  // Pair-block width: 128 (256-column tiles) or 64 (128-column tiles, twice
-  // the tiles: finer load balance for the epilogue-bound gated GEMM).
-  // IRO_GATED_PAIR selects it; the default is 128.
-  int pair = 128;
-  if (const char* ev = getenv("IRO_GATED_PAIR"))
-    if (atoi(ev) == 64) pair = 64;
-  const int H = w1->N, K = w1->K;
+  const int pair = 128, H = w1->N, K = w1->K;
   const int Hp = round_up(H, pair);
   int st;
   if (!ctx_current(&st)) return st;
