@@ -49,11 +49,15 @@ constexpr int kSmemMax = 232448;  // 227 KB opt-in per CTA
 constexpr int kStgBytes = 32 * kChunk * 4;  // one staging tile: 32 rows x 16 fp32
 constexpr int kStgBufs = 2;                 // staging tiles per epilogue warp
 
-template <int BN, int EPI>
+// PAIR: a two-CTA cluster shares one tcgen05.mma.cta_group::2 of M = 256
+// (each CTA's 128 A rows) x N = BN; each CTA stages only half of B (BN/2
+// rows), so a CTA's operand bytes per output drop by a third at BN = 256.
+template <int BN, int EPI, bool PAIR = false>
 struct Cfg {
   static constexpr int NA = (EPI == EPI_DUAL) ? 2 : 1;
   static constexpr int A_BYTES = BM * BKB;
-  static constexpr int B_BYTES = BN * BKB;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B rows this CTA stages
+  static constexpr int B_BYTES = B_ROWS * BKB;
   static constexpr int STAGE = NA * A_BYTES + B_BYTES;
   static constexpr int STG = kEpiWarps * kStgBufs * kStgBytes;
   static constexpr int PARAMS = 2 * 3 * BN * 4;  // double-buffered colsum/scale/bias
@@ -68,7 +72,8 @@ struct Cfg {
                                    : (2 * ACC_COLS) <= 256 ? 256
                                                            : 512;
   static constexpr int SMEM = STAGES * STAGE + FIXED;
-  static constexpr uint32_t IDESC = idesc_i8(BM, BN, 0);
+  static constexpr uint32_t IDESC = idesc_i8(PAIR ? 2 * BM : BM, BN, 0);
+  static_assert(!PAIR || EPI != EPI_DUAL, "the two-accumulator form runs on one CTA");
   static_assert(2 * ACC_COLS <= 512, "TMEM holds 512 columns");
   static_assert(STAGES >= 2, "pipeline needs two stages");
   static_assert(SMEM <= kSmemMax, "shared memory budget");
@@ -134,18 +139,123 @@ __device__ __forceinline__ void trace_mark(const GemmParams& p, int slot) {
   if (p.trace) p.trace[blockIdx.x * TR_SLOTS + slot] = globaltimer_ns();
 }
 
+// ---- CTA pairs (two-CTA clusters, tcgen05 cta_group::2), no multicast loads.
+
+__device__ __forceinline__ uint32_t pair_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void pair_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t pair_addr(const void* ptr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(ptr)), "r"(rank));
+  return r;
+}
+
+// Bounded wait with cluster-scope acquire, for phases completed by the peer
+// CTA's arrivals (its TMEM reads must be ordered before the next MMAs).
+__device__ __forceinline__ bool pair_wait(uint64_t* bar, uint32_t parity, DevError* err,
+                                          int where, volatile int* abort_flag,
+                                          uint64_t limit_ns) {
+  auto poll = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+  };
+  if (poll()) return true;
+  const long long t0 = clock64();
+  const long long limit_cycles = (long long)(limit_ns * 2ull);
+  while (!poll()) {
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (clock64() - t0 > limit_cycles) {
+      report_error(err, IRO_ERR_DEVICE_TIMEOUT, where);
+      if (abort_flag != nullptr) *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void pair_arrive(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// TMA tile load into this CTA's shared memory, completion counted on an
+// mbarrier of either CTA of the pair (`cluster_bar`, a shared::cluster
+// address).  Not a multicast load.
+__device__ __forceinline__ void pair_tma_load_2d(void* dst, const CUtensorMap* map,
+                                                 uint32_t cluster_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[smem, 128 rows per CTA] . B[smem, BN/2 rows per
+// CTA]^T, kind::i8, M = 256, issued by the leader CTA.
+__device__ __forceinline__ void pair_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` (same offset) in both CTAs of the pair once the pair MMAs
+// issued so far have completed.  The multicast here is the completion
+// signal's, not a load's.
+__device__ __forceinline__ void pair_commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+// The same on this (the leader) CTA's barrier only.
+__device__ __forceinline__ void pair_commit_local(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
 // Output tensor maps (row-major fp32, box 32 rows x 16 columns, 64-byte swizzle).
 struct OutMaps {
   CUtensorMap m[4];
 };
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ OutMaps tmO, const GemmParams p) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, PAIR>;
+  // PAIR: CTAs 2k and 2k+1 form a cluster that works through pair tiles
+  // (2 x 128 rows); rank r owns row block 2 * mb + r of pair tile mb.  The
+  // leader (rank 0) issues the MMAs and holds the stage and accumulator
+  // barriers they wait on.
+  const uint32_t rank = PAIR ? pair_rank() : 0u;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -174,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], kEpiWarps);
+      mbar_init(&tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     for (int i = 0; i < 2 * kEpiWarps; i++) mbar_init(&xbar[i], 1);
     mbar_init(drain, 1);
@@ -187,11 +297,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (EPI == EPI_DUAL || EPI == EPI_DUAL2) tma_prefetch_desc(&tmA2);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(C::TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) pair_sync();  // the leader's barriers exist before the peer signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Everything above overlaps the previous kernel's tail under a
@@ -206,9 +325,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       long long armed = 0;  // stages armed so far (loads issued)
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < p.num_tiles; tile += tstep) {
         int mb, nb;
         tile_coords(p, tile, mb, nb);
+        if (PAIR) mb = 2 * mb + (int)rank;
         for (int kb = 0; kb < p.num_kb; kb++) {
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u, p.err, 1, abort_flag, p.limit_ns)) {
             ok = false;
@@ -217,6 +337,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           armed++;
           uint8_t* sa = smem + s * C::STAGE;
           uint8_t* sb = sa + C::NA * C::A_BYTES;
+          if (PAIR) {
+            // Both CTAs' A rows and B halves complete on the leader's full[s],
+            // which the leader arms with the pair's bytes.
+            const uint32_t fb = pair_addr(&full[s], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE);
+            if (EPI == EPI_DUAL2) {
+              pair_tma_load_2d(sa, &tmA, fb, kb * BKB, mb * kHalfM);
+              pair_tma_load_2d(sa + kHalfM * BKB, &tmA2, fb, kb * BKB, mb * kHalfM);
+            } else {
+              pair_tma_load_2d(sa, &tmA, fb, kb * BKB, mb * BM);
+            }
+            pair_tma_load_2d(sb, &tmB, fb, kb * BKB, nb * BN + (int)rank * C::B_ROWS);
+            if (tile == tile0 && kb == 0) trace_mark(p, TR_TMA0);
+            if (++s == C::STAGES) {
+              s = 0;
+              ph ^= 1u;
+            }
+            continue;
+          }
           mbar_arrive_expect_tx(&full[s], C::STAGE);
           if (EPI == EPI_DUAL2) {
             // Rows 0-63 of the A tile: term 1 of output rows mb*64..; rows
@@ -228,18 +367,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (EPI == EPI_DUAL) tma_load_2d(sa + C::A_BYTES, &tmA2, &full[s], kb * BKB, mb * BM);
           tma_load_2d(sb, &tmB, &full[s], kb * BKB, nb * BN);
-          if (tile == (int)blockIdx.x && kb == 0) trace_mark(p, TR_TMA0);
+          if (tile == tile0 && kb == 0) trace_mark(p, TR_TMA0);
           if (++s == C::STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
       }
-      if (!ok) {
+      if (!ok && rank == 0) {
         // A wait gave up: no load may still be landing in shared memory when
         // the CTA exits.  Wait (bounded, regardless of the abort flag) for
         // the last armed phase of every stage; in the normal path the MMA
-        // warp has consumed them all.
+        // warp has consumed them all.  (A pair's phases, counted on the
+        // leader, include the peer's loads; the peer leaves only after the
+        // closing cluster barrier.)
         for (int st = 0; st < C::STAGES && st < armed; st++) {
           const long long uses = (armed - 1 - st) / C::STAGES + 1;
           mbar_wait_bounded(&full[st], (uint32_t)((uses - 1) & 1), p.err, 13, nullptr,
@@ -250,14 +391,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        if (!mbar_wait_bounded(&tempty[acc], aph ^ 1u, p.err, 2, abort_flag, p.limit_ns)) {
+      for (int tile = tile0; ok && tile < p.num_tiles; tile += tstep) {
+        const bool free_acc =
+            PAIR ? pair_wait(&tempty[acc], aph ^ 1u, p.err, 2, abort_flag, p.limit_ns)
+                 : mbar_wait_bounded(&tempty[acc], aph ^ 1u, p.err, 2, abort_flag, p.limit_ns);
+        if (!free_acc) {
           ok = false;
           break;
         }
@@ -269,33 +413,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          if (tile == (int)blockIdx.x && kb == 0) trace_mark(p, TR_FULL0);
+          if (tile == tile0 && kb == 0) trace_mark(p, TR_FULL0);
           const uint32_t a_addr = smem_u32(smem + s * C::STAGE);
           const uint32_t b_addr = a_addr + C::NA * C::A_BYTES;
 #pragma unroll
           for (int j = 0; j < BKB / 32; j++) {
             const uint64_t bd = sw128_desc(b_addr + 32 * j);
             const uint32_t accum = (kb > 0 || j > 0) ? 1u : 0u;
-            mma_i8(d, sw128_desc(a_addr + 32 * j), bd, C::IDESC, accum);
-            if (EPI == EPI_DUAL)
-              mma_i8(d + BN, sw128_desc(a_addr + C::A_BYTES + 32 * j), bd, C::IDESC, accum);
+            if (PAIR) {
+              pair_mma_i8(d, sw128_desc(a_addr + 32 * j), bd, C::IDESC, accum);
+            } else {
+              mma_i8(d, sw128_desc(a_addr + 32 * j), bd, C::IDESC, accum);
+              if (EPI == EPI_DUAL)
+                mma_i8(d + BN, sw128_desc(a_addr + C::A_BYTES + 32 * j), bd, C::IDESC, accum);
+            }
           }
-          mma_commit(&empty[s]);
+          if (PAIR) pair_commit_both(&empty[s]);
+          else mma_commit(&empty[s]);
           if (++s == C::STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
-        if (tile == (int)blockIdx.x) trace_mark(p, TR_MMA_END0);
+        if (PAIR) pair_commit_both(&tfull[acc]);
+        else mma_commit(&tfull[acc]);
+        if (tile == tile0) trace_mark(p, TR_MMA_END0);
         acc ^= 1;
         if (acc == 0) aph ^= 1u;
       }
       if (!ok) {
         // MMAs of an unfinished tile may still run: wait (bounded) for all of
         // them before TMEM is freed.
-        mma_commit(drain);
+        if (PAIR) pair_commit_local(drain);
+        else mma_commit(drain);
         mbar_wait_bounded(drain, 0, p.err, 14, nullptr, p.limit_ns);
       }
     }
@@ -324,6 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto fetch = [&](int t) {
       int mb, nb;
       tile_coords(p, t, mb, nb);
+      if (PAIR) mb = 2 * mb + (int)rank;
       const int n = nb * BN + et;
       const bool ok = et < BN && n < p.N;
       pf.cs = ok ? __ldg(p.wcolsum + n) : 0;
@@ -345,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pf.sx2 = (EPI == EPI_DUAL && rok) ? __ldg(p.sx2 + r) : 0.0f;
       pf.zp2 = (EPI == EPI_DUAL && rok) ? __ldg(p.zp2 + r) : 0;
     };
-    if ((int)blockIdx.x < p.num_tiles) fetch(blockIdx.x);
+    if (tile0 < p.num_tiles) fetch(tile0);
     // Old output values (y += ..., or the gated residual) come in by TMA
     // tile loads into the staging buffer that the chunk's result then goes
     // out from: one bulk copy per 32 x 16 chunk instead of per-lane row
@@ -381,9 +533,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       xfail = __any_sync(0xffffffffu, !ok);
       return !xfail;
     };
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    // The leader's accumulator-free barrier (the MMA warp waits on it).
+    const uint32_t tempty_leader0 = PAIR ? pair_addr(&tempty[0], 0) : 0u;
+    for (int tile = tile0; tile < p.num_tiles; tile += tstep) {
       int mb, nb;
       tile_coords(p, tile, mb, nb);
+      if (PAIR) mb = 2 * mb + (int)rank;
       // Stage this tile's per-column parameters (the buffer was last read by
       // the tile before the previous one, which every warp has finished).
       float* pc = prm + pbuf * 3 * BN;
@@ -402,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int zp = pf.zp;
       const float sx2 = pf.sx2;
       const int zp2 = pf.zp2;
-      if (tile + (int)gridDim.x < p.num_tiles) fetch(tile + (int)gridDim.x);
+      if (tile + tstep < p.num_tiles) fetch(tile + tstep);
       // The first chunk's old values load while the accumulator fills.
       // Quadrants wholly below the last row load nothing (and store nothing).
       const bool xrow = xload && row0 < p.M;
@@ -416,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      if (e == 0 && lane == 0 && tile == (int)blockIdx.x) trace_mark(p, TR_EPI0);
+      if (e == 0 && lane == 0 && tile == tile0) trace_mark(p, TR_EPI0);
       const uint32_t tbase =
           tmem_base + (uint32_t)(acc * C::ACC_COLS) + ((uint32_t)(quad * 32) << 16);
 
@@ -763,8 +918,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (e == 0 && lane == 0 && tile == (int)blockIdx.x) trace_mark(p, TR_EPI_END0);
+      if (lane == 0) {
+        if (PAIR) pair_arrive(tempty_leader0 + 8u * (uint32_t)acc);
+        else mbar_arrive(&tempty[acc]);
+      }
+      if (e == 0 && lane == 0 && tile == tile0) trace_mark(p, TR_EPI_END0);
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
       pbuf ^= 1;
@@ -774,14 +932,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
+  // A pair: the leader's MMAs no longer read this CTA's shared memory, and
+  // every remote arrival has landed, before either CTA frees anything.
+  if (PAIR) pair_sync();
   if (threadIdx.x == 0 && p.trace) {
     trace_mark(p, TR_EXIT);
     p.trace[blockIdx.x * TR_SLOTS + TR_TILES] =
-        (unsigned long long)((p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+        (unsigned long long)((p.num_tiles - tile0 + tstep - 1) / tstep);
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(C::TMEM_COLS)
+                   : "memory");
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -824,12 +990,12 @@ static bool out_tma_ok(const float* base, int ld) {
   return base != nullptr && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (ld & 3) == 0;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool PAIR = false>
 static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStream_t s) {
-  using C = Cfg<BN, EPI>;
+  using C = Cfg<BN, EPI, PAIR>;
   static bool attr_done[64] = {false};
   if (!attr_done[c->device]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, PAIR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return map_cuda(e);
     attr_done[c->device] = true;
@@ -839,7 +1005,8 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
   constexpr int ABOX = EPI == EPI_DUAL2 ? kHalfM : BM;  // A rows per TMA box
   int st = make_tmap_u8(&ta, r.a, (uint64_t)w->K, (uint64_t)r.M, (uint64_t)r.lda, BKB, ABOX);
   if (st) return st;
-  st = make_tmap_u8(&tb, w->data, (uint64_t)w->K, (uint64_t)w->N, (uint64_t)w->ld, BKB, BN);
+  st = make_tmap_u8(&tb, w->data, (uint64_t)w->K, (uint64_t)w->N, (uint64_t)w->ld, BKB,
+                    C::B_ROWS);
   if (st) return st;
   if (EPI == EPI_DUAL || EPI == EPI_DUAL2) {
     st = make_tmap_u8(&ta2, r.a2, (uint64_t)w->K, (uint64_t)r.M, (uint64_t)r.lda, BKB, ABOX);
@@ -878,7 +1045,9 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
   }
   if (st) return st;
   p.tma_out = tma ? 1 : 0;
-  p.tiles_m = cdiv(r.M, EPI == EPI_DUAL2 ? kHalfM : BM);
+  // Output rows per tile: 128 (64 for the stacked two-term form), twice that
+  // for a pair tile.
+  p.tiles_m = cdiv(r.M, (EPI == EPI_DUAL2 ? kHalfM : BM) * (PAIR ? 2 : 1));
   p.tiles_n = cdiv(w->N, BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   {
@@ -886,19 +1055,67 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
     const size_t b_bytes = (size_t)w->N * w->K;
     p.n_fast = a_bytes > b_bytes ? 1 : 0;
   }
-  const int grid = p.num_tiles < c->num_sms ? p.num_tiles : c->num_sms;
+  // Persistent grid: one CTA per SM, or as many co-resident pairs as the
+  // GPCs hold (a GPC with an odd count of free SMs leaves one idle).
+  int slots = c->num_sms;
+  if (PAIR) {
+    static int pairs[64] = {0};
+    if (!pairs[c->device]) {
+      cudaLaunchConfig_t oc;
+      memset(&oc, 0, sizeof(oc));
+      oc.gridDim = dim3(c->num_sms);
+      oc.blockDim = dim3(kThreads);
+      oc.dynamicSmemBytes = (size_t)C::SMEM;
+      cudaLaunchAttribute ca[1];
+      ca[0].id = cudaLaunchAttributeClusterDimension;
+      ca[0].val.clusterDim.x = 2;
+      ca[0].val.clusterDim.y = 1;
+      ca[0].val.clusterDim.z = 1;
+      oc.attrs = ca;
+      oc.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_kernel<BN, EPI, PAIR>, &oc) != cudaSuccess ||
+          n <= 0) {
+        cudaGetLastError();
+        n = c->num_sms / 2;
+      }
+      pairs[c->device] = n < c->num_sms / 2 ? n : c->num_sms / 2;
+    }
+    slots = pairs[c->device];
+  }
+  const int grid = (p.num_tiles < slots ? p.num_tiles : slots) * (PAIR ? 2 : 1);
   unsigned long long* tr = nullptr;
   if (trace_enabled() && !r.no_alloc) {
     cudaMalloc(&tr, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid);
     cudaMemsetAsync(tr, 0, sizeof(unsigned long long) * TR_SLOTS * (size_t)grid, s);
     p.trace = tr;
   }
-  cudaError_t le = launch_pdl(gemm_i8_kernel<BN, EPI>, dim3(grid), dim3(kThreads),
-                              (size_t)C::SMEM, s, ta, tb, ta2, om, p);
+  cudaError_t le;
+  if (PAIR) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    le = cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, PAIR>, ta, tb, ta2, om, p);
+  } else {
+    le = launch_pdl(gemm_i8_kernel<BN, EPI, PAIR>, dim3(grid), dim3(kThreads), (size_t)C::SMEM,
+                    s, ta, tb, ta2, om, p);
+  }
   st = le == cudaSuccess ? check_launch() : (cudaGetLastError(), map_cuda(le));
   if (tr) {
     char name[48];
-    snprintf(name, sizeof(name), "bn%d/epi%d", BN, EPI);
+    snprintf(name, sizeof(name), "bn%d/epi%d%s", BN, EPI, PAIR ? "/pair" : "");
     trace_report(name, r.M, w->N, w->K, tr, grid, s);
     cudaFree(tr);
   }
@@ -922,6 +1139,18 @@ static int pick_bn(int M, int N, int sms, int dual) {
     }
   }
   return best;
+}
+
+// CTA-pair tiles (tcgen05 cta_group::2, two-CTA clusters, 256 x 256 per
+// pair): the pair MMA runs at the full tensor rate (measured ~137 cycles per
+// 256x256x32 int8 MMA, against ~200 for the one-CTA 128x256x32), but each
+// CTA's epilogue of a tile measured 25-45% slower in a pair, so pairs pay
+// only where the mainloop dominates: the stacked two-term linear (EPI_DUAL2,
+// K = 2816) over several waves (the DiT's W2 at 24,000 rows: 115 us against
+// 127).  Elsewhere (gated, QKVG, plain linears) they measured slower.
+static bool pair_pays(const GemmRequest& r, int num_sms) {
+  const long pair_tiles = (long)cdiv(r.M, 2 * kHalfM) * cdiv(r.w->N, 256);
+  return r.w->K >= 2048 && pair_tiles >= 2L * (num_sms / 2);
 }
 
 int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
@@ -1030,6 +1259,8 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
         return IRO_ERR_INVALID;
       }
       // Into y: both terms stacked in one A tile, N = 256 MMAs.
+      if (r.nout == 0 && !r.force_bn && pair_pays(r, c->num_sms))
+        return launch_t<256, EPI_DUAL2, true>(c, r, p, s);
       if (r.nout == 0 && !r.force_bn) return launch_t<256, EPI_DUAL2>(c, r, p, s);
       const int bn = r.force_bn ? r.force_bn : pick_bn(r.M, w->N, c->num_sms, 1);
       if (bn == 128) return launch_t<128, EPI_DUAL>(c, r, p, s);

@@ -288,6 +288,34 @@ def test_linear2_dual_term(M, N, K):
     assert_same(y.get(), y2, "two-term outputs")
 
 
+@pytest.mark.parametrize("M,N", [(24000, 1024), (19999, 1280)])
+def test_linear2_dual_term_cta_pairs(M, N):
+    """The two-term linear at the DiT's W2 size (K = 2816, many waves) runs
+    on CTA pairs (tcgen05 cta_group::2, 256-row pair tiles, each CTA staging
+    half of the weight tile); the last pair tile of M = 19999 is ragged.  A
+    row sample (first and last 128 rows, 256 random) bit-exact against the
+    oracle."""
+    K = 2816
+    rng = np.random.default_rng(M + N)
+    h = (rng.standard_normal((M, K)) * 0.3).astype(np.float32)
+    ow = oracle.weight_quantize(_rand_weight(rng, N, K))
+    b = (rng.standard_normal(N) * 0.01).astype(np.float32)
+    hd = iro.DevBuf.from_host(h)
+    bufs = [iro.DevBuf((M, K), np.uint8), iro.DevBuf(M, np.float32), iro.DevBuf(M, np.int32),
+            iro.DevBuf((M, K), np.uint8), iro.DevBuf(M, np.float32), iro.DevBuf(M, np.int32)]
+    iro.quantize_rows_residual_dev(hd, M, K, *bufs[:3], None, *bufs[3:])
+    dw = iro.DevWeight.upload((ow.data, ow.scale, ow.colsum))
+    bd = iro.DevBuf.from_host(b)
+    y = iro.DevBuf((M, N), np.float32)
+    iro.linear2_dev(*bufs, dw, bd, y, M)
+    iro.synchronize()
+    rows = np.unique(np.r_[0:128, M - 128:M, rng.integers(0, M, 256)])
+    (q1, s1, z1), _, (q2, s2, z2) = oracle.quantize_rows_residual(h[rows])
+    y1, _ = oracle.linear_ex(q1, s1, z1, ow, b)
+    y2, _ = oracle.linear_ex(q2, s2, z2, ow, None, y=y1, accumulate=True)
+    assert_same(y.get()[rows], y2, "two-term outputs")
+
+
 @pytest.mark.parametrize("M,seg", [(512, 1024), (37, 1280), (750, 256)])
 def test_qkvg_split(M, seg):
     """dit.c:785-792: one quantised x, four projections; fused N-concat GEMM
