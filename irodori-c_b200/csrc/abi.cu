@@ -12,7 +12,6 @@
 
 #include "diag.cuh"
 #include "gemm_i8.cuh"
-#include "swiglu_fused.cuh"
 #include "quantize.cuh"
 
 using namespace iro;
@@ -717,7 +716,7 @@ size_t iro_int8_swiglu_workspace_bytes(int M, int D, int H, int residual_w2) {
              al(sizeof(float) * (size_t)M * H) +                           // hidden
              al((size_t)M * round_up(H, 16)) + 2 * al(sizeof(float) * M);   // qh, sh, zh
   if (residual_w2) t += al((size_t)M * round_up(H, 16)) + 2 * al(sizeof(float) * M);
-  return t + swiglu_fused_extra_bytes(M);
+  return t;
 }
 
 int iro_int8_swiglu_dev(const float* x, int M, const IroInt8DevWeight* w13,
@@ -803,21 +802,6 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
     qh2 = take((size_t)M * H);
     sh2 = reinterpret_cast<float*>(take(sizeof(float) * M));
     zh2 = reinterpret_cast<int32_t*>(take(sizeof(float) * M));
-  }
-  if (!rgate && !qx_in && !residual_w13 && stats_layer < 0 &&
-      swiglu_fused_supported(c, x, M, w13, w2, out, residual_w2)) {
-    SwigluBuffers b;
-    b.qx = qx;
-    b.sx = sx;
-    b.zx = zx;
-    b.hidden = hid;
-    b.qh = qh;
-    b.sh = sh;
-    b.zh = zh;
-    b.hlo = reinterpret_cast<int*>(take(sizeof(int) * M));
-    b.hhi = reinterpret_cast<int*>(take(sizeof(int) * M));
-    b.ctr = reinterpret_cast<int*>(ws + off);
-    return swiglu_fused_launch(c, x, M, w13, w2, b2 ? b2 : w2->bias, out, b, s);
   }
   if (residual_w13) {
     // Two-term W1/W3: both activation terms through the pair-block weight

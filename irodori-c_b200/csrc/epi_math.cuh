@@ -1,5 +1,5 @@
-// epi_math.cuh — per-chunk epilogue arithmetic shared by the GEMM kernels
-// (gemm_i8.cu) and the fused SwiGLU block kernel (swiglu_fused.cu).
+// epi_math.cuh — per-chunk epilogue arithmetic of the GEMM kernel
+// (gemm_i8.cu).
 //
 // A chunk is 16 consecutive accumulator columns of one TMEM lane (one output
 // row per thread, tcgen05.ld 32x32b).  Column parameters (colsum, weight

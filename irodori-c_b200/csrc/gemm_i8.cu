@@ -1200,12 +1200,6 @@ int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   switch (r.epi) {
     case EPI_LINEAR: {
       if (!r.y) return IRO_ERR_INVALID;
-      // Opt-in (IRO_GEMM_SPLITK=1): on config-2 W2 the split kernel runs in
-      // about the same time as this one (the 64 KB partial-sum exchange
-      // between the pair costs what the shorter mainloop saves).
-      const char* sk = getenv("IRO_GEMM_SPLITK");
-      if (sk && *sk == '1' && !trace_enabled() && splitk_eligible(r, c->num_sms))
-        return splitk_launch(c, r, s);
       const int bn = r.force_bn ? r.force_bn : pick_bn(r.M, w->N, c->num_sms, 0);
       if (bn == 256) return launch_t<256, EPI_LINEAR>(c, r, p, s);
       if (bn == 128) return launch_t<128, EPI_LINEAR>(c, r, p, s);

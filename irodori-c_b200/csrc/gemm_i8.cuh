@@ -84,9 +84,5 @@ int swiglu_run(Ctx* c, const float* x, int M, const IroInt8DevWeight* w13,
 // W1/W3 buffers when residual_w13 is set).
 size_t swiglu_workspace_bytes_ex(int M, int D, int H, int residual_w2, int residual_w13);
 
-// Split-K over a two-CTA cluster for plain linears with few, long tiles
-// (gemm_splitk.cu); gemm_launch picks it when eligible and IRO_GEMM_SPLITK=1.
-bool splitk_eligible(const GemmRequest& r, int num_sms);
-int splitk_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
 
 }  // namespace iro

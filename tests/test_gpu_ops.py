@@ -221,32 +221,6 @@ def test_linear_sweep_shapes_bit_exact(M, N):
     assert_same(yd2.get()[rows], oy, "outputs without raw sums")
 
 
-@pytest.mark.parametrize("M,N,K", [(2048, 1024, 2816), (300, 512, 4096), (1000, 520, 2816),
-                                   (129, 1024, 1030)])
-@pytest.mark.parametrize("bias,accumulate", [(True, False), (False, True)])
-def test_linear_dev_split_k_bit_exact(M, N, K, bias, accumulate, monkeypatch):
-    """With IRO_GEMM_SPLITK=1, shapes with few, long tiles and no raw-sum
-    output take the two-CTA split-K kernel: partial int32 sums exchanged
-    through distributed shared memory, then the same epilogue, so outputs
-    stay bit-exact."""
-    monkeypatch.setenv("IRO_GEMM_SPLITK", "1")
-    rng = np.random.default_rng(M * 11 + N + K)
-    w = _rand_weight(rng, N, K)
-    x = rng.standard_normal((M, K)).astype(np.float32)
-    ow = oracle.weight_quantize(w)
-    q, s, z = oracle.quantize_rows(x)
-    b = (rng.standard_normal(N) * 0.01).astype(np.float32) if bias else None
-    y0 = rng.standard_normal((M, N)).astype(np.float32) if accumulate else None
-    dw = iro.DevWeight.upload((ow.data, ow.scale, ow.colsum))
-    qd, sd, zd = iro.DevBuf.from_host(q), iro.DevBuf.from_host(s), iro.DevBuf.from_host(z)
-    bd = iro.DevBuf.from_host(b) if bias else None
-    yd = iro.DevBuf.from_host(y0) if accumulate else iro.DevBuf((M, N), np.float32)
-    iro.linear_dev(qd, sd, zd, dw, bd, yd, M, accumulate=accumulate)
-    iro.synchronize()
-    oy, _ = oracle.linear_ex(q, s, z, ow, b, y=y0, accumulate=accumulate)
-    assert_same(yd.get(), oy, "outputs")
-
-
 def test_linear_symmetric_mode_undoes_offset():
     """Symmetric s8 activations stored as u8+128 with zero=128: the s32 sum of
     the u8 GEMM minus 128*colsum equals the s8 x s8 sum."""

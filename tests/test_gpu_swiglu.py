@@ -204,22 +204,3 @@ def test_swiglu_pipe_submits_overlap_and_match():
         iro.synchronize()
         assert (outs[i].numpy().view(np.uint32) == ref.get().view(np.uint32)).all(), f"step {i}"
     pipe.free()
-
-
-@pytest.mark.parametrize("M,D,H", [(2048, 1024, 2816), (300, 1280, 3680), (5, 256, 208),
-                                   (4200, 1024, 2816), (129, 512, 384)])
-def test_fused_block_equals_separate_kernels(M, D, H, monkeypatch):
-    """The single-kernel block (quantise, W1|W3 + silu, requantise, W2 in one
-    cooperative launch, selected by IRO_SWIGLU_FUSED=1) runs the
-    separate-kernel path's arithmetic, so the two agree bit for bit."""
-    x, ws, bs = make_block(M * 3 + H, M, D, H)
-    w13, dw2 = upload(ws, bs)
-    xd = iro.DevBuf.from_host(x)
-    outs = []
-    for fused in ("1", "0"):
-        monkeypatch.setenv("IRO_SWIGLU_FUSED", fused)
-        out = iro.DevBuf((M, D), np.float32)
-        iro.swiglu_dev(xd, M, w13, dw2, None, out)
-        iro.synchronize()
-        outs.append(out.get())
-    assert (outs[0].view(np.uint32) == outs[1].view(np.uint32)).all()
