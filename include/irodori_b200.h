@@ -266,6 +266,19 @@ int iro_int8_swiglu_pipe_submit(IroSwigluPipe *pipe, const float *x_host, float 
 int iro_int8_swiglu_pipe_wait(IroSwigluPipe *pipe);
 void iro_int8_swiglu_pipe_free(IroSwigluPipe *pipe);
 
+/* Per-shape GEMM profile (ops.c:14-110, ops.h:126-129, the reference's
+   IRO_GEMM_PROFILE): with IRO_GEMM_PROFILE set and not "0", every int8 GEMM
+   launch is timed on the device (CUDA events around the kernel) and counted
+   per (kind, M, N, K, lda, ldb, ldc, beta), at most 256 shapes.  emit_json
+   writes one JSON line in the reference's schema to stderr (backend
+   "cuda-sm100a-tcgen05-i8"); iro_dit_sample_euler_dev resets the profile at
+   its start and emits it at its end, as sampler.c:142-144, 312-321 do.
+   Profiling serialises the launches it brackets. */
+int iro_cuda_gemm_profile_enabled(void);
+void iro_cuda_gemm_profile_reset(void);
+void iro_cuda_gemm_profile_emit_json(const char *status, int steps, int sequence_length,
+                                     int context_tokens);
+
 /* The SwiGLU block without allocation.  No counterpart in the reference.
    For callers that cannot allocate device memory where they run the block:
    engines that reserve all device memory at start-up and treat a later

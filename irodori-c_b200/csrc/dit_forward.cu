@@ -578,13 +578,19 @@ int iro_dit_sample_euler_dev(const IroDiTModelDev* m, float* state, int R, int c
     cond_mask_kernel<<<mb, 256, 0, s>>>(mask, tb.cond_mask, R, cfg, C);
     if ((st = check_launch())) return st;
   }
+  // sampler.c:142-144, 312-321: one IRO_GEMM_PROFILE record per sampling run.
+  iro_cuda_gemm_profile_reset();
   for (int step = 0; step < steps; step++) {
     const float t = ts[step];
     const bool use_cfg = cfg > 1 && t >= cfg_min_t && t <= cfg_max_t;
     st = step_impl(c, m, state, R, use_cfg ? cfg : 1, cfg, S, t, tn[step], cfg_scales, ctx_k,
                    ctx_v, use_cfg ? mask : (cfg > 1 ? tb.cond_mask : mask), C, tb, cb, step, s);
-    if (st) return st;
+    if (st) {
+      iro_cuda_gemm_profile_emit_json("error", steps, S, C);
+      return st;
+    }
   }
+  iro_cuda_gemm_profile_emit_json("ok", steps, S, C);
   return IRO_OK;
 }
 

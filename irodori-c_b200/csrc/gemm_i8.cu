@@ -1153,7 +1153,17 @@ static bool pair_pays(const GemmRequest& r, int num_sms) {
   return r.w->K >= 2048 && pair_tiles >= 2L * (num_sms / 2);
 }
 
+static int gemm_launch_impl(Ctx* c, const GemmRequest& r, cudaStream_t s);
+
 int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s) {
+  // IRO_GEMM_PROFILE: device time of the launch per shape (gemm_profile.cu).
+  void* tok = (r.M > 0 && r.w) ? gemm_profile_begin(r, s) : nullptr;
+  const int st = gemm_launch_impl(c, r, s);
+  if (tok) gemm_profile_end(tok, r, s);
+  return st;
+}
+
+static int gemm_launch_impl(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   const IroInt8DevWeight* w = r.w;
   if (r.M == 0) return IRO_OK;
   if (r.M < 0 || !w || !w->data || !r.a || !r.sx || !r.zp) return IRO_ERR_INVALID;

@@ -66,6 +66,11 @@ struct GemmRequest {
 
 int gemm_launch(Ctx* c, const GemmRequest& r, cudaStream_t s);
 
+// IRO_GEMM_PROFILE (gemm_profile.cu): per-shape device time of gemm_launch.
+bool gemm_profile_on();
+void* gemm_profile_begin(const GemmRequest& r, cudaStream_t s);
+void gemm_profile_end(void* token, const GemmRequest& r, cudaStream_t s);
+
 // iro_int8_swiglu_dev with an optional gated residual in the W2 epilogue:
 // out += rgate[row / rgate_rows] * swiglu(x) when rgate is set (out then
 // holds the residual stream), out = swiglu(x) otherwise.  With qx set, x is

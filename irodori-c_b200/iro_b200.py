@@ -81,6 +81,9 @@ SIGNATURES = {
     "iro_cuda_device_count": (_i, []),
     "iro_cuda_stream": (_vp, []),
     "iro_cuda_synchronize": (_i, [_vp]),
+    "iro_cuda_gemm_profile_enabled": (_i, []),
+    "iro_cuda_gemm_profile_reset": (None, []),
+    "iro_cuda_gemm_profile_emit_json": (None, [C.c_char_p, _i, _i, _i]),
     "iro_dev_malloc": (_vp, [_sz]),
     "iro_dev_free": (None, [_vp]),
     "iro_memcpy_htod": (_i, [_vp, _vp, _sz, _vp]),
