@@ -182,6 +182,84 @@ int iro_int8_dev_weight_gated_pair(IroInt8DevWeight *dst, const IroInt8Weight *w
                                    const float *b3);
 void iro_int8_dev_weight_free(IroInt8DevWeight *w);
 
+/* Device bytes of a weight's payload: codes (N x ld), scale, colsum and
+   bias.  0 for an empty weight. */
+size_t iro_int8_dev_weight_bytes(const IroInt8DevWeight *w);
+
+/* Int8 model containers ----------------------------------------------------
+   Device mirrors of the reference's engine-owned int8 copies.  The host-side
+   structs below have the member order and types of dit.h:53-55
+   (IroDiTInt8Layer) and dacvae.h:52-67 (IroDACVAEInt8*), so an engine can
+   pass its own quantised copies (e.g. `(const IroDiTInt8HostLayer *)
+   dit_int8.layer`) after iro_dit_int8_quantize / iro_dacvae_int8_quantize.
+   `bytes` counts the resident device payload (codes, scales, colsums,
+   biases), as the reference's `bytes` does for its host copies
+   (dit.c:253-256, dacvae.c:236-258; reported by generate.h:45-47). */
+typedef struct {
+    IroInt8Weight wq, wk, wv, gate, wo, w1, w2, w3;
+} IroDiTInt8HostLayer;
+
+typedef struct {
+    IroInt8DevWeight qkvg;  /* wq|wk|wv|gate concatenated along N */
+    IroInt8DevWeight wo;
+    IroInt8DevWeight w13;   /* w1, w3 in the GATED_PAIR layout */
+    IroInt8DevWeight w2;
+} IroDiTInt8DevLayer;
+
+typedef struct {
+    IroDiTInt8DevLayer layer[16];
+    int layers;
+    size_t bytes;
+} IroDiTInt8Dev;
+
+/* Upload `n_layers` (1..16) layers.  Returns IRO_OK or IRO_ERR_*; on error
+   nothing stays allocated. */
+int iro_dit_int8_dev_upload(IroDiTInt8Dev *dst, const IroDiTInt8HostLayer *layers,
+                            int n_layers);
+void iro_dit_int8_dev_free(IroDiTInt8Dev *q);
+
+#define IRO_B200_DACVAE_STAGES 4     /* dacvae.h:8 */
+#define IRO_B200_DACVAE_RESIDUALS 3  /* dacvae.h:9 */
+
+typedef struct {
+    IroInt8Weight conv0; /* [C, 7*C] */
+    IroInt8Weight conv1; /* [C, C] */
+} IroDACVAEInt8HostResidual;
+
+typedef struct {
+    IroInt8Weight upsample; /* [kernel*out, in] */
+    IroDACVAEInt8HostResidual residual[IRO_B200_DACVAE_RESIDUALS];
+} IroDACVAEInt8HostStage;
+
+typedef struct {
+    IroInt8Weight initial; /* [1536, 7*1024] */
+    IroDACVAEInt8HostStage stage[IRO_B200_DACVAE_STAGES];
+    size_t bytes;
+} IroDACVAEInt8Host;
+
+typedef struct {
+    IroInt8DevWeight conv0, conv1;
+} IroDACVAEInt8DevResidual;
+
+typedef struct {
+    IroInt8DevWeight upsample;
+    IroDACVAEInt8DevResidual residual[IRO_B200_DACVAE_RESIDUALS];
+} IroDACVAEInt8DevStage;
+
+typedef struct {
+    IroInt8DevWeight initial;
+    IroDACVAEInt8DevStage stage[IRO_B200_DACVAE_STAGES];
+    size_t bytes;
+} IroDACVAEInt8Dev;
+
+/* Upload every weight of a host IroDACVAEInt8 copy (the conv weights as
+   [N, kernel*in], the transposed convolutions as [kernel*out, in], as
+   iro_int8_conv1d_dev, iro_int8_convtranspose1d_dev and
+   iro_int8_codec_conv1_dev take them).  Returns IRO_OK or IRO_ERR_*; on
+   error nothing stays allocated. */
+int iro_dacvae_int8_dev_upload(IroDACVAEInt8Dev *dst, const IroDACVAEInt8Host *src);
+void iro_dacvae_int8_dev_free(IroDACVAEInt8Dev *q);
+
 /* Quantisers (device pointers, stream ordered) ------------------------------ */
 
 /* ops.c:321-348 on the device: q u8 [M,K], scale [M], zero [M]. */

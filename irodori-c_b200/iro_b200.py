@@ -56,6 +56,44 @@ class IroDiTBlockDev(C.Structure):
                 ("norm_eps", C.c_float), ("residual_mask", C.c_int)]
 
 
+class IroDiTInt8HostLayer(C.Structure):
+    _fields_ = [(n, IroInt8Weight) for n in ("wq", "wk", "wv", "gate", "wo", "w1", "w2", "w3")]
+
+
+class IroDiTInt8DevLayer(C.Structure):
+    _fields_ = [(n, IroInt8DevWeight) for n in ("qkvg", "wo", "w13", "w2")]
+
+
+class IroDiTInt8Dev(C.Structure):
+    _fields_ = [("layer", IroDiTInt8DevLayer * 16), ("layers", C.c_int), ("bytes", C.c_size_t)]
+
+
+class IroDACVAEInt8HostResidual(C.Structure):
+    _fields_ = [("conv0", IroInt8Weight), ("conv1", IroInt8Weight)]
+
+
+class IroDACVAEInt8HostStage(C.Structure):
+    _fields_ = [("upsample", IroInt8Weight), ("residual", IroDACVAEInt8HostResidual * 3)]
+
+
+class IroDACVAEInt8Host(C.Structure):
+    _fields_ = [("initial", IroInt8Weight), ("stage", IroDACVAEInt8HostStage * 4),
+                ("bytes", C.c_size_t)]
+
+
+class IroDACVAEInt8DevResidual(C.Structure):
+    _fields_ = [("conv0", IroInt8DevWeight), ("conv1", IroInt8DevWeight)]
+
+
+class IroDACVAEInt8DevStage(C.Structure):
+    _fields_ = [("upsample", IroInt8DevWeight), ("residual", IroDACVAEInt8DevResidual * 3)]
+
+
+class IroDACVAEInt8Dev(C.Structure):
+    _fields_ = [("initial", IroInt8DevWeight), ("stage", IroDACVAEInt8DevStage * 4),
+                ("bytes", C.c_size_t)]
+
+
 _vp, _i, _sz, _u64 = C.c_void_p, C.c_int, C.c_size_t, C.c_uint64
 _W = C.POINTER(IroInt8Weight)
 _DW = C.POINTER(IroInt8DevWeight)
@@ -81,6 +119,13 @@ SIGNATURES = {
     "iro_cuda_device_count": (_i, []),
     "iro_cuda_stream": (_vp, []),
     "iro_cuda_synchronize": (_i, [_vp]),
+    "iro_int8_dev_weight_bytes": (_sz, [_DW]),
+    "iro_dit_int8_dev_upload": (_i, [C.POINTER(IroDiTInt8Dev), C.POINTER(IroDiTInt8HostLayer),
+                                     _i]),
+    "iro_dit_int8_dev_free": (None, [C.POINTER(IroDiTInt8Dev)]),
+    "iro_dacvae_int8_dev_upload": (_i, [C.POINTER(IroDACVAEInt8Dev),
+                                        C.POINTER(IroDACVAEInt8Host)]),
+    "iro_dacvae_int8_dev_free": (None, [C.POINTER(IroDACVAEInt8Dev)]),
     "iro_cuda_gemm_profile_enabled": (_i, []),
     "iro_cuda_gemm_profile_reset": (None, []),
     "iro_cuda_gemm_profile_emit_json": (None, [C.c_char_p, _i, _i, _i]),

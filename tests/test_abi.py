@@ -102,3 +102,41 @@ def test_c_dropin_binary_binds_the_int8_api_to_this_library():
     assert "refops_iro_int8_linear_ex" in syms
     dyn = subprocess.run(["readelf", "-d", binp], capture_output=True, text=True).stdout
     assert "libirodori_b200.so" in dyn
+
+
+def _layout_probe(src, incs, tmp):
+    import subprocess
+    c = os.path.join(tmp, "probe.c")
+    exe = os.path.join(tmp, "probe")
+    open(c, "w").write(src)
+    subprocess.run(["gcc", "-std=c11", *[f"-I{i}" for i in incs], c, "-o", exe], check=True,
+                   capture_output=True)
+    return subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
+
+
+def test_int8_container_layouts_match_the_reference(tmp_path):
+    """IroDiTInt8HostLayer / IroDACVAEInt8Host have the size and member
+    offsets of the reference's IroDiTInt8Layer (dit.h:53-55) and
+    IroDACVAEInt8 (dacvae.h:52-67), so an engine passes its own copies."""
+    # The reference tree beside this repository (as __graft_entry__ finds it).
+    ref = os.environ.get("IRO_REFERENCE_DIR",
+                         os.path.join(os.path.dirname(os.path.dirname(iro.HERE)), "reference"))
+    if not os.path.isfile(os.path.join(ref, "dit.h")):
+        pytest.skip("reference headers not present")
+    body = r"""
+#include <stddef.h>
+#include <stdio.h>
+int main(void) {
+  printf("%zu %zu %zu %zu ", sizeof(DL), offsetof(DL, gate), offsetof(DL, w2), offsetof(DL, w3));
+  printf("%zu %zu %zu %zu\n", sizeof(CQ), offsetof(CQ, stage), offsetof(CQ, stage[1].residual[2].conv1),
+         offsetof(CQ, bytes));
+  return 0;
+}
+"""
+    theirs = _layout_probe('#include "dit.h"\n#include "dacvae.h"\ntypedef IroDiTInt8Layer DL;\n'
+                           'typedef IroDACVAEInt8 CQ;\n' + body, [ref], str(tmp_path))
+    inc = os.path.dirname(iro.HEADER_PATH)
+    ours = _layout_probe('#include <stdint.h>\n#include "irodori_b200.h"\n'
+                         'typedef IroDiTInt8HostLayer DL;\ntypedef IroDACVAEInt8Host CQ;\n' + body,
+                         [inc], str(tmp_path))
+    assert ours == theirs, (ours, theirs)
