@@ -192,8 +192,9 @@ size_t iro_int8_dev_weight_bytes(const IroInt8DevWeight *w);
    (IroDiTInt8Layer) and dacvae.h:52-67 (IroDACVAEInt8*), so an engine can
    pass its own quantised copies (e.g. `(const IroDiTInt8HostLayer *)
    dit_int8.layer`) after iro_dit_int8_quantize / iro_dacvae_int8_quantize.
-   `bytes` counts the resident device payload (codes, scales, colsums,
-   biases), as the reference's `bytes` does for its host copies
+   `bytes` counts the resident device payload (codes with their 16-byte row
+   pitch, scales, colsums, biases, and the W1|W3 pair layout's padding rows),
+   as the reference's `bytes` does for its host copies
    (dit.c:253-256, dacvae.c:236-258; reported by generate.h:45-47). */
 typedef struct {
     IroInt8Weight wq, wk, wv, gate, wo, w1, w2, w3;

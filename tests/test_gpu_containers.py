@@ -41,7 +41,8 @@ def test_dit_container_matches_separate_uploads():
     assert cont.bytes == sum(L.iro_int8_dev_weight_bytes(C.byref(p)) for p in parts)
     D, H = 1280, 3680
     expect = 0
-    for n, k in ((4 * D, D), (D, D), (2 * H, D), (D, H)):
+    Hp = (H + 127) // 128 * 128  # the W1|W3 pair layout pads H to whole 128-row blocks
+    for n, k in ((4 * D, D), (D, D), (2 * Hp, D), (D, H)):
         expect += n * ((k + 15) // 16 * 16) + 8 * n
     assert cont.bytes == 2 * expect
     # Layer 0 through the container's weights vs a block built separately.
