@@ -538,6 +538,23 @@ int iro_dit_euler_step_dev(const IroDiTModelDev *m, float *state, int R, int cfg
    iro_dit_output, dit.c:1070); workspace >= 4*B*S*model_dim bytes.  The fp32
    linears sum each output in the reference's scalar order without fused
    multiply-adds. */
+/* The two halves of iro_dit_euler_step_dev, for a step split across GPUs by
+   CFG branch (fewer requests than GPUs): iro_dit_velocity_dev runs the model
+   (conditioner, input projection, blocks, output head) and writes the raw
+   velocity of every row, [R*cfg, S, latent], without touching the state;
+   iro_dit_cfg_update_dev then applies sampler.c:283-297's guided Euler update
+   to the state from the velocities of all cfg branches per request (rows r*cfg
+   .. r*cfg+cfg-1), in the same arithmetic as iro_dit_euler_step_dev.  One GPU
+   can run one branch (cfg 1, that branch's mask row), the branches' velocities
+   meet by an all-gather, and every GPU then applies the same update.
+   Workspace: iro_dit_step_workspace_bytes.  Returns IRO_OK or IRO_ERR_*. */
+int iro_dit_velocity_dev(const IroDiTModelDev *m, const float *state, int R, int cfg, int S,
+                         float t, const float *const *ctx_k, const float *const *ctx_v,
+                         const uint8_t *mask, int C, float *velocity, void *workspace,
+                         void *stream);
+int iro_dit_cfg_update_dev(const IroDiTModelDev *m, float *state, const float *velocity, int R,
+                           int cfg, int S, float t, float t_next, const float *cfg_scales,
+                           void *stream);
 size_t iro_dit_stage_workspace_bytes(const IroDiTModelDev *m, int rows);
 int iro_dit_condition_dev(const IroDiTModelDev *m, const float *t, int B, float *cond,
                           void *workspace, void *stream);

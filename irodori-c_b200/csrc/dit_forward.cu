@@ -427,11 +427,12 @@ int condition_all(const IroDiTModelDev* m, const float* t_host, const CondBufs& 
 
 // One step with `cfg` active rows per request, `mask` [R*cfg, C] for those
 // rows; `full_cfg` is the width the scratch was sized for; the step's
-// conditioning is row `row` of `cb`.
+// conditioning is row `row` of `cb`.  With `vel_out` the per-row velocities
+// [R*cfg, S, L] go there and the state is not updated.
 int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int full_cfg,
               int S, float t, float t_next, const float* scales, const float* const* ctx_k,
               const float* const* ctx_v, const uint8_t* mask, int C, const StepBufs& tb,
-              const CondBufs& cb, int row, cudaStream_t s) {
+              const CondBufs& cb, int row, cudaStream_t s, float* vel_out = nullptr) {
   const int D = m->block[0].model_dim, L = m->latent_dim;
   const int B = R * cfg, Bfull = R * full_cfg;
   uint8_t* ws = tb.rest;
@@ -443,6 +444,7 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
   };
   float* x = reinterpret_cast<float*>(take(sizeof(float) * (size_t)Bfull * S * D));
   float* vel = reinterpret_cast<float*>(take(sizeof(float) * (size_t)Bfull * S * L));
+  if (vel_out) vel = vel_out;
   void* blk_ws = ws + off;
   int st;
   // Input projection per request, each row stored to its CFG rows.
@@ -460,6 +462,7 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
   rmsnorm_ref_kernel<<<cdiv(B * S, kNR), 256, 0, s>>>(x, m->out_norm, x, B * S, D, m->norm_eps);
   if ((st = check_launch())) return st;
   if ((st = linear_ref(x, m->out_w, m->out_b, vel, B * S, L, D, 0, s))) return st;
+  if (vel_out) return IRO_OK;
   const float dt = t_next - t;
   const float s1 = cfg > 1 ? scales[0] : 0.0f, s2 = cfg > 2 ? scales[1] : 0.0f;
   const float s3 = cfg > 3 ? scales[2] : 0.0f;
@@ -539,6 +542,51 @@ int iro_dit_euler_step_dev(const IroDiTModelDev* m, float* state, int R, int cfg
   if ((st = condition_all(m, &t, cb, s))) return st;
   return step_impl(c, m, state, R, cfg, cfg, S, t, t_next, cfg_scales, ctx_k, ctx_v, mask, C, tb,
                    cb, 0, s);
+}
+
+int iro_dit_velocity_dev(const IroDiTModelDev* m, const float* state, int R, int cfg, int S,
+                         float t, const float* const* ctx_k, const float* const* ctx_v,
+                         const uint8_t* mask, int C, float* velocity, void* workspace,
+                         void* stream) {
+  static const float no_scales[3] = {0.0f, 0.0f, 0.0f};
+  if (!velocity ||
+      !valid_run(m, state, R, cfg, S, no_scales, ctx_k, ctx_v, mask, C))
+    return IRO_ERR_INVALID;
+  int st = check_blocks(m, state, R, cfg, S, ctx_k, ctx_v, mask, C);
+  if (st) return st;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  cudaStream_t s = pick_stream(c, stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (!ws) {
+    ws = static_cast<uint8_t*>(arena_get(c, iro_dit_step_workspace_bytes(m, R, cfg, S, C), &st));
+    if (!ws) return st;
+  }
+  StepBufs tb = carve(ws, S);
+  const CondBufs cb = carve_cond(m, 1, ws + head_bytes(R, S, C));
+  tb.rest = ws + head_bytes(R, S, C) + cond_bytes(m, 1);
+  if ((st = upload_rope(tb, S, s))) return st;
+  if ((st = condition_all(m, &t, cb, s))) return st;
+  return step_impl(c, m, const_cast<float*>(state), R, cfg, cfg, S, t, t, no_scales, ctx_k, ctx_v,
+                   mask, C, tb, cb, 0, s, velocity);
+}
+
+int iro_dit_cfg_update_dev(const IroDiTModelDev* m, float* state, const float* velocity, int R,
+                           int cfg, int S, float t, float t_next, const float* cfg_scales,
+                           void* stream) {
+  if (!valid_model(m) || !state || !velocity || R <= 0 || cfg < 1 || cfg > 4 || S <= 0 ||
+      (cfg > 1 && !cfg_scales))
+    return IRO_ERR_INVALID;
+  int st;
+  Ctx* c = ctx_current(&st);
+  if (!c) return st;
+  cudaStream_t s = pick_stream(c, stream);
+  const long long one = (long long)S * m->latent_dim;
+  const float s1 = cfg > 1 ? cfg_scales[0] : 0.0f, s2 = cfg > 2 ? cfg_scales[1] : 0.0f;
+  const float s3 = cfg > 3 ? cfg_scales[2] : 0.0f;
+  const int ub = (int)std::min<long long>((R * one + 255) / 256, c->num_sms * 16LL);
+  euler_cfg_kernel<<<ub, 256, 0, s>>>(state, velocity, R, cfg, one, t_next - t, s1, s2, s3);
+  return check_launch();
 }
 
 int iro_dit_sample_euler_dev(const IroDiTModelDev* m, float* state, int R, int cfg, int S,

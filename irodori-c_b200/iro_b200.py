@@ -126,6 +126,10 @@ SIGNATURES = {
     "iro_dacvae_int8_dev_upload": (_i, [C.POINTER(IroDACVAEInt8Dev),
                                         C.POINTER(IroDACVAEInt8Host)]),
     "iro_dacvae_int8_dev_free": (None, [C.POINTER(IroDACVAEInt8Dev)]),
+    "iro_dit_velocity_dev": (_i, [C.c_void_p, _vp, _i, _i, _i, C.c_float, _vp, _vp, _vp, _i,
+                                  _vp, _vp, _vp]),
+    "iro_dit_cfg_update_dev": (_i, [C.c_void_p, _vp, _vp, _i, _i, _i, C.c_float, C.c_float,
+                                    _vp, _vp]),
     "iro_cuda_gemm_profile_enabled": (_i, []),
     "iro_cuda_gemm_profile_reset": (None, []),
     "iro_cuda_gemm_profile_emit_json": (None, [C.c_char_p, _i, _i, _i]),
@@ -722,6 +726,20 @@ class DiTModel:
                                              init_scale, cfg_min_t, cfg_max_t, sc, ks, vs,
                                              _p(mask), n_ctx, _p(workspace), stream),
               "dit_sample_euler_dev")
+
+    def velocity(self, state, R, cfg, S, t, ctx_k, ctx_v, mask, n_ctx, velocity, workspace=None,
+                 stream=None):
+        """Per-row velocities [R*cfg, S, 32] of one model forward (no update)."""
+        ks = (_vp * len(ctx_k))(*[k.ptr for k in ctx_k])
+        vs = (_vp * len(ctx_v))(*[v.ptr for v in ctx_v])
+        check(lib().iro_dit_velocity_dev(C.byref(self.st), _p(state), R, cfg, S, t, ks, vs,
+                                         _p(mask), n_ctx, _p(velocity), _p(workspace), stream),
+              "dit_velocity_dev")
+
+    def cfg_update(self, state, velocity, R, cfg, S, t, t_next, cfg_scales, stream=None):
+        sc = (C.c_float * 3)(*(list(cfg_scales) + [0.0] * (3 - len(cfg_scales))))
+        check(lib().iro_dit_cfg_update_dev(C.byref(self.st), _p(state), _p(velocity), R, cfg, S,
+                                           t, t_next, sc, stream), "dit_cfg_update_dev")
 
     def condition(self, t, cond):
         t = np.ascontiguousarray(np.atleast_1d(t), np.float32)
