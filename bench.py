@@ -569,6 +569,64 @@ def leg_dit(args, iro, stream, dims, world, max_ranks, barrier, case=None):
     return res, c
 
 
+def leg_dit_cfg_split(args, iro, stream, world, rank, dist, max_ranks, barrier):
+    """One request on `world` GPUs, split by CFG branch (fewer requests than
+    GPUs): rank r runs the branches b with b % world == r through
+    iro_dit_velocity_dev, the velocities meet by an NCCL all-gather over
+    NVLink every step ([ceil(4/world), S, 32] fp32 per rank), and every rank
+    applies the guided update (iro_dit_cfg_update_dev) to its copy of the
+    state.  Compared with the same step of the whole request on one GPU
+    (rank 0 alone, iro_dit_euler_step_dev)."""
+    import torch
+
+    c = DitCase(iro, "cfg3", 1, seed=91)
+    mine = [b for b in range(DIT_CFG) if b % world == rank]
+    bmax = -(-DIT_CFG // world)
+    ws = iro.DevBuf(c.model.workspace_bytes(1, DIT_CFG, DIT_S, DIT_C), np.uint8)
+    state = torch.from_numpy(c.state0).cuda()
+    send = torch.zeros((bmax, DIT_S, 32), dtype=torch.float32, device="cuda")
+    recv = torch.empty((world * bmax, DIT_S, 32), dtype=torch.float32, device="cuda")
+    # Gathered slot (rank r, index i) holds branch r + i * world.
+    order = [r + i * world for i in range(bmax) for r in range(world)]
+    pick = torch.tensor([order.index(b) for b in range(DIT_CFG)], device="cuda")
+    mask_mine = iro.DevBuf.from_host(np.ascontiguousarray(c.mask[mine])) if mine else None
+    steps = args.steps
+
+    def step(i):
+        t, tn = 1.0 - i / (steps + 1), 1.0 - (i + 1) / (steps + 1)
+        if mine:
+            c.model.velocity(state, 1, len(mine), DIT_S, t, c.ckd, c.cvd, mask_mine, DIT_C, send,
+                             workspace=ws)
+        with torch.cuda.stream(stream):
+            dist.all_gather_into_tensor(recv, send)
+            full = recv.index_select(0, pick)
+        c.model.cfg_update(state, full, 1, DIT_CFG, DIT_S, t, tn, DIT_SCALES)
+
+    for i in range(args.warmup):
+        step(i)
+    iro.synchronize()
+    barrier()
+    ms = max_ranks(timed(stream, step, steps) / steps)
+    single = None
+    if rank == 0:
+        st1 = torch.from_numpy(c.state0).cuda()
+        one = lambda i: c.model.euler_step(st1, 1, DIT_CFG, DIT_S, 1.0 - i / (steps + 1),  # noqa
+                                           1.0 - (i + 1) / (steps + 1), DIT_SCALES, c.ckd, c.cvd,
+                                           c.maskd, DIT_C, workspace=ws)
+        for i in range(3):
+            one(i)
+        single = timed(stream, one, steps) / steps
+    single = max_ranks(single if single is not None else 0.0)
+    ws.free()
+    return {"value": round(1000.0 / ms, 3), "unit": "steps/s", "ms_per_step": round(ms, 3),
+            "requests": 1, "gpus": world, "branches_per_gpu": bmax,
+            "one_gpu_ms_per_step": round(single, 3),
+            "speedup_vs_one_gpu": round(single / ms, 3),
+            "collective": "all_gather_into_tensor of the branch velocities (NCCL) every step",
+            "workload": f"cfg3 dims, 1 request x {DIT_CFG} CFG branches x {DIT_S} frames, "
+                        f"{DIT_C} context tokens, CFG window open every step"}
+
+
 def leg_dit_gemm(args, iro, stream, dims, max_ranks):
     """The config-3 W1|W3 gated GEMM (the DiT's largest int8 GEMM, M = 24000
     rows) alone: the DiT line's roofline kernel."""
@@ -774,6 +832,9 @@ def run_ours(args):
                        keep_host=(rank == 0 and world == 1 and not args.no_cpu))
         refd, _ = leg_dit(args, iro, stream, "reference", world, max_ranks, barrier, case=case)
         nested["dit_ref_dims"] = refd
+        if world > 1:
+            nested["dit_cfg_split"] = leg_dit_cfg_split(args, iro, stream, world, rank, dist,
+                                                        max_ranks, barrier)
         c_ms, wq, cinp, cbias = leg_conv7(args, iro, stream, max_ranks)
         nested["conv7"] = {"value": round(world * conv_ops() / (c_ms * 1e-3) / 1e12, 2),
                            "unit": "TOPS", "ms_per_step": round(c_ms, 4),
