@@ -825,7 +825,7 @@ def run_ours(args):
                            "silu) at M = 24000, the DiT's largest int8 GEMM",
                            "achieved": round(g_tops, 1), "peak": round(int8_peak, 1),
                            "unit": "TFLOP/s", "frac": round(g_tops / int8_peak, 4),
-                           "traffic": profile_traffic("gemm_i8_dit_m24000.md"),
+                           "traffic": profile_traffic("gemm_i8_gated_m24000.md"),
                            "ms_per_launch": round(g_ms, 4), "ops_per_launch": g_ops}
         nested["dit"] = dit
         case = DitCase(iro, "reference", DIT_REQUESTS, seed=35 + rank,
