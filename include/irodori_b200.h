@@ -437,7 +437,21 @@ int iro_int8_codec_conv1_dev(const float *hidden, int rows, const IroInt8DevWeig
    residual_mask follows IRO_INT8_RESIDUAL (dit.c:429-436): the groups whose
    activations are quantised with a second residual term, 1 = Q/K/V/gate,
    2 = Wo, 4 = W1/W3, 8 = W2 (the reference default), any combination; other
-   bits are IRO_ERR_INVALID. */
+   bits are IRO_ERR_INVALID.
+   fp32_groups and emulate are the reference's error-attribution switches
+   (dit.c:273-335, the environment variables IRO_INT8_MASK and
+   IRO_INT8_EMULATE), per block; zero (the default) runs every group in int8.
+   fp32_groups: the groups (same bits as residual_mask) left out of the int8
+   path, i.e. 15 & ~IRO_INT8_MASK: fp32 activations x the fp32 weights.
+   emulate: for the int8 groups, 1 = fp32 activations x the dequantised int8
+   weights (weight-only error), any other non-zero value = the quantiser's
+   codes turned back into fp32 x the fp32 weights (activation-only error).
+   w_fp32: the fp32 weights [N, K] on the device, in the order wq, wk, wv,
+   gate, wo, w1, w3, w2; needed for the fp32 groups and for emulate != 0, 1.
+   A group whose int8 weight is not used may leave it zeroed.  These modes
+   are diagnostics: a plain fp32 GEMM, correct rather than fast, with more
+   workspace (iro_dit_block_workspace_bytes counts it).  A two-term W1/W3
+   (residual_mask bit 4) feeding a non-int8 W2 is IRO_ERR_UNSUPPORTED. */
 typedef struct {
     const float *adaln[2][9];
     const float *q_norm;
@@ -446,6 +460,9 @@ typedef struct {
     int model_dim, heads, head_dim, adaln_rank, mlp_dim;
     float norm_eps;
     int residual_mask;
+    int fp32_groups;
+    int emulate;
+    const float *w_fp32[8];
 } IroDiTBlockDev;
 
 /* The reference's int8 policy switches, read from the same environment
@@ -464,6 +481,11 @@ int iro_policy_codec_int8_mask(void);
 int iro_policy_codec_residual_mask(void);
 int iro_policy_codec_residual_stages(void);
 int iro_policy_codec_residual(int stage, int group);
+/* The reference's diagnostic switches for the DiT block's fp32_groups and
+   emulate: 15 & ~IRO_INT8_MASK (dit.c:284-291, default mask 15, so 0) and
+   IRO_INT8_EMULATE (dit.c:297-304, default 0), parsed the same way. */
+int iro_policy_dit_fp32_groups(void);
+int iro_policy_dit_emulate(void);
 
 /* Activation diagnostics (dit.c:340-412), recorded by the sampler entry
    points (iro_dit_euler_step_dev, iro_dit_sample_euler_dev: layer index known)

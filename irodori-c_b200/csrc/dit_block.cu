@@ -26,6 +26,7 @@
 #include "diag.cuh"
 #include "dit_attention.cuh"
 #include "dit_block.cuh"
+#include "dit_diag32.cuh"
 #include "gemm_i8.cuh"
 #include "quantize.cuh"
 
@@ -592,6 +593,47 @@ int dit_adaln_params(const IroDiTBlockDev* const* blks, int n_blocks, const floa
   return check_launch();
 }
 
+namespace {
+
+// Mode of one projection group under the block's diagnostic switches
+// (dit.c:780-797, 876-883, 940-969): left out of the int8 mask -> fp32,
+// else int8, or emulated when emulate is set (1 = weight-only, any other
+// value = activation-only error, as int8_linear_emulated decides).
+int group_mode(const IroDiTBlockDev* blk, int group) {
+  if (blk->fp32_groups & group) return DIAG_FP32;
+  if (blk->emulate == 0) return DIAG_INT8;
+  return blk->emulate == 1 ? DIAG_EMULATE_WEIGHT : DIAG_EMULATE_ACTIVATION;
+}
+
+bool diag_active(const IroDiTBlockDev* blk) { return blk->fp32_groups != 0 || blk->emulate != 0; }
+
+// The SwiGLU scratch is only live in the MLP half, the V^T copies only in
+// the attention half: they share the tail of the workspace.
+size_t block_tail_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int context_batch) {
+  const int M = B * S;
+  return std::max(swiglu_workspace_bytes_ex(M, blk->model_dim, blk->mlp_dim,
+                                            (blk->residual_mask & 8) != 0,
+                                            (blk->residual_mask & 4) != 0),
+                  attention_tc_workspace_bytes(B, S, C, context_batch, blk->model_dim));
+}
+
+// The diagnostic paths' region after the tail: the projections' scratch,
+// then the hidden [M, H], the W3 output [M, H] and W2's codes (two terms)
+// with their row parameters.
+size_t diag_scratch_bytes(const IroDiTBlockDev* blk, int M) {
+  const int D = blk->model_dim, H = blk->mlp_dim;
+  return std::max(diag_linear_scratch_bytes(M, D, D),
+                  std::max(diag_linear_scratch_bytes(M, D, H), diag_linear_scratch_bytes(M, H, D)));
+}
+
+size_t diag_region_bytes(const IroDiTBlockDev* blk, int M) {
+  const size_t H = (size_t)blk->mlp_dim;
+  return al256(diag_scratch_bytes(blk, M)) + 2 * al256(sizeof(float) * M * H) +
+         2 * (al256((size_t)M * H) + 2 * al256(sizeof(float) * M));
+}
+
+}  // namespace
+
 size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int context_batch) {
   const size_t M = (size_t)B * S, D = (size_t)blk->model_dim;
   size_t t = 0;
@@ -599,12 +641,9 @@ size_t dit_block_body_bytes(const IroDiTBlockDev* blk, int B, int S, int C, int 
   t += 2 * (al256(M * D) + 2 * al256(sizeof(float) * M));          // codes (two terms) + row params
   t += al256(sizeof(int) * (size_t)B * C) + al256(sizeof(int) * B);
   t += al256(sizeof(float) * 2 * 32 * (size_t)S);                   // grouped RoPE tables
-  // The SwiGLU scratch is only live in the MLP half, the V^T copies only in
-  // the attention half: they share the tail of the workspace.
-  return t + std::max(swiglu_workspace_bytes_ex((int)M, blk->model_dim, blk->mlp_dim,
-                                                (blk->residual_mask & 8) != 0,
-                                                (blk->residual_mask & 4) != 0),
-                      attention_tc_workspace_bytes(B, S, C, context_batch, blk->model_dim));
+  const size_t tail = block_tail_bytes(blk, B, S, C, context_batch);
+  if (!diag_active(blk)) return t + tail;
+  return t + al256(tail) + diag_region_bytes(blk, (int)M);
 }
 
 int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, const float* ctx_k,
@@ -620,11 +659,27 @@ int dit_block_check(const IroDiTBlockDev* blk, const float* x, int cond_rows, co
     return IRO_ERR_UNSUPPORTED;
   // Two-term activation policy: any combination of the four groups
   // (dit.c:429-436); the reference's default is W2 only (8).
-  if ((blk->residual_mask & ~15) != 0) return IRO_ERR_INVALID;
-  if (blk->qkvg.N != 4 * D || blk->qkvg.K != D || blk->wo.N != D || blk->wo.K != D ||
-      blk->w13.layout != IRO_LAYOUT_GATED_PAIR || blk->w13.K != D || blk->w13.hidden != H ||
-      blk->w2.N != D || blk->w2.K != H)
+  if ((blk->residual_mask & ~15) != 0 || (blk->fp32_groups & ~15) != 0) return IRO_ERR_INVALID;
+  const int m_qkvg = group_mode(blk, 1), m_wo = group_mode(blk, 2);
+  const int m_w13 = group_mode(blk, 4), m_w2 = group_mode(blk, 8);
+  // The int8 weights where a group reads them (int8 and weight emulation),
+  // the fp32 weights where it reads those (fp32 and activation emulation).
+  auto int8_used = [](int m) { return m == DIAG_INT8 || m == DIAG_EMULATE_WEIGHT; };
+  auto fp32_used = [](int m) { return m == DIAG_FP32 || m == DIAG_EMULATE_ACTIVATION; };
+  if (int8_used(m_qkvg) &&
+      (blk->qkvg.N != 4 * D || blk->qkvg.K != D || blk->qkvg.layout != IRO_LAYOUT_PLAIN))
     return IRO_ERR_INVALID;
+  if (int8_used(m_wo) && (blk->wo.N != D || blk->wo.K != D)) return IRO_ERR_INVALID;
+  if (int8_used(m_w13) &&
+      (blk->w13.layout != IRO_LAYOUT_GATED_PAIR || blk->w13.K != D || blk->w13.hidden != H))
+    return IRO_ERR_INVALID;
+  if (int8_used(m_w2) && (blk->w2.N != D || blk->w2.K != H)) return IRO_ERR_INVALID;
+  const int groups[8] = {m_qkvg, m_qkvg, m_qkvg, m_qkvg, m_wo, m_w13, m_w13, m_w2};
+  for (int i = 0; i < 8; i++)
+    if (fp32_used(groups[i]) && !blk->w_fp32[i]) return IRO_ERR_INVALID;
+  // The two-term W1/W3 path runs inside the int8 SwiGLU only.
+  if ((blk->residual_mask & 4) && m_w13 == DIAG_INT8 && m_w2 != DIAG_INT8)
+    return IRO_ERR_UNSUPPORTED;
   return IRO_OK;
 }
 
@@ -667,6 +722,23 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
   const bool res_qkvg = (blk->residual_mask & 1) != 0, res_wo = (blk->residual_mask & 2) != 0;
   const bool res_w13 = (blk->residual_mask & 4) != 0, res_w2 = (blk->residual_mask & 8) != 0;
   const int diag_layer = (stats_layer >= 0 && diag_enabled()) ? stats_layer : -1;
+  // The diagnostic modes per group (fp32_groups / emulate) and their region
+  // after the tail.
+  const int m_qkvg = group_mode(blk, 1), m_wo = group_mode(blk, 2);
+  const int m_w13 = group_mode(blk, 4), m_w2 = group_mode(blk, 8);
+  const int H = blk->mlp_dim;
+  uint8_t* dreg = static_cast<uint8_t*>(sw_ws) + al256(block_tail_bytes(blk, B, S, C, context_batch));
+  void* dscratch = dreg;
+  float* dhid = reinterpret_cast<float*>(dreg + al256(diag_scratch_bytes(blk, (int)M)));
+  float* da3 = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(dhid) +
+                                        al256(sizeof(float) * M * H));
+  uint8_t* dq = reinterpret_cast<uint8_t*>(da3) + al256(sizeof(float) * M * H);
+  float* dqs = reinterpret_cast<float*>(dq + al256(M * H));
+  int32_t* dqz = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(dqs) + al256(sizeof(float) * M));
+  uint8_t* dq2 = reinterpret_cast<uint8_t*>(dqz) + al256(sizeof(float) * M);
+  float* dqs2 = reinterpret_cast<float*>(dq2 + al256(M * H));
+  int32_t* dqz2 =
+      reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(dqs2) + al256(sizeof(float) * M));
 
   const int prow = B / cond_rows;  // batch rows per AdaLN parameter row
   for (int half = 0; half < 2; half++) {
@@ -677,18 +749,24 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
     // the SwiGLU) in one pass; h is materialised for the two-term policies
     // and for shapes the fused kernel does not take.
     const bool two_term = half == 0 ? res_qkvg : res_w13;
-    st = (two_term || diag_layer >= 0) ? (int)IRO_ERR_UNSUPPORTED
-                  : adaln_quant_launch(x, (int)M, S, D, blk->norm_eps, prow, shift, scale, codes,
-                                       rs, rz, s);
+    const bool int8_in = (half == 0 ? m_qkvg : m_w13) == DIAG_INT8;
+    st = (two_term || diag_layer >= 0 || !int8_in)
+             ? (int)IRO_ERR_UNSUPPORTED
+             : adaln_quant_launch(x, (int)M, S, D, blk->norm_eps, prow, shift, scale, codes, rs,
+                                  rz, s);
     const bool fused = st == IRO_OK;
     if (st == IRO_ERR_UNSUPPORTED) {
       adaln_apply_kernel<<<cdiv((int)M, 8), 256, 0, s>>>(x, (int)M, S, D, blk->norm_eps, prow,
                                                          shift, scale, h);
       if ((st = check_launch())) return st;
-      // Q/K/V/gate or W1/W3 input diagnostics (dit.c:787, 944).
-      if (diag_layer >= 0 && (st = diag_record(diag_layer, half == 0 ? 0 : 2, h, (int)M, D, s)))
+      // Q/K/V/gate or W1/W3 input diagnostics (dit.c:787, 944), recorded on
+      // the int8 path as the reference does.
+      if (int8_in && diag_layer >= 0 &&
+          (st = diag_record(diag_layer, half == 0 ? 0 : 2, h, (int)M, D, s)))
         return st;
-      if (half == 0 && res_qkvg)
+      if (!int8_in)
+        st = IRO_OK;
+      else if (half == 0 && res_qkvg)
         st = quantize_rows_residual_launch(h, (int)M, D, codes, rs, rz, nullptr, codes2, rs2,
                                            rz2, s);
       else if (!(half == 1 && res_w13))
@@ -705,9 +783,19 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
                        sw_ws, nullptr, attention_mode() == 2 ? 0 : 1};
       const bool tc = attention_mode() != 1 && attention_tc_supported(ar);
       auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-      const bool fuse_heads = tc && !res_qkvg && al16(blk->q_norm) && al16(blk->k_norm);
+      const bool fuse_heads =
+          tc && !res_qkvg && m_qkvg == DIAG_INT8 && al16(blk->q_norm) && al16(blk->k_norm);
       float* vt = static_cast<float*>(sw_ws);
       const int vld = attention_tc_vt_ld(S);
+      if (m_qkvg != DIAG_INT8) {
+        // The fp32 / emulated projections, one per output (dit.c:780-784,
+        // 793-797).
+        float* outs[4] = {q, k, v, g};
+        for (int i = 0; i < 4; i++)
+          if ((st = diag_linear(c, m_qkvg, h, (int)M, D, &blk->qkvg, i * D, 0, blk->w_fp32[i],
+                                outs[i], D, dscratch, s)))
+            return st;
+      } else {
       GemmRequest r;
       r.epi = res_qkvg ? EPI_DUAL : fuse_heads ? EPI_QKV : EPI_SPLIT;
       r.M = (int)M;
@@ -745,6 +833,7 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
         r.eps = blk->norm_eps;
       }
       if ((st = gemm_launch(c, r, s))) return st;
+      }
       if (tc) {
         if (!fuse_heads) {
           // Head norm + RoPE with the self V^T rows the attention kernel reads.
@@ -763,6 +852,15 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
         AttnArgs aa{q, k, v, g, ctx_k, ctx_v, clist, ccount, B / context_batch, S, C, D, mix};
         attention_kernel<<<dim3(cdiv(S, kAQ), NH, B), kAThreads, 0, s>>>(aa);
         if ((st = check_launch())) return st;
+      }
+      if (m_wo != DIAG_INT8) {
+        // The fp32 / emulated Wo (dit.c:876-877, 882-883), then the gated
+        // residual x += gate * out (dit.c:1013-1020) on its own.
+        if ((st = diag_linear(c, m_wo, mix, (int)M, D, &blk->wo, 0, 0, blk->w_fp32[4], q, D,
+                              dscratch, s)))
+          return st;
+        if ((st = gated_residual_launch(c, x, q, gate, S * prow, (int)M, D, s))) return st;
+        continue;
       }
       // Wo on the quantised gated mix (dit.c:876-884), with the gated
       // residual x += gate * Wo(mix) (dit.c:1013-1020) in its epilogue.
@@ -789,6 +887,64 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       o.rgate = gate;
       o.rgate_rows = S * prow;
       if ((st = gemm_launch(c, o, s))) return st;
+    } else if (m_w13 != DIAG_INT8 || m_w2 != DIAG_INT8) {
+      // SwiGLU with a diagnostic group (dit.c:940-969): W1/W3 into the plain
+      // hidden [M, H], silu(w1) * w3, then W2 and the gated residual.
+      if (m_w13 == DIAG_INT8) {
+        // Single-term int8 W1/W3 with the gate in its epilogue (the two-term
+        // one is rejected by the block check).
+        GemmRequest gr;
+        gr.epi = EPI_GATED;
+        gr.M = (int)M;
+        gr.a = codes;
+        gr.lda = D;
+        gr.sx = rs;
+        gr.zp = rz;
+        gr.w = &blk->w13;
+        gr.hidden = dhid;
+        gr.ldh = H;
+        if ((st = gemm_launch(c, gr, s))) return st;
+      } else {
+        if ((st = diag_linear(c, m_w13, h, (int)M, D, &blk->w13, 0, 0, blk->w_fp32[5], dhid, H,
+                              dscratch, s)) ||
+            (st = diag_linear(c, m_w13, h, (int)M, D, &blk->w13, 0, 1, blk->w_fp32[6], da3, H,
+                              dscratch, s)) ||
+            (st = silu_mul_plain_launch(c, dhid, da3, (long long)M * H, dhid, s)))
+          return st;
+      }
+      if (m_w2 == DIAG_INT8) {
+        // W2 input diagnostics (dit.c:964), then the int8 W2 with the gated
+        // residual in its epilogue.
+        if (diag_layer >= 0 && (st = diag_record(diag_layer, 3, dhid, (int)M, H, s))) return st;
+        st = res_w2 ? quantize_rows_residual_launch(dhid, (int)M, H, dq, dqs, dqz, nullptr, dq2,
+                                                    dqs2, dqz2, s)
+                    : quantize_rows_launch(dhid, (int)M, H, dq, dqs, dqz, 0, s);
+        if (st) return st;
+        GemmRequest o;
+        o.epi = res_w2 ? EPI_DUAL : EPI_LINEAR;
+        o.M = (int)M;
+        o.a = dq;
+        o.lda = H;
+        o.sx = dqs;
+        o.zp = dqz;
+        if (res_w2) {
+          o.a2 = dq2;
+          o.sx2 = dqs2;
+          o.zp2 = dqz2;
+        }
+        o.w = &blk->w2;
+        o.bias = blk->w2.bias;
+        o.y = x;
+        o.ldy = D;
+        o.rgate = gate;
+        o.rgate_rows = S * prow;
+        if ((st = gemm_launch(c, o, s))) return st;
+      } else {
+        if ((st = diag_linear(c, m_w2, dhid, (int)M, H, &blk->w2, 0, 0, blk->w_fp32[7], q, D,
+                              dscratch, s)) ||
+            (st = gated_residual_launch(c, x, q, gate, S * prow, (int)M, D, s)))
+          return st;
+      }
     } else {
       // SwiGLU (dit.c:913-969), x += gate * W2(...) in the W2 epilogue.
       if (res_w13)

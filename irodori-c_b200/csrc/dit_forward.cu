@@ -517,7 +517,12 @@ size_t iro_dit_sample_workspace_bytes(const IroDiTModelDev* m, int R, int cfg, i
   size_t t = head_bytes(R, S, C) + cond_bytes(m, steps);
   t += al256(sizeof(float) * (size_t)B * S * D);                       // x
   t += al256(sizeof(float) * (size_t)B * S * m->latent_dim);           // velocity
-  return t + dit_block_body_bytes(&m->block[0], B, S, C, R);
+  // Blocks may differ in their policies (two-term groups, diagnostic modes),
+  // so the shared block workspace is the largest any layer needs.
+  size_t body = 0;
+  for (int l = 0; l < m->layers; l++)
+    body = std::max(body, dit_block_body_bytes(&m->block[l], B, S, C, R));
+  return t + body;
 }
 
 int iro_dit_euler_step_dev(const IroDiTModelDev* m, float* state, int R, int cfg, int S,

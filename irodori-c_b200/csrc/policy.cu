@@ -19,6 +19,16 @@ extern "C" {
 
 int iro_policy_dit_residual_mask(void) { return env_mask("IRO_INT8_RESIDUAL", 8); }
 
+// dit.c:284-291: IRO_INT8_MASK, default 15 (every group in int8); the block
+// takes the complement, the groups left in fp32.
+int iro_policy_dit_fp32_groups(void) { return 15 & ~env_mask("IRO_INT8_MASK", 15); }
+
+// dit.c:297-304: IRO_INT8_EMULATE, strtol base 0 without a mask, default 0.
+int iro_policy_dit_emulate(void) {
+  const char* e = getenv("IRO_INT8_EMULATE");
+  return (e && *e) ? (int)strtol(e, nullptr, 0) : 0;
+}
+
 int iro_policy_codec_int8_mask(void) { return env_mask("IRO_CODEC_INT8_MASK", 15); }
 
 int iro_policy_codec_residual_mask(void) {

@@ -53,7 +53,8 @@ class IroDiTBlockDev(C.Structure):
                 ("qkvg", IroInt8DevWeight), ("wo", IroInt8DevWeight), ("w13", IroInt8DevWeight),
                 ("w2", IroInt8DevWeight), ("model_dim", C.c_int), ("heads", C.c_int),
                 ("head_dim", C.c_int), ("adaln_rank", C.c_int), ("mlp_dim", C.c_int),
-                ("norm_eps", C.c_float), ("residual_mask", C.c_int)]
+                ("norm_eps", C.c_float), ("residual_mask", C.c_int),
+                ("fp32_groups", C.c_int), ("emulate", C.c_int), ("w_fp32", C.c_void_p * 8)]
 
 
 class IroDiTInt8HostLayer(C.Structure):
@@ -187,6 +188,8 @@ SIGNATURES = {
                                     _vp, _i, _vp, _vp]),
     "iro_dit_stage_workspace_bytes": (_sz, [_vp, _i]),
     "iro_policy_dit_residual_mask": (_i, []),
+    "iro_policy_dit_fp32_groups": (_i, []),
+    "iro_policy_dit_emulate": (_i, []),
     "iro_dit_stats_read": (_i, [_i, _i, C.POINTER(C.c_double), C.POINTER(C.c_double), _vp, _i]),
     "iro_dit_stats_reset": (None, []),
     "iro_dit_stats_report": (None, []),
@@ -652,7 +655,11 @@ class DiTBlock:
     AdaLN/norm arrays and int8 weights (HostWeight or (data, scale, colsum))."""
 
     def __init__(self, adaln, q_norm, k_norm, wq, wk, wv, wg, wo, w1, w3, w2, model_dim=1280,
-                 heads=20, rank=192, mlp_dim=3680, eps=1e-5, residual_mask=8):
+                 heads=20, rank=192, mlp_dim=3680, eps=1e-5, residual_mask=8, fp32_weights=None,
+                 fp32_groups=0, emulate=0):
+        """fp32_weights: host fp32 arrays (wq, wk, wv, gate, wo, w1, w3, w2), uploaded
+        for the diagnostic modes fp32_groups / emulate (the reference's
+        15 & ~IRO_INT8_MASK and IRO_INT8_EMULATE, dit.c:273-335)."""
         self.bufs = [DevBuf.from_host(np.ascontiguousarray(a, np.float32)) for a in adaln]
         self.qn = DevBuf.from_host(np.ascontiguousarray(q_norm, np.float32))
         self.kn = DevBuf.from_host(np.ascontiguousarray(k_norm, np.float32))
@@ -669,6 +676,11 @@ class DiTBlock:
         st.model_dim, st.heads, st.head_dim, st.adaln_rank, st.mlp_dim = (model_dim, heads, 64,
                                                                           rank, mlp_dim)
         st.norm_eps, st.residual_mask = eps, residual_mask
+        self.fp32 = [DevBuf.from_host(np.ascontiguousarray(a, np.float32))
+                     for a in (fp32_weights or [])]
+        for i, b in enumerate(self.fp32):
+            st.w_fp32[i] = b.ptr
+        st.fp32_groups, st.emulate = fp32_groups, emulate
         self.st = st
 
     def run(self, x, cond, ctx_k, ctx_v, mask, context_batch, B, S, n_ctx, rope_cos, rope_sin,

@@ -350,6 +350,8 @@ def ref_lib(kind="ieee"):
             L.ref_dit_swiglu_int8.restype = C.c_int
             L.ref_dit_block_int8.argtypes = [_vp] * 5 + [C.c_int] * 4 + [_vp] * 6
             L.ref_dit_block_int8.restype = C.c_int
+            L.ref_dit_block_w.argtypes = [_vp] * 5 + [C.c_int] * 4 + [_vp] * 7
+            L.ref_dit_block_w.restype = C.c_int
             L.ref_dit_block_dims.argtypes = [C.POINTER(C.c_int)] * 4
             L.ref_dit_block_dims.restype = C.c_int
             L.ref_dit_condition_w.argtypes = [_vp] * 4 + [C.c_int, _vp]
@@ -500,10 +502,13 @@ def ref_codec_upsample_residual():
 
 
 def ref_dit_block(x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C_ctx, adaln, q_norm,
-                  k_norm, weights, kind="dit"):
+                  k_norm, weights, kind="dit", fp32_weights=None):
     """The reference's dit_block (dit.c:983-1051) at layer 0 with int8
     projections.  weights: Weight objects wq, wk, wv, gate, wo, w1, w3, w2.
-    Returns the updated x [B*S, D]."""
+    fp32_weights: the fp32 projections in the same order, which the
+    reference's diagnostic switches IRO_INT8_MASK / IRO_INT8_EMULATE read
+    (dit.c:273-335; the reference takes both from this process's
+    environment, once).  Returns the updated x [B*S, D]."""
     L = ref_lib(kind)
     x = _c(x, np.float32).copy()
     keep = [_c(a, np.float32) for a in adaln]
@@ -511,11 +516,13 @@ def ref_dit_block(x, cond, ctx_k, ctx_v, mask, context_batch, B, S, C_ctx, adaln
     wd = (_vp * 8)(*[w.data.ctypes.data for w in weights])
     wsc = (_vp * 8)(*[w.scale.ctypes.data for w in weights])
     wcs = (_vp * 8)(*[w.colsum.ctypes.data for w in weights])
+    f32 = [_c(w, np.float32) for w in fp32_weights] if fp32_weights is not None else None
+    wf = (_vp * 8)(*[w.ctypes.data for w in f32]) if f32 is not None else None
     cond = _c(cond, np.float32); ctx_k = _c(ctx_k, np.float32); ctx_v = _c(ctx_v, np.float32)
     mask = _c(mask, np.uint8); q_norm = _c(q_norm, np.float32); k_norm = _c(k_norm, np.float32)
-    rc = L.ref_dit_block_int8(_ptr(x), _ptr(cond), _ptr(ctx_k), _ptr(ctx_v), _ptr(mask),
-                              context_batch, B, S, C_ctx, ada, _ptr(q_norm), _ptr(k_norm),
-                              wd, wsc, wcs)
+    rc = L.ref_dit_block_w(_ptr(x), _ptr(cond), _ptr(ctx_k), _ptr(ctx_v), _ptr(mask),
+                           context_batch, B, S, C_ctx, ada, _ptr(q_norm), _ptr(k_norm),
+                           wd, wsc, wcs, wf)
     if rc != 0:
         raise RuntimeError("reference dit_block failed")
     return x

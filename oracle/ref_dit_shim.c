@@ -46,12 +46,35 @@ int ref_dit_swiglu_int8(const float *x, int rows,
    adaln: 18 fp32 pointers, attention then MLP AdaLN, each in IroAdaLN order;
    wq, wk, wv, gate, wo, w1, w3, w2: int8 weights quantised by the caller with
    iro_int8_weight_quantize.  x [B*S, 1280] is updated in place. */
+int ref_dit_block_w(float *x, const float *cond, const float *ctx_k,
+                    const float *ctx_v, const uint8_t *ctx_mask,
+                    int context_batch, int B, int S, int C,
+                    const float *const *adaln, const float *q_norm,
+                    const float *k_norm, const int8_t *const *wdata,
+                    const float *const *wscale, const int32_t *const *wcolsum,
+                    const float *const *w_fp32);
+
 int ref_dit_block_int8(float *x, const float *cond, const float *ctx_k,
                        const float *ctx_v, const uint8_t *ctx_mask,
                        int context_batch, int B, int S, int C,
                        const float *const *adaln, const float *q_norm,
                        const float *k_norm, const int8_t *const *wdata,
                        const float *const *wscale, const int32_t *const *wcolsum) {
+    return ref_dit_block_w(x, cond, ctx_k, ctx_v, ctx_mask, context_batch, B, S, C,
+                           adaln, q_norm, k_norm, wdata, wscale, wcolsum, NULL);
+}
+
+/* The same block with the fp32 projection weights set as well (w_fp32: wq,
+   wk, wv, gate, wo, w1, w3, w2), for the reference's diagnostic switches
+   IRO_INT8_MASK and IRO_INT8_EMULATE (dit.c:273-335), which it reads from
+   the process environment once. */
+int ref_dit_block_w(float *x, const float *cond, const float *ctx_k,
+                    const float *ctx_v, const uint8_t *ctx_mask,
+                    int context_batch, int B, int S, int C,
+                    const float *const *adaln, const float *q_norm,
+                    const float *k_norm, const int8_t *const *wdata,
+                    const float *const *wscale, const int32_t *const *wcolsum,
+                    const float *const *w_fp32) {
     IroDiT *d = calloc(1, sizeof(IroDiT));
     IroDiTInt8 *q = calloc(1, sizeof(IroDiTInt8));
     if (!d || !q) { free(d); free(q); return -1; }
@@ -64,6 +87,12 @@ int ref_dit_block_int8(float *x, const float *cond, const float *ctx_k,
     }
     d->attention[0].q_norm = q_norm;
     d->attention[0].k_norm = k_norm;
+    if (w_fp32) {
+        d->attention[0].wq = w_fp32[0]; d->attention[0].wk = w_fp32[1];
+        d->attention[0].wv = w_fp32[2]; d->attention[0].gate = w_fp32[3];
+        d->attention[0].wo = w_fp32[4];
+        d->mlp[0].w1 = w_fp32[5]; d->mlp[0].w3 = w_fp32[6]; d->mlp[0].w2 = w_fp32[7];
+    }
     d->norm_eps = 1e-5f;
     IroDiTInt8Layer *l = &q->layer[0];
     const int shapes[8][2] = {{MODEL_DIM, MODEL_DIM}, {MODEL_DIM, MODEL_DIM},
@@ -124,3 +153,8 @@ int ref_dit_output_w(const float *out_norm, const float *out_w, const float *out
 /* The reference's residual-policy switch as it reads it (dit.c:429-436);
    cached per process by the reference. */
 int ref_dit_residual_mask(void) { return dit_int8_residual_mask(); }
+
+/* The reference's diagnostic switches IRO_INT8_MASK and IRO_INT8_EMULATE as
+   its own readers parse them (dit.c:284-304). */
+int ref_dit_int8_mask(void) { return dit_int8_mask(); }
+int ref_dit_int8_emulate(void) { return dit_int8_emulate(); }

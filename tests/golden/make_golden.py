@@ -212,6 +212,49 @@ def dit_block_resid():
     return res
 
 
+# seed, B, S, C, context_batch, IRO_INT8_MASK, IRO_INT8_EMULATE
+DIT_BLOCK_DIAG_CASES = [(41, 2, 20, 12, 1, 0, 0), (42, 1, 40, 9, 1, 5, 0),
+                        (43, 2, 20, 20, 2, 10, 0), (44, 2, 20, 12, 1, 15, 1),
+                        (45, 1, 40, 9, 1, 15, 2), (46, 2, 20, 20, 2, 6, 2)]
+
+
+def dit_block_diag_child(idx, path):
+    """Child process with IRO_INT8_MASK / IRO_INT8_EMULATE set for one case
+    (the reference reads both once per process, dit.c:284-304) and
+    IRO_INT8_RESIDUAL unset (default two-term W2)."""
+    seed, B, S, C, cb, imask, emu = DIT_BLOCK_DIAG_CASES[idx]
+    x, cond, ck, cv, mask, adaln, qn, kn, ws = inputs.dit_block_case(seed, B, S, C, cb)
+    W = [oracle.ref_weight_quantize(w) for w in ws]
+    out = oracle.ref_dit_block(x, cond, ck, cv, mask, cb, B, S, C, adaln, qn, kn, W,
+                               fp32_weights=ws)
+    np.savez(path, out=out, case=np.array(DIT_BLOCK_DIAG_CASES[idx], np.int32),
+             inputs_sha=np.frombuffer(inputs.sha(x, cond, ck, cv, mask, *adaln, qn, kn, *ws),
+                                      np.uint8))
+
+
+def run_dit_block_diag_child(idx, path):
+    """Runs dit_block_diag_child(idx) in a fresh interpreter with the case's
+    switches in its environment."""
+    e = dict(os.environ)
+    e.pop("IRO_INT8_RESIDUAL", None)
+    e["IRO_INT8_MASK"] = str(DIT_BLOCK_DIAG_CASES[idx][5])
+    e["IRO_INT8_EMULATE"] = str(DIT_BLOCK_DIAG_CASES[idx][6])
+    subprocess.run([sys.executable, os.path.abspath(__file__), "--dit-block-diag-child", str(idx),
+                    path], check=True, env=e)
+
+
+def dit_block_diag():
+    res = {}
+    for i in range(len(DIT_BLOCK_DIAG_CASES)):
+        path = os.path.join(HERE, f"_tmp_dit_block_diag_{i}.npz")
+        run_dit_block_diag_child(i, path)
+        g = dict(np.load(path))
+        os.remove(path)
+        for k, v in g.items():
+            res[f"c{i}_{k}"] = v
+    return res
+
+
 def dit_block():
     e = dict(os.environ)
     e.pop("IRO_INT8_RESIDUAL", None)
@@ -258,6 +301,9 @@ def dit_step():
 
 
 def main():
+    if len(sys.argv) > 3 and sys.argv[1] == "--dit-block-diag-child":
+        dit_block_diag_child(int(sys.argv[2]), sys.argv[3])
+        return
     if len(sys.argv) > 2 and sys.argv[1] == "--dit-block-resid-child":
         dit_block_resid_child(int(sys.argv[2]))
         return
@@ -277,7 +323,8 @@ def main():
     for name, fn in (("int8_ops", int8_ops), ("residual", residual), ("conv7", conv7),
                      ("sym_quant", sym), ("dit_swiglu", dit_swiglu), ("convt", convt),
                      ("conv1", conv1), ("dit_block", dit_block),
-                     ("dit_step", dit_step), ("dit_block_resid", dit_block_resid)):
+                     ("dit_step", dit_step), ("dit_block_resid", dit_block_resid),
+                     ("dit_block_diag", dit_block_diag)):
         if only and name not in only:
             continue
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **fn())

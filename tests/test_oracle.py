@@ -184,6 +184,18 @@ def test_golden_dit_block_and_step_reproduced(ref_dit):
                                           [s1, s2]), g["step_out"])
 
 
+def test_golden_dit_block_diag_reproduced(ref_dit, tmp_path):
+    """The diagnostic-mode fixture (IRO_INT8_MASK / IRO_INT8_EMULATE set in
+    a child process, as tests/golden/make_golden.py records it) is what the
+    reference produces now: activation emulation on a mixed mask."""
+    import make_golden
+    idx = 5
+    path = str(tmp_path / "diag.npz")
+    make_golden.run_dit_block_diag_child(idx, path)
+    got, g = np.load(path), load("dit_block_diag")
+    assert same(got["case"], g[f"c{idx}_case"]) and same(got["out"], g[f"c{idx}_out"])
+
+
 def test_reference_dit_block_sensitivity(ref_dit):
     """The int8 block is sensitive to fp32 rounding: a one-ulp perturbation
     of the reference's own input moves its output by about 1e-3 of its

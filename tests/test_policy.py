@@ -22,11 +22,14 @@ import iro_b200 as iro
 import oracle
 L = iro.lib()
 out = {"dit": L.iro_policy_dit_residual_mask(),
+       "dit_diag": [L.iro_policy_dit_fp32_groups(), L.iro_policy_dit_emulate()],
        "codec": [L.iro_policy_codec_int8_mask(), L.iro_policy_codec_residual_mask(),
                  L.iro_policy_codec_residual_stages()],
        "decide": [[L.iro_policy_codec_residual(st, g) for g in (1, 2, 4, 8)] for st in range(4)]}
 if oracle.ref_available("dit"):
-    out["ref_dit"] = oracle.ref_lib("dit").ref_dit_residual_mask()
+    R = oracle.ref_lib("dit")
+    out["ref_dit"] = R.ref_dit_residual_mask()
+    out["ref_dit_diag"] = [15 & ~R.ref_dit_int8_mask(), R.ref_dit_int8_emulate()]
 if oracle.ref_available("codec"):
     R = oracle.ref_lib("codec")
     m, r, s = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
@@ -36,7 +39,7 @@ print(json.dumps(out))
 """
 
 NAMES = ["IRO_INT8_RESIDUAL", "IRO_CODEC_INT8_MASK", "IRO_CODEC_INT8_RESIDUAL",
-         "IRO_CODEC_INT8_RESIDUAL_STAGES"]
+         "IRO_CODEC_INT8_RESIDUAL_STAGES", "IRO_INT8_MASK", "IRO_INT8_EMULATE"]
 
 
 def run_child(value):
@@ -65,6 +68,12 @@ def test_policy_switches_match_reference(value):
 
     expect = (lambda d: d if value in (None, "") else c_strtol(value) & 15)
     assert out["dit"] == expect(8)
+    # IRO_INT8_MASK masked to 4 bits (default 15), complemented into the
+    # block's fp32 groups; IRO_INT8_EMULATE unmasked (default 0).
+    assert out["dit_diag"] == [15 & ~expect(15),
+                               0 if value in (None, "") else c_strtol(value)]
+    if "ref_dit_diag" in out:
+        assert out["dit_diag"] == out["ref_dit_diag"]
     assert out["codec"] == [expect(15), expect(12), expect(8)]
     if "ref_dit" in out:
         assert out["dit"] == out["ref_dit"]
