@@ -39,7 +39,12 @@ enum {
     IRO_ERR_OOM = -4,            /* device or host allocation failed        */
     IRO_ERR_DEVICE_TIMEOUT = -5, /* a bounded in-kernel wait gave up        */
     IRO_ERR_UNSUPPORTED = -6,    /* shape outside what a kernel supports    */
-    IRO_ERR_SELFCHECK = -7       /* the exact-sum probe failed              */
+    IRO_ERR_SELFCHECK = -7,      /* the exact-sum probe failed              */
+    IRO_ERR_RANGE = -8           /* a DiT attention operand (q, k, v, context
+                                    k/v) beyond the fp16 range (|x| >= 65520)
+                                    of the tensor-core attention; the fp32
+                                    attention (IRO_DIT_ATTENTION=simt) takes
+                                    any finite value                         */
 };
 
 /* ======================================================================= */

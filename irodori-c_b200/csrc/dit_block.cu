@@ -279,14 +279,15 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 }
 
 // qk_norm_rope_kernel's work for a tile of 32 tokens of one batch row and one
-// head, plus that tile of V transposed into the attention kernel's per-head
+// head, written as the tensor-core attention's fp16 operands (q16, k16
+// [B*S, D], range-checked), plus that tile of V transposed into the per-head
 // V^T rows (vt[((b * heads + h) * 64 + d) * ld + s], zero for s in [S, ld)).
 // 8 warps x 4 tokens for q and k; V through a shared-memory transpose.
-__global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
-    float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v,
-    float* __restrict__ vt, int S, int D, int heads, int ld, float eps,
-    const float* __restrict__ qw, const float* __restrict__ kw, const float* __restrict__ rcos,
-    const float* __restrict__ rsin) {
+__global__ void __launch_bounds__(256) qk_norm_rope_half_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    __half* __restrict__ q16, __half* __restrict__ k16, __half* __restrict__ vt, int S, int D,
+    int heads, int ld, float eps, const float* __restrict__ qw, const float* __restrict__ kw,
+    const float* __restrict__ rcos, const float* __restrict__ rsin, DevError* err) {
   __shared__ float tile[kHD][33];
   const int s0 = blockIdx.x * 32, hd = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
@@ -336,18 +337,18 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
     const float k0 = __fmul_rn(kv[i].x, __fmul_rn(kinv, kw0));
     const float k1 = __fmul_rn(kv[i].y, __fmul_rn(kinv, kw1));
     const size_t off = ((size_t)b * S + s) * D + hd * kHD + d;
-    if (hd >= heads / 2) {
-      *reinterpret_cast<float2*>(q + off) = make_float2(q0, q1);
-      *reinterpret_cast<float2*>(k + off) = make_float2(k0, k1);
-    } else {
+    float2 qo = make_float2(q0, q1), ko = make_float2(k0, k1);
+    if (hd < heads / 2) {
       const float c = rcos[(size_t)s * (kHD / 2) + lane], sn = rsin[(size_t)s * (kHD / 2) + lane];
-      *reinterpret_cast<float2*>(q + off) =
-          make_float2(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, sn)),
-                      __fadd_rn(__fmul_rn(q0, sn), __fmul_rn(q1, c)));
-      *reinterpret_cast<float2*>(k + off) =
-          make_float2(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, sn)),
-                      __fadd_rn(__fmul_rn(k0, sn), __fmul_rn(k1, c)));
+      qo = make_float2(__fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, sn)),
+                       __fadd_rn(__fmul_rn(q0, sn), __fmul_rn(q1, c)));
+      ko = make_float2(__fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, sn)),
+                       __fadd_rn(__fmul_rn(k0, sn), __fmul_rn(k1, c)));
     }
+    *reinterpret_cast<__half2*>(q16 + off) =
+        __halves2half2(to_half_checked(qo.x, err, 105), to_half_checked(qo.y, err, 105));
+    *reinterpret_cast<__half2*>(k16 + off) =
+        __halves2half2(to_half_checked(ko.x, err, 106), to_half_checked(ko.y, err, 106));
   }
 #pragma unroll
   for (int r = 0; r < 8; r++) {
@@ -358,7 +359,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vt_kernel(
   for (int i = t; i < 32 * kHD; i += 256) {
     const int dd = i / 32, ss = i % 32;
     const int s = s0 + ss;
-    if (s < ld) vt[(((size_t)b * heads + hd) * kHD + dd) * ld + s] = tile[dd][ss];
+    if (s < ld)
+      vt[(((size_t)b * heads + hd) * kHD + dd) * ld + s] = to_half_checked(tile[dd][ss], err, 107);
   }
 }
 
@@ -520,15 +522,12 @@ __global__ void __launch_bounds__(kAThreads) attention_kernel(AttnArgs a) {
 size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
 // IRO_DIT_ATTENTION=simt selects the fp32 CUDA-core attention kernel above
-// (exact fp32 products) instead of the tensor-core one, =pair the
-// tensor-core kernel on CTA pairs (M = 256 MMAs; at config 3 it measured
-// 423 us per layer against 351 for one CTA per 128 queries); the CUDA-core
-// kernel also serves requests the tensor-core one does not take (unaligned
-// context buffers).
+// (exact fp32 products) instead of the tensor-core one (fp16 operands); the
+// CUDA-core kernel also serves requests the tensor-core one does not take
+// (unaligned context buffers).
 int attention_mode() {
   const char* e = getenv("IRO_DIT_ATTENTION");
   if (e && strcmp(e, "simt") == 0) return 1;
-  if (e && strcmp(e, "pair") == 0) return 2;  // CTA pairs, M = 256 MMAs
   return 0;
 }
 
@@ -779,14 +778,13 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       // QKVG on one quantised copy of h (dit.c:785-792).  With the
       // tensor-core attention and the single-term policy, the head norm,
       // RoPE and the V transpose run in the GEMM's epilogue (EPI_QKV).
-      AttnTcRequest ar{q, k, v, g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH,
-                       sw_ws, nullptr, attention_mode() == 2 ? 0 : 1};
+      AttnTcRequest ar{g, ctx_k, ctx_v, ctx_mask, mix, B, S, C, context_batch, D, NH, sw_ws};
       const bool tc = attention_mode() != 1 && attention_tc_supported(ar);
       auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
       const bool fuse_heads =
           tc && !res_qkvg && m_qkvg == DIAG_INT8 && al16(blk->q_norm) && al16(blk->k_norm);
-      float* vt = static_cast<float*>(sw_ws);
-      const int vld = attention_tc_vt_ld(S);
+      // The tensor-core attention's fp16 operands (q, k, V^T) in the tail.
+      const AttnTcOperands ao = attention_tc_operands(ar);
       if (m_qkvg != DIAG_INT8) {
         // The fp32 / emulated projections, one per output (dit.c:780-784,
         // 793-797).
@@ -822,13 +820,15 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
           if ((st = check_launch())) return st;
           rope_t = rope_ws;
         }
-        r.outs[2] = nullptr;
+        r.outs[0] = r.outs[1] = r.outs[2] = nullptr;
         r.hn_q = blk->q_norm;
         r.hn_k = blk->k_norm;
         r.rcos = rope_t;
         r.rsin = rope_t + 32 * (size_t)S;
-        r.vt = vt;
-        r.vt_ld = vld;
+        r.hq = ao.q;
+        r.hk = ao.k;
+        r.hvt = ao.vt;
+        r.vt_ld = ao.ldv;
         r.tokens = S;
         r.eps = blk->norm_eps;
       }
@@ -836,12 +836,12 @@ int dit_block_run(Ctx* c, const IroDiTBlockDev* blk, float* x, const float* cons
       }
       if (tc) {
         if (!fuse_heads) {
-          // Head norm + RoPE with the self V^T rows the attention kernel reads.
-          qk_norm_rope_vt_kernel<<<dim3(cdiv(S, 32), NH, B), 256, 0, s>>>(
-              q, k, v, vt, S, D, NH, vld, blk->norm_eps, blk->q_norm, blk->k_norm, rcos, rsin);
+          // Head norm + RoPE into the fp16 q, k, with the self V^T rows.
+          qk_norm_rope_half_kernel<<<dim3(cdiv(S, 32), NH, B), 256, 0, s>>>(
+              q, k, v, ao.q, ao.k, ao.vt, S, D, NH, ao.ldv, blk->norm_eps, blk->q_norm,
+              blk->k_norm, rcos, rsin, c->err);
           if ((st = check_launch())) return st;
         }
-        ar.vt_self = vt;
         if ((st = attention_tc_launch(c, ar, s))) return st;
       } else {
         qk_norm_rope_kernel<<<cdiv((int)M * NH, 8), 256, 0, s>>>(

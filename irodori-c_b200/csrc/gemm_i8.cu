@@ -106,7 +106,9 @@ struct GemmParams {
   const float* hn_k;
   const float* rcos;
   const float* rsin;
-  float* vt;
+  __half* hq;
+  __half* hk;
+  __half* hvt;
   int vt_ld, tokens, heads;
   float eps;
   DevError* err;
@@ -666,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // warp's 32 consecutive tokens read 512 contiguous bytes.
             const float4* rc4 = reinterpret_cast<const float4*>(p.rcos) + tok;
             const float4* rs4 = reinterpret_cast<const float4*>(p.rsin) + tok;
-            float* drow = p.outs[g] + (size_t)row * p.seg + col0;
+            __half* hrow = (g == 0 ? p.hq : p.hk) + (size_t)row * p.seg + col0;
             for (int ch = 0; ch < 64; ch += kChunk) {
               // This chunk's RoPE groups load before the TMEM read and the
               // dequantisation, which then cover their latency.
@@ -705,10 +707,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                   }
                 }
               }
-              emit(v, &tmO.m[g], col0 + ch, p.seg, drow + ch);
+              if (row_ok) {
+                // 16 halves: two 16-byte stores of this row's chunk.
+                uint32_t hw[kChunk / 2];
+#pragma unroll
+                for (int j = 0; j < kChunk / 2; j++) {
+                  const __half lo = to_half_checked(v[2 * j], p.err, 102 + g);
+                  const __half hi = to_half_checked(v[2 * j + 1], p.err, 102 + g);
+                  hw[j] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(hrow + ch);
+                dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+              }
             }
           } else if (g == 2) {
-            float* vrow = p.vt + (size_t)(seq * p.heads + head) * 64 * p.vt_ld + tok;
+            __half* vrow = p.hvt + (size_t)(seq * p.heads + head) * 64 * p.vt_ld + tok;
             const int pad = (row_ok && tok == p.tokens - 1) ? p.vt_ld - p.tokens : 0;
             for (int ch = 0; ch < 64; ch += kChunk) {
               float v[kChunk];
@@ -716,9 +730,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (row_ok) {
 #pragma unroll
                 for (int j = 0; j < kChunk; j++) {
-                  float* dst = vrow + (size_t)(ch + j) * p.vt_ld;
-                  dst[0] = v[j];
-                  for (int t = 1; t <= pad; t++) dst[t] = 0.0f;
+                  __half* dst = vrow + (size_t)(ch + j) * p.vt_ld;
+                  dst[0] = to_half_checked(v[j], p.err, 104);
+                  for (int t = 1; t <= pad; t++) dst[t] = __float2half_rn(0.0f);
                 }
               }
             }
@@ -1026,12 +1040,11 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
       st = make_tmap_f32_sw128(&om.m[0], r.hidden, (uint64_t)w->hidden, (uint64_t)r.M,
                                (uint64_t)r.ldh * 4);
   } else if (EPI == EPI_QKV) {
-    // q, k and the gate through tile stores; v goes to V^T by direct stores.
-    for (int i : {0, 1, 3}) tma = tma && out_tma_ok(r.outs[i], r.seg);
-    for (int i : {0, 1, 3})
-      if (tma && st == IRO_OK)
-        st = make_tmap_f32_sw128(&om.m[i], r.outs[i], (uint64_t)r.seg, (uint64_t)r.M,
-                                 (uint64_t)r.seg * 4);
+    // The gate through tile stores; q, k and V^T in fp16 by direct stores.
+    tma = out_tma_ok(r.outs[3], r.seg);
+    if (tma)
+      st = make_tmap_f32_sw128(&om.m[3], r.outs[3], (uint64_t)r.seg, (uint64_t)r.M,
+                               (uint64_t)r.seg * 4);
   } else if (EPI == EPI_SPLIT || (EPI == EPI_DUAL && r.nout > 0)) {
     for (int i = 0; i < r.nout && tma; i++) tma = out_tma_ok(r.outs[i], r.seg);
     for (int i = 0; tma && i < r.nout && st == IRO_OK; i++)
@@ -1200,7 +1213,9 @@ static int gemm_launch_impl(Ctx* c, const GemmRequest& r, cudaStream_t s) {
   p.hn_k = r.hn_k;
   p.rcos = r.rcos;
   p.rsin = r.rsin;
-  p.vt = r.vt;
+  p.hq = r.hq;
+  p.hk = r.hk;
+  p.hvt = r.hvt;
   p.vt_ld = r.vt_ld;
   p.tokens = r.tokens;
   p.heads = r.seg / 64;
@@ -1232,14 +1247,14 @@ static int gemm_launch_impl(Ctx* c, const GemmRequest& r, cudaStream_t s) {
       if (r.nout != 4 || r.seg <= 0 || r.seg % 64 != 0 || r.seg * 4 != w->N || r.accumulate ||
           r.bias ||  // the bias slot carries the norm weights
           r.work || r.tokens <= 0 || r.M % r.tokens != 0 || r.vt_ld < r.tokens ||
-          r.vt_ld - r.tokens > 3)
+          r.vt_ld - r.tokens > 7 || r.vt_ld % 8 != 0)
         return IRO_ERR_UNSUPPORTED;
-      if (!r.outs[0] || !r.outs[1] || !r.outs[3] || !r.vt || !r.hn_q || !r.hn_k || !r.rcos ||
-          !r.rsin)
+      if (!r.hq || !r.hk || !r.outs[3] || !r.hvt || !r.hn_q || !r.hn_k || !r.rcos || !r.rsin)
         return IRO_ERR_INVALID;
-      // Vector loads of the norm weights and the grouped RoPE tables.
+      // Vector loads of the norm weights and the grouped RoPE tables, vector
+      // stores of the fp16 q and k rows.
       for (const void* q : {(const void*)r.hn_q, (const void*)r.hn_k, (const void*)r.rcos,
-                            (const void*)r.rsin})
+                            (const void*)r.rsin, (const void*)r.hq, (const void*)r.hk})
         if ((reinterpret_cast<uintptr_t>(q) & 15u) != 0) return IRO_ERR_UNSUPPORTED;
       return launch_t<256, EPI_QKV>(c, r, p, s);
     }

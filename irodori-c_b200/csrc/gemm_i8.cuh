@@ -49,14 +49,19 @@ struct GemmRequest {
   // EPI_QKV: head RMSNorm weights of q and k ([seg], head dim 64, 16-byte
   // aligned), the RoPE tables in groups of four pairs ([8][tokens][4] cos /
   // sin: element ((pair / 4) * tokens + token) * 4 + pair % 4, so a warp's 32
-  // rows read 32 consecutive tokens' groups), the V^T destination ([rows / tokens]
-  // x heads x 64 rows of vt_ld floats; columns tokens..vt_ld-1 are zeroed)
-  // and the norm epsilon.  Row r is token r % tokens of sequence r / tokens.
+  // rows read 32 consecutive tokens' groups) and the norm epsilon.  The
+  // attention operands go out in fp16 (range-checked, IRO_ERR_RANGE): q and
+  // k to hq / hk ([rows, seg], 16-byte aligned), v transposed to hvt
+  // ([rows / tokens] x heads x 64 rows of vt_ld halves, vt_ld a multiple of
+  // 8; columns tokens..vt_ld-1 are zeroed); the gate to outs[3] in fp32.
+  // Row r is token r % tokens of sequence r / tokens.
   const float* hn_q = nullptr;
   const float* hn_k = nullptr;
   const float* rcos = nullptr;
   const float* rsin = nullptr;
-  float* vt = nullptr;
+  __half* hq = nullptr;
+  __half* hk = nullptr;
+  __half* hvt = nullptr;
   int vt_ld = 0;
   int tokens = 0;
   float eps = 0.0f;

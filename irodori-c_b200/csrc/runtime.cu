@@ -188,8 +188,8 @@ static int take_error_word(DevError* word) {
     return IRO_ERR_CUDA;
   }
   if (h.code != 0) {
-    fprintf(stderr, "irodori_b200: device reported error %d (wait site %d, block %d)\n", h.code,
-            h.where, h.block);
+    fprintf(stderr, "irodori_b200: device reported error %d (%s; site %d, block %d)\n", h.code,
+            iro_cuda_error_string(h.code), h.where, h.block);
     if (cudaMemset(word, 0, sizeof(DevError)) != cudaSuccess) cudaGetLastError();
   }
   return h.code;
@@ -306,6 +306,7 @@ const char* iro_cuda_error_string(int code) {
     case IRO_ERR_DEVICE_TIMEOUT: return "bounded device wait gave up";
     case IRO_ERR_UNSUPPORTED: return "unsupported shape or alignment";
     case IRO_ERR_SELFCHECK: return "exact-sum selfcheck failed";
+    case IRO_ERR_RANGE: return "attention operand beyond the fp16 range";
     default: return "unknown";
   }
 }

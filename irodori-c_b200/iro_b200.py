@@ -25,6 +25,7 @@ IRO_ERR_OOM = -4
 IRO_ERR_DEVICE_TIMEOUT = -5
 IRO_ERR_UNSUPPORTED = -6
 IRO_ERR_SELFCHECK = -7
+IRO_ERR_RANGE = -8
 LAYOUT_PLAIN = 0
 LAYOUT_GATED_PAIR = 1
 
