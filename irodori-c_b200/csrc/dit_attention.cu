@@ -115,18 +115,39 @@ struct Args {
   uint64_t limit_ns;
 };
 
+// max(a, b, c) in one instruction (three-input max, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// a * b + c and a + b on packed pairs (fma / add .f32x2, sm_100), each lane
+// rounded as its scalar form.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Two floats as one 32-bit TMEM column of the f16 A operand: element 2i in
-// the low half, 2i + 1 in the high half.
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
 }
 
 template <int N>
@@ -358,13 +379,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
+      // Eight running maxima, two scores per three-input max.
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; i++) mx[i] = __uint_as_float(r[i]);
 #pragma unroll
-      for (int i = 8; i < 64; i++) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
-      float hmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int i = 8; i < 64; i += 16)
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          mx[c] = fmax3(mx[c], __uint_as_float(r[i + c]),
+                        i + 8 + c < 64 ? __uint_as_float(r[i + 8 + c]) : mx[c]);
+      const float hmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                               fmaxf(mx[6], mx[7]));
       // The row maximum over both halves (double-buffered by tile parity: a
       // partner past this tile's barrier has read the previous tile's slot).
       xmax[((j & 1) * 2 + hf) * kQ + row] = hmax;
@@ -400,17 +426,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           m = mnew;
         }
       }
-      float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const float neg_m = -m;
+      // Pairs of keys through the packed f32x2 FMA and add: t = s * c - m,
+      // p = 2^t, per-lane sums in two pairs of accumulators.
+      float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      const float2 scale2 = make_float2(kScaleLog2, kScaleLog2), negm2 = make_float2(-m, -m);
 #pragma unroll
       for (int i = 0; i < 32; i++) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(r[2 * i]), kScaleLog2, neg_m));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), kScaleLog2, neg_m));
-        ps[(2 * i) & 3] += p0;
-        ps[(2 * i + 1) & 3] += p1;
-        r[i] = pack_half2(p0, p1);  // that score was read at pair i / 2
+        const float2 t = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                               scale2, negm2);
+        const float2 pp = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+        ps[i & 1] = fadd2(ps[i & 1], pp);
+        r[i] = pack_half2_rn(pp.x, pp.y);  // fp16 pair of the A operand: key 2i low, 2i + 1 high
       }
-      l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      l += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
       // P_j goes over P_{j-1} once PV_{j-1} has read it.
       if (j > 0 && !pv_waited) {
         ok = mbar_wait_bounded(pv_done, (j - 1) & 1, a.err, 12, abort_flag, a.limit_ns);

@@ -461,6 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64; // 0..511
     uint8_t* stg_mine = stg_base + e * kStgBufs * kStgBytes;
     int sbuf = 0;  // next staging tile of this warp
+    bool head_pending = false;  // EPI_QKV: a whole-head store may still read both buffers
     int acc = 0;
     uint32_t aph = 0;
     int pbuf = 0;
@@ -586,7 +587,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           // for that one (at most kStgBufs - 1 stores stay in flight).
           uint8_t* stg = stg_mine + sbuf * kStgBytes;
           sbuf = sbuf + 1 == kStgBufs ? 0 : sbuf + 1;
-          if (lane == 0) bulk_wait_read<kStgBufs - 1>();
+          if (lane == 0) {
+            if (EPI == EPI_QKV && head_pending) bulk_wait_read<0>();
+            else bulk_wait_read<kStgBufs - 1>();
+          }
+          head_pending = false;
           __syncwarp();
           stage_row16(stg, lane, v);
           fence_async_shared();
@@ -669,6 +674,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float4* rc4 = reinterpret_cast<const float4*>(p.rcos) + tok;
             const float4* rs4 = reinterpret_cast<const float4*>(p.rsin) + tok;
             __half* hrow = (g == 0 ? p.hq : p.hk) + (size_t)row * p.seg + col0;
+            if (p.tma_out) {
+              // The warp's 32 rows x 64 halves go out as one tile store from
+              // both staging buffers (4 KB, rows of 128 bytes in the 128-byte
+              // swizzle); every earlier store of this warp has read them.
+              if (lane == 0) bulk_wait_read<0>();
+              __syncwarp();
+            }
             for (int ch = 0; ch < 64; ch += kChunk) {
               // This chunk's RoPE groups load before the TMEM read and the
               // dequantisation, which then cover their latency.
@@ -707,19 +719,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                   }
                 }
               }
-              if (row_ok) {
-                // 16 halves: two 16-byte stores of this row's chunk.
-                uint32_t hw[kChunk / 2];
+              uint32_t hw[kChunk / 2];
 #pragma unroll
-                for (int j = 0; j < kChunk / 2; j++) {
-                  const __half lo = to_half_checked(v[2 * j], p.err, 102 + g);
-                  const __half hi = to_half_checked(v[2 * j + 1], p.err, 102 + g);
-                  hw[j] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-                }
+              for (int j = 0; j < kChunk / 2; j++) hw[j] = pack_half2_rn(v[2 * j], v[2 * j + 1]);
+              check_half_range(v, p.err, 102 + g);
+              if (p.tma_out) {
+                // 16-byte chunks c, c + 1 of this lane's row, swizzled.
+                uint8_t* srow = stg_mine + lane * 128;
+                const int c = ch >> 3;
+                *reinterpret_cast<uint4*>(srow + ((c ^ (lane & 7)) << 4)) =
+                    make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(srow + (((c + 1) ^ (lane & 7)) << 4)) =
+                    make_uint4(hw[4], hw[5], hw[6], hw[7]);
+              } else if (row_ok) {
                 uint4* dst = reinterpret_cast<uint4*>(hrow + ch);
                 dst[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                 dst[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
               }
+            }
+            if (p.tma_out) {
+              fence_async_shared();
+              __syncwarp();
+              if (lane == 0 && row0 < p.M) {
+                tma_store_2d(&tmO.m[g], stg_mine, col0, row0);
+                bulk_commit();
+              }
+              __syncwarp();
+              sbuf = 0;
+              head_pending = true;  // the next staging write waits for this read
             }
           } else if (g == 2) {
             __half* vrow = p.hvt + (size_t)(seq * p.heads + head) * 64 * p.vt_ld + tok;
@@ -728,10 +755,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               float v[kChunk];
               deq(c0 + ch, v);
               if (row_ok) {
+                check_half_range(v, p.err, 104);
 #pragma unroll
                 for (int j = 0; j < kChunk; j++) {
                   __half* dst = vrow + (size_t)(ch + j) * p.vt_ld;
-                  dst[0] = to_half_checked(v[j], p.err, 104);
+                  dst[0] = __float2half_rn(v[j]);
                   for (int t = 1; t <= pad; t++) dst[t] = __float2half_rn(0.0f);
                 }
               }
@@ -1040,11 +1068,19 @@ static int launch_t(Ctx* c, const GemmRequest& r, const GemmParams& p0, cudaStre
       st = make_tmap_f32_sw128(&om.m[0], r.hidden, (uint64_t)w->hidden, (uint64_t)r.M,
                                (uint64_t)r.ldh * 4);
   } else if (EPI == EPI_QKV) {
-    // The gate through tile stores; q, k and V^T in fp16 by direct stores.
+    // The gate and the fp16 q, k through tile stores (q, k: one 32-row x
+    // 64-half head per warp, 128-byte swizzle); V^T by direct stores.
     tma = out_tma_ok(r.outs[3], r.seg);
     if (tma)
       st = make_tmap_f32_sw128(&om.m[3], r.outs[3], (uint64_t)r.seg, (uint64_t)r.M,
                                (uint64_t)r.seg * 4);
+    for (int i = 0; i < 2 && tma && st == IRO_OK; i++) {
+      const cuuint64_t dims[2] = {(cuuint64_t)r.seg, (cuuint64_t)r.M};
+      const cuuint64_t strides[1] = {(cuuint64_t)r.seg * 2};
+      const cuuint32_t box[2] = {64, 32};
+      st = encode_tmap(&om.m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, i == 0 ? r.hq : r.hk, dims,
+                       strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
   } else if (EPI == EPI_SPLIT || (EPI == EPI_DUAL && r.nout > 0)) {
     for (int i = 0; i < r.nout && tma; i++) tma = out_tma_ok(r.outs[i], r.seg);
     for (int i = 0; tma && i < r.nout && st == IRO_OK; i++)

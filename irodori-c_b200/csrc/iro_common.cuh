@@ -42,6 +42,24 @@ __device__ __forceinline__ __half to_half_checked(float x, DevError* err, int wh
   return __float2half_rn(x);
 }
 
+// Two floats as packed halves (lo in the low 16 bits), round to nearest.
+__device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// to_half_checked's range check for a chunk of values at once: the largest
+// finite magnitude against 65520 (a chunk holding an inf is not reported;
+// the inf passes through as in fp32).
+template <int N>
+__device__ __forceinline__ void check_half_range(const float (&v)[N], DevError* err, int where) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < N; i++) amax = fmaxf(amax, fabsf(v[i]));
+  if (amax >= 65520.0f && amax != __int_as_float(0x7f800000)) report_error(err, IRO_ERR_RANGE, where);
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
