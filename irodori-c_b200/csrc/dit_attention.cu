@@ -160,7 +160,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmCK,
-                        const __grid_constant__ CUtensorMap tmCV, const Args a) {
+                        const __grid_constant__ CUtensorMap tmCV,
+                        const __grid_constant__ CUtensorMap tmG, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -178,7 +179,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* p_full = bars + 11;    // P_j in TMEM (256 arrivals)
   uint64_t* pv_done = bars + 12;   // PV_j complete (P free, O quiescent)
   uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* xbar = bars + 14;      // 4: the softmax partners of each TMEM quadrant (64 arrivals)
+  uint64_t* g_full = bars + 18;    // the gate tile in the freed K stages
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* ctx_bits = reinterpret_cast<uint32_t*>(smem + kBarOff + 256);
 
@@ -201,6 +204,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(p_full, 256);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < 4; i++) mbar_init(&xbar[i], 64);
+    mbar_init(g_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -210,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmCK);
     tma_prefetch_desc(&tmCV);
+    tma_prefetch_desc(&tmG);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -256,9 +262,27 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         issued = j + 1;
       }
+      // The gate tile [128 rows x 64 dims] fp32, for the epilogue, into the
+      // two K stages once the last S products have read them (dims 32 c ..
+      // 32 c + 31 into stage c, 128-byte swizzled rows).
+      bool g_issued = false;
+      if (lane == 0 && issued == T) {
+        bool ok = true;
+        for (int j = T - 1; ok && j >= 0 && j >= T - kStages; j--)
+          ok = mbar_wait_bounded(&k_empty[j & 1], (j >> 1) & 1, a.err, 15, abort_flag,
+                                 a.limit_ns);
+        if (ok) {
+          mbar_arrive_expect_tx(g_full, kStages * kKBytes);
+#pragma unroll
+          for (int c = 0; c < 2; c++)
+            tma_load_2d(sK + c * kKBytes, &tmG, g_full, hd * kDH + 32 * c, b * a.S + q0);
+          g_issued = true;
+        }
+      }
       // Drain: every load issued has landed before the CTA may exit (on the
       // normal path these phases completed long ago).
       if (lane == 0) mbar_wait_bounded(q_full, 0, a.err, 9, nullptr, a.limit_ns);
+      if (g_issued) mbar_wait_bounded(g_full, 0, a.err, 9, nullptr, a.limit_ns);
       for (int j = issued - 1; j >= 0 && j >= issued - kStages; j--)
         mbar_wait_bounded(&full[j & 1], (j >> 1) & 1, a.err, 9, nullptr, a.limit_ns);
     }
@@ -318,9 +342,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---------------- softmax + epilogue (8 warps) ----------------
     // Two threads per query row: warps 2-5 take keys 0-63 of each tile,
     // warps 6-9 keys 64-127 (a warp reads the TMEM lanes of quadrant warp % 4).
-    // The partners meet once per tile, on a named barrier of the quadrant's
-    // two warps, to share the row maximum; l is summed per half and added at
-    // the end.
+    // The partners meet once per tile on their quadrant's mbarrier (phase j
+    // for tile j, phase T for the final sums) to share the row maximum; l is
+    // summed per half and added at the end.  The meeting is a bounded wait
+    // like every other one, so a partner that gave up cannot strand the
+    // other (a hardware named barrier would wait for it forever).
     const int quad = warp & 3;          // TMEM lanes 32*quad .. 32*quad+31
     const int hf = (warp - 2) >> 2;     // key half of each tile
     const int row = quad * 32 + lane;
@@ -330,17 +356,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t colS = kColS + 64u * hf, colP = kColP + 32u * hf, colO = kColO + 32u * hf;
     float* xmax = reinterpret_cast<float*>(ctx_bits + kMaxCtxWords);  // [2 tiles][2 halves][128]
     float* xl = xmax + 2 * 2 * kQ;                                   // [2 halves][128]
-    // The batch row's context mask as bits (dit.c:828-839).
+    // The batch row's context mask as bits (dit.c:828-839): word w from one
+    // coalesced 32-byte load and a ballot, words spread over the 8 warps.
     {
       const uint8_t* mrow = a.mask + (size_t)b * a.C;
       const int nw = a.n_ctx * (kKT / 32);  // whole tiles; bits past C stay 0
-      for (int w = st_id; w < nw; w += 256) {
-        uint32_t bits = 0;
-        for (int k = 0; k < 32; k++) {
-          const int c = w * 32 + k;
-          if (c < a.C && mrow[c] != 0) bits |= 1u << k;
-        }
-        ctx_bits[w] = bits;
+      for (int w = (warp - 2); w < nw; w += 8) {
+        const int c = w * 32 + lane;
+        const uint32_t bits = __ballot_sync(0xffffffffu, c < a.C && mrow[c] != 0);
+        if (lane == 0) ctx_bits[w] = bits;
       }
       named_bar(1, 256);
     }
@@ -394,7 +418,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       // The row maximum over both halves (double-buffered by tile parity: a
       // partner past this tile's barrier has read the previous tile's slot).
       xmax[((j & 1) * 2 + hf) * kQ + row] = hmax;
-      named_bar(2 + quad, 64);
+      mbar_arrive(&xbar[quad]);
+      ok = mbar_wait_bounded(&xbar[quad], j & 1, a.err, 13, abort_flag, a.limit_ns);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
       const float rmax = fmaxf(hmax, xmax[((j & 1) * 2 + (hf ^ 1)) * kQ + row]);
       const float mnew = fmaxf(m, rmax * kScaleLog2);
       const bool need = mnew > m + kRescaleGap;
@@ -456,27 +485,33 @@ __global__ void __launch_bounds__(kThreads, 2)
     // The row's l: both halves summed with the same maxima.
     if (ok) {
       xl[hf * kQ + row] = l;
-      named_bar(2 + quad, 64);
-      l += xl[(hf ^ 1) * kQ + row];
-      ok = mbar_wait_bounded(pv_done, (T - 1) & 1, a.err, 11, abort_flag, a.limit_ns);
+      mbar_arrive(&xbar[quad]);
+      ok = mbar_wait_bounded(&xbar[quad], T & 1, a.err, 14, abort_flag, a.limit_ns);
       ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        l += xl[(hf ^ 1) * kQ + row];
+        ok = mbar_wait_bounded(pv_done, (T - 1) & 1, a.err, 11, abort_flag, a.limit_ns);
+        ok = __all_sync(0xffffffffu, ok);
+      }
     }
     if (ok) {
       tc_fence_after();
       uint32_t o[32];
       tmem_ld_32x32b_x32(lane_base + colO, o);
       tmem_ld_wait();
-      if (qrow < a.S) {
-        // Dimensions 32 hf .. 32 hf + 31 of the head.  The sigmoid gate in
+      ok = mbar_wait_bounded(g_full, 0, a.err, 16, abort_flag, a.limit_ns);
+      if (ok && qrow < a.S) {
+        // Dimensions 32 hf .. 32 hf + 31 of the head; the gate from K stage
+        // hf (16-byte chunk i of the row at i ^ (row & 7)).  The sigmoid in
         // fast single-precision form (ex2.approx-based exp and division,
         // relative error ~1e-6, far under the fp16 operands' rounding).
         const size_t off = ((size_t)b * a.S + qrow) * a.D + (size_t)hd * kDH + 32 * hf;
-        const float4* gr = reinterpret_cast<const float4*>(a.g + off);
+        const uint8_t* grow = sK + hf * kKBytes + row * kRow;
         float4* out = reinterpret_cast<float4*>(a.mix + off);
         const float inv_l = __fdiv_rn(1.0f, l);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-          const float4 gv = gr[i];
+          const float4 gv = *reinterpret_cast<const float4*>(grow + ((i ^ (row & 7)) << 4));
           float4 ov;
           ov.x = __uint_as_float(o[4 * i]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.x));
           ov.y = __uint_as_float(o[4 * i + 1]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.y));
@@ -571,6 +606,15 @@ int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
   if (!st) st = map2d_h(&mv, o.vt, o.ldv, (long long)r.B * r.D, kDH);
   if (!st) st = map2d_h(&mck, o.ck, r.D, crows, kKT);
   if (!st) st = map2d_h(&mcv, o.cvt, o.ldc, (long long)r.context_batch * r.D, kDH);
+  CUtensorMap mg;
+  if (!st) {
+    // The gate: fp32 [B*S, D], boxes of 32 floats (128 bytes) x 128 rows.
+    const cuuint64_t dims[2] = {(cuuint64_t)r.D, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)r.D * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)kQ};
+    st = encode_tmap(&mg, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, r.g, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (st) return st;
   Args a;
   a.S = r.S;
@@ -587,7 +631,7 @@ int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
   a.limit_ns = kWaitLimitNs;
   const dim3 grid(cdiv(r.S, kQ), r.heads, r.B);
   cudaError_t e = launch_pdl(attention_tc_kernel, grid, dim3(kThreads), (size_t)kSmem, s, mq, mk,
-                             mv, mck, mcv, a);
+                             mv, mck, mcv, mg, a);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return map_cuda(e);
