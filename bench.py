@@ -960,7 +960,7 @@ def run_dit(args):
         return
     res.update({"metric": "DiT Euler steps/sec", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-                "dtype": "int8 GEMMs, tf32 attention (fp32 accumulate)",
+                "dtype": "int8 GEMMs, fp16-operand attention (fp32 accumulate)",
                 "data": "synthetic (random-init weights, N(0,1) latents)"})
     print(json.dumps(res), flush=True)
 

@@ -31,12 +31,12 @@
 // only raised (and O rescaled in TMEM) when a tile's maximum exceeds it by
 // more than log2(e^8), so p <= e^8 (well inside fp16) and O is rescaled a
 // handful of times per row.  Since p / sum p does not depend on m, this
-// changes rounding only.  fp16 keeps the 10-bit mantissa of tf32, so the
-// products carry tf32's rounding (about 1e-3 relative on the attention
-// output) against exact fp32 products in attention_kernel (dit_block.cu,
-// IRO_DIT_ATTENTION=simt); the operands must stay below 65520 in magnitude,
-// which every producer checks (IRO_ERR_RANGE).  p below 2^-14 is stored as
-// an fp16 subnormal: an absolute error under 2^-25 against l >= 1.
+// changes rounding only.  The operands are rounded to fp16 (10-bit
+// mantissa) when they are written, against exact fp32 products in
+// attention_kernel (dit_block.cu, IRO_DIT_ATTENTION=simt); they must stay
+// below 65520 in magnitude, which every producer checks (IRO_ERR_RANGE).
+// p below 2^-14 is stored as an fp16 subnormal: an absolute error under
+// 2^-25 against l >= 1.
 //
 // Every wait is bounded (DevError + abort flag); on give-up each role drains
 // what it issued before the TMEM is freed.

@@ -7,8 +7,8 @@
 //   QKVG           (dit.c:785-792)           one int8 GEMM, four outputs
 //   head RMSNorm + half RoPE (dit.c:638-706) qk_norm_rope_kernel
 //   joint attention, sigmoid gate (dit.c:806-862)  attention_tc_kernel
-//                  (dit_attention.cu; tf32 tensor cores), or attention_kernel
-//                  (fp32 CUDA cores)
+//                  (dit_attention.cu; tensor cores, fp16 operands, fp32
+//                  accumulation), or attention_kernel (fp32 CUDA cores)
 //   Wo             (dit.c:876-884)           int8 GEMM
 //   gated residual (dit.c:1013-1020)         in the Wo and W2 GEMM epilogues
 //   SwiGLU         (dit.c:913-969)           iro_int8_swiglu_dev

@@ -445,35 +445,6 @@ __device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t m
   return d;
 }
 
-// Instruction descriptor for kind::tf32: D = f32, A = B = tf32, A K-major,
-// B K-major (b_mn = 0) or MN-major (1), shape M x N.
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, int b_mn) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)b_mn << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-// D[tmem] (+)= A[smem] . B[smem]^T, kind::tf32 (fp32 operands read as tf32).
-__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] . B[smem]^T, kind::tf32, A = 128 lanes x K columns.
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // Instruction descriptor for kind::f16 with f16 operands: D = f32, A = B =
 // f16, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {

@@ -25,7 +25,7 @@ So the tests print the error against the absolute gates and assert against
 the envelope: per step, max and mean velocity error within 2.5x the
 reference's own one-ulp response at that step (one random perturbation, so
 its max is itself noisy); the final latent likewise.  Both attention kernels
-are run: the default tensor-core one (tf32 operands) and
+are run: the default tensor-core one (fp16 operands) and
 IRO_DIT_ATTENTION=simt (exact fp32 products)."""
 import os
 import sys
