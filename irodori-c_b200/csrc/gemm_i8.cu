@@ -659,13 +659,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           };
           if (g < 2) {
+            // Pass 1: the mean square; each dequantised chunk goes back over
+            // its accumulator in TMEM (this tile's columns, this warp's lanes),
+            // so pass 2 reads it instead of dequantising again.
             float ms = 0.0f;
             for (int ch = 0; ch < 64; ch += kChunk) {
               float v[kChunk];
               deq(c0 + ch, v);
 #pragma unroll
               for (int j = 0; j < kChunk; j++) ms = __fadd_rn(ms, __fmul_rn(v[j], v[j]));
+              tmem_st_32x32b_x16(tbase + c0 + ch, reinterpret_cast<const uint32_t(&)[kChunk]>(v));
             }
+            tmem_st_wait();
             const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, 64.0f), p.eps)));
             const bool rope = head < p.heads / 2;
             // RoPE tables in groups of four pairs, [8][tokens][4]: one vector
@@ -682,8 +687,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
             }
             for (int ch = 0; ch < 64; ch += kChunk) {
-              // This chunk's RoPE groups load before the TMEM read and the
-              // dequantisation, which then cover their latency.
+              // This chunk's RoPE groups load before the TMEM read, which
+              // then covers their latency.
               float4 c4[2], s4[2];
               if (rope) {
 #pragma unroll
@@ -694,7 +699,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
               float v[kChunk];
-              deq(c0 + ch, v);
+              tmem_ld_32x32b_x16(tbase + c0 + ch, reinterpret_cast<uint32_t(&)[kChunk]>(v));
+              tmem_ld_wait();
 #pragma unroll
               for (int j = 0; j < kChunk; j += 4) {
                 // Norm weights staged with the tile's column parameters.

@@ -1,5 +1,5 @@
-"""A step split across ranks by CFG branch (fewer requests than GPUs,
-SURVEY-level option of sharding one request's CFG rows): each rank runs
+"""A step split across ranks by CFG branch (fewer requests than GPUs: one
+request's CFG rows sharded across the ranks): each rank runs
 iro_dit_velocity_dev on its own branches (their mask rows), the velocities
 meet by an all-gather in branch order, and iro_dit_cfg_update_dev applies
 the guided Euler update (sampler.c:283-297).  Two gloo ranks share cuda:0
