@@ -201,8 +201,7 @@ __global__ void __launch_bounds__(256) adaln_quant_kernel(const float* __restric
   for (int i = 0; i < V; i++) {
     const int j = i * 32 + lane;
     if (j < D4)
-      dst[j] = quant_code(v[i].x, qinv, zpf) | (quant_code(v[i].y, qinv, zpf) << 8) |
-               (quant_code(v[i].z, qinv, zpf) << 16) | (quant_code(v[i].w, qinv, zpf) << 24);
+      dst[j] = quant_code4(v[i], qinv, zpf);
   }
   if (lane == 0) {
     qs[row] = s;

@@ -94,11 +94,23 @@ __device__ __forceinline__ void row_params(float lo, float hi, float& s,
 }
 
 // One asymmetric code: clamp(rint(x*inv + zp), 0, 255); NaN -> 0 as the
-// reference's (uint8_t) cast gives on x86-64.  The clamp is fmaxf/fminf,
-// whose NaN rule (the non-NaN operand wins) sends a NaN to 0 as well.
+// reference's (uint8_t) cast gives on x86-64.  t = x*inv + zp is rounded as
+// the reference rounds it; clamping t to [0, 255] before rounding gives the
+// same code (rint is monotone and keeps 0 and 255; fmaxf sends a NaN to 0),
+// and the rounding is one add of 1.5 * 2^23: for t in [0, 255] the sum is
+// exactly 1.5 * 2^23 + rint(t) (ties to even, as nearbyintf), so the code is
+// the low byte of its bits and the rounded value is the sum minus 1.5 * 2^23.
+// No float<->int conversions (which issue at half rate).
+constexpr float kRintMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr uint32_t kRintMagicBits = 0x4B400000u;
+
+__device__ __forceinline__ float quant_round(float x, float inv, float zpf) {
+  const float t = fminf(fmaxf(__fadd_rn(__fmul_rn(x, inv), zpf), 0.0f), 255.0f);
+  return __fadd_rn(t, kRintMagic);
+}
+
 __device__ __forceinline__ uint32_t quant_code(float x, float inv, float zpf) {
-  const float v = fminf(fmaxf(rintf(__fadd_rn(__fmul_rn(x, inv), zpf)), 0.0f), 255.0f);
-  return (uint32_t)__float2int_rz(v);
+  return __float_as_uint(quant_round(x, inv, zpf)) - kRintMagicBits;
 }
 
 // The same code, also returning the clamped float value (the conv's
@@ -106,9 +118,26 @@ __device__ __forceinline__ uint32_t quant_code(float x, float inv, float zpf) {
 // this gives 0; the remainder is NaN either way (it subtracts from x).
 __device__ __forceinline__ uint32_t quant_code_v(float x, float inv, float zpf,
                                                  float& vout) {
-  const float v = fminf(fmaxf(rintf(__fadd_rn(__fmul_rn(x, inv), zpf)), 0.0f), 255.0f);
-  vout = v;
-  return (uint32_t)__float2int_rz(v);
+  const float m = quant_round(x, inv, zpf);
+  vout = __fsub_rn(m, kRintMagic);
+  return __float_as_uint(m) - kRintMagicBits;
+}
+
+// Four codes packed little-endian (x in the low byte), with the rounded
+// values (for the two-term residual) in r.
+__device__ __forceinline__ uint32_t quant_code4(float4 x, float inv, float zpf, float4& r) {
+  const float m0 = quant_round(x.x, inv, zpf), m1 = quant_round(x.y, inv, zpf);
+  const float m2 = quant_round(x.z, inv, zpf), m3 = quant_round(x.w, inv, zpf);
+  r = make_float4(__fsub_rn(m0, kRintMagic), __fsub_rn(m1, kRintMagic),
+                  __fsub_rn(m2, kRintMagic), __fsub_rn(m3, kRintMagic));
+  const uint32_t lo = __byte_perm(__float_as_uint(m0), __float_as_uint(m1), 0x0040);
+  const uint32_t hi = __byte_perm(__float_as_uint(m2), __float_as_uint(m3), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
+__device__ __forceinline__ uint32_t quant_code4(float4 x, float inv, float zpf) {
+  float4 r;
+  return quant_code4(x, inv, zpf, r);
 }
 
 // Running min/max of a row.  The reference updates with strict comparisons

@@ -123,15 +123,14 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec(QuantArgs a) {
   for (int i = 0; i < V; i++) {
     const int j = i * kQThreads + tid;
     if (j < K4) {
-      const uint32_t c0 = quant_code(v[i].x, inv, zpf), c1 = quant_code(v[i].y, inv, zpf);
-      const uint32_t c2 = quant_code(v[i].z, inv, zpf), c3 = quant_code(v[i].w, inv, zpf);
-      dst[j] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+      float4 q;
+      dst[j] = quant_code4(v[i], inv, zpf, q);
       if (MODE == QM_RESID) {
         // ops.c:436-439: r = x - s*((float)q - zp), in place of x.
-        v[i].x = __fsub_rn(v[i].x, __fmul_rn(s, __fsub_rn((float)c0, zpf)));
-        v[i].y = __fsub_rn(v[i].y, __fmul_rn(s, __fsub_rn((float)c1, zpf)));
-        v[i].z = __fsub_rn(v[i].z, __fmul_rn(s, __fsub_rn((float)c2, zpf)));
-        v[i].w = __fsub_rn(v[i].w, __fmul_rn(s, __fsub_rn((float)c3, zpf)));
+        v[i].x = __fsub_rn(v[i].x, __fmul_rn(s, __fsub_rn(q.x, zpf)));
+        v[i].y = __fsub_rn(v[i].y, __fmul_rn(s, __fsub_rn(q.y, zpf)));
+        v[i].z = __fsub_rn(v[i].z, __fmul_rn(s, __fsub_rn(q.z, zpf)));
+        v[i].w = __fsub_rn(v[i].w, __fmul_rn(s, __fsub_rn(q.w, zpf)));
       }
     }
   }
@@ -162,9 +161,7 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_vec(QuantArgs a) {
 #pragma unroll
   for (int i = 0; i < V; i++) {
     const int j = i * kQThreads + tid;
-    if (j < K4)
-      dst2[j] = quant_code(v[i].x, inv2, zpf2) | (quant_code(v[i].y, inv2, zpf2) << 8) |
-                (quant_code(v[i].z, inv2, zpf2) << 16) | (quant_code(v[i].w, inv2, zpf2) << 24);
+    if (j < K4) dst2[j] = quant_code4(v[i], inv2, zpf2);
   }
   if (tid == 0) {
     a.scale2[row] = s2;
