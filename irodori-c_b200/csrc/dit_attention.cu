@@ -60,9 +60,8 @@ constexpr int kVBytes = (kKT / 64) * kVChunk;  // 16 KB
 constexpr int kStages = 2;
 constexpr int kBarOff = kQBytes + kStages * (kKBytes + kVBytes);  // 80 KB of tiles
 constexpr int kMaxCtxWords = 256;            // context mask bits in shared memory (C <= 8192)
-// Barriers, the context mask bits, then the softmax partners' row maxima
-// (2 tiles x 2 halves x 128) and sums (2 x 128).
-constexpr int kSmem = 1024 + kBarOff + 256 + 4 * kMaxCtxWords + 4 * (4 * kQ + 2 * kQ);
+// Barriers, then the context mask bits.
+constexpr int kSmem = 1024 + kBarOff + 256 + 4 * kMaxCtxWords;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColP = 128, kColO = 192;
 // Scores are kept in the log2 domain: t = s_raw * (1/8) * log2(e), p = 2^(t - m).
@@ -144,6 +143,38 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return d;
 }
 
+// 16-lane TMEM shapes (a warp reads 16 lanes from its lane base, four
+// threads per lane; thread t holds lanes base + t / 4 and base + t / 4 + 8):
+//   16x256b: per 8-column repetition c, the registers 4c .. 4c + 3 are
+//            (lane t/4, columns 8c + 2(t%4) and + 1), then (lane t/4 + 8,
+//            the same two columns);
+//   16x128b: per 4-column repetition c, registers 2c, 2c + 1 are lane t/4 and
+//            lane t/4 + 8 at column 4c + t%4.
+__device__ __forceinline__ void tmem_ld_16x256b_x16(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_16x128b_x16(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.16x128b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+               : "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -179,9 +210,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* p_full = bars + 11;    // P_j in TMEM (256 arrivals)
   uint64_t* pv_done = bars + 12;   // PV_j complete (P free, O quiescent)
   uint64_t* drain = bars + 13;
-  uint64_t* xbar = bars + 14;      // 4: the softmax partners of each TMEM quadrant (64 arrivals)
-  uint64_t* g_full = bars + 18;    // the gate tile in the freed K stages
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* g_full = bars + 14;    // the gate tile in the freed K stages
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint32_t* ctx_bits = reinterpret_cast<uint32_t*>(smem + kBarOff + 256);
 
@@ -204,7 +234,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(p_full, 256);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
-    for (int i = 0; i < 4; i++) mbar_init(&xbar[i], 64);
     mbar_init(g_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -340,22 +369,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   } else {
     // ---------------- softmax + epilogue (8 warps) ----------------
-    // Two threads per query row: warps 2-5 take keys 0-63 of each tile,
-    // warps 6-9 keys 64-127 (a warp reads the TMEM lanes of quadrant warp % 4).
-    // The partners meet once per tile on their quadrant's mbarrier (phase j
-    // for tile j, phase T for the final sums) to share the row maximum; l is
-    // summed per half and added at the end.  The meeting is a bounded wait
-    // like every other one, so a partner that gave up cannot strand the
-    // other (a hardware named barrier would wait for it forever).
-    const int quad = warp & 3;          // TMEM lanes 32*quad .. 32*quad+31
-    const int hf = (warp - 2) >> 2;     // key half of each tile
-    const int row = quad * 32 + lane;
-    const int qrow = q0 + row;
+    // Each warp owns 16 query rows (TMEM lanes 32 * (warp % 4) + 16 * sub ..
+    // + 15) with four threads per row, through the 16-lane TMEM shapes:
+    // thread t holds rows t / 4 and t / 4 + 8 of the warp's 16, and of each
+    // 8-key group the two keys 2(t%4), 2(t%4) + 1.  The four threads of a row
+    // share its maximum and sum by shuffles.
+    const int quad = warp & 3;
+    const int sub = (warp - 2) >> 2;
     const int st_id = threadIdx.x - 64;  // 0..255
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t colS = kColS + 64u * hf, colP = kColP + 32u * hf, colO = kColO + 32u * hf;
-    float* xmax = reinterpret_cast<float*>(ctx_bits + kMaxCtxWords);  // [2 tiles][2 halves][128]
-    float* xl = xmax + 2 * 2 * kQ;                                   // [2 halves][128]
+    const int jj = lane & 3;             // key pair within each 8-key group
+    const int lbase = quad * 32 + sub * 16;
+    const int rr0 = lbase + (lane >> 2), rr1 = rr0 + 8;  // this thread's two rows
+    const uint32_t lane_addr = tmem + ((uint32_t)lbase << 16);
     // The batch row's context mask as bits (dit.c:828-839): word w from one
     // coalesced 32-byte load and a ballot, words spread over the 8 warps.
     {
@@ -368,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       named_bar(1, 256);
     }
-    float m = -INFINITY, l = 0.0f;  // running max (log2 domain) and this half's sum
+    float m0 = -INFINITY, m1 = -INFINITY;  // running maxima (log2 domain) of the two rows
+    float l0 = 0.0f, l1 = 0.0f;            // this thread's share of their sums
     bool ok = true;
     for (int j = 0; j < T; j++) {
       ok = mbar_wait_bounded(s_full, j & 1, a.err, 7, abort_flag, a.limit_ns);
@@ -378,58 +404,66 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       tc_fence_after();
       uint32_t r[64];
-      tmem_ld_32x32b_x32(lane_base + colS, sub32(r, 0));
-      tmem_ld_32x32b_x32(lane_base + colS + 32u, sub32(r, 1));
+      tmem_ld_16x256b_x16(lane_addr + kColS, r);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(s_free);  // the MMA warp may overwrite S with S_{j+1}
-      // Keys outside the row's set get -inf (their p is exactly 0).
+      // Keys outside the row's set get -inf (their p is exactly 0); key
+      // 8c + 2jj + e sits in registers 4c + e (row 0) and 4c + 2 + e (row 1).
       if (j < a.n_self) {
-        const int lim = a.S - j * kKT - 64 * hf;
-        if (lim < 64) {
+        const int lim = a.S - j * kKT - 2 * jj;
+        if (lim < kKT) {
 #pragma unroll
-          for (int i = 0; i < 64; i++)
-            if (i >= lim) r[i] = __float_as_uint(-INFINITY);
+          for (int c = 0; c < 16; c++)
+#pragma unroll
+            for (int e = 0; e < 2; e++)
+              if (8 * c + e >= lim) {
+                r[4 * c + e] = __float_as_uint(-INFINITY);
+                r[4 * c + 2 + e] = __float_as_uint(-INFINITY);
+              }
         }
       } else {
-        const int w0 = (j - a.n_self) * (kKT / 32) + 2 * hf;
+        const int w0 = (j - a.n_self) * (kKT / 32);
 #pragma unroll
-        for (int c = 0; c < 2; c++) {
-          const uint32_t bits = ctx_bits[w0 + c];  // zero past C
-          if (bits != 0xffffffffu) {
+        for (int q4 = 0; q4 < 4; q4++) {
+          const uint32_t bits = ctx_bits[w0 + q4] >> (2 * jj);  // zero past C
+          if ((bits & 0x03030303u) != 0x03030303u) {
 #pragma unroll
-            for (int i = 0; i < 32; i++)
-              if (!((bits >> i) & 1u)) r[32 * c + i] = __float_as_uint(-INFINITY);
+            for (int cc = 0; cc < 4; cc++)
+#pragma unroll
+              for (int e = 0; e < 2; e++)
+                if (!((bits >> (8 * cc + e)) & 1u)) {
+                  r[4 * (4 * q4 + cc) + e] = __float_as_uint(-INFINITY);
+                  r[4 * (4 * q4 + cc) + 2 + e] = __float_as_uint(-INFINITY);
+                }
           }
         }
       }
-      // Eight running maxima, two scores per three-input max.
-      float mx[8];
+      // Row maxima: this thread's 32 scores of each row, then the row's four
+      // threads.
+      float x0 = fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1]));
+      float x1 = fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3]));
+      float y0 = fmaxf(__uint_as_float(r[4]), __uint_as_float(r[5]));
+      float y1 = fmaxf(__uint_as_float(r[6]), __uint_as_float(r[7]));
 #pragma unroll
-      for (int i = 0; i < 8; i++) mx[i] = __uint_as_float(r[i]);
-#pragma unroll
-      for (int i = 8; i < 64; i += 16)
-#pragma unroll
-        for (int c = 0; c < 8; c++)
-          mx[c] = fmax3(mx[c], __uint_as_float(r[i + c]),
-                        i + 8 + c < 64 ? __uint_as_float(r[i + 8 + c]) : mx[c]);
-      const float hmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
-                               fmaxf(mx[6], mx[7]));
-      // The row maximum over both halves (double-buffered by tile parity: a
-      // partner past this tile's barrier has read the previous tile's slot).
-      xmax[((j & 1) * 2 + hf) * kQ + row] = hmax;
-      mbar_arrive(&xbar[quad]);
-      ok = mbar_wait_bounded(&xbar[quad], j & 1, a.err, 13, abort_flag, a.limit_ns);
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
+      for (int c = 2; c < 16; c += 2) {
+        x0 = fmax3(x0, __uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]));
+        x1 = fmax3(x1, __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
+        y0 = fmax3(y0, __uint_as_float(r[4 * c + 4]), __uint_as_float(r[4 * c + 5]));
+        y1 = fmax3(y1, __uint_as_float(r[4 * c + 6]), __uint_as_float(r[4 * c + 7]));
       }
-      const float rmax = fmaxf(hmax, xmax[((j & 1) * 2 + (hf ^ 1)) * kQ + row]);
-      const float mnew = fmaxf(m, rmax * kScaleLog2);
-      const bool need = mnew > m + kRescaleGap;
+      float rmax0 = fmaxf(x0, y0), rmax1 = fmaxf(x1, y1);
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        rmax0 = fmaxf(rmax0, __shfl_xor_sync(0xffffffffu, rmax0, o));
+        rmax1 = fmaxf(rmax1, __shfl_xor_sync(0xffffffffu, rmax1, o));
+      }
+      const float mn0 = fmaxf(m0, rmax0 * kScaleLog2), mn1 = fmaxf(m1, rmax1 * kScaleLog2);
+      const bool need0 = mn0 > m0 + kRescaleGap, need1 = mn1 > m1 + kRescaleGap;
       bool pv_waited = false;
-      if (__any_sync(0xffffffffu, need)) {
-        const float f = need ? ex2_approx(m - mnew) : 1.0f;
+      if (__any_sync(0xffffffffu, need0 || need1)) {
+        const float f0 = need0 ? ex2_approx(m0 - mn0) : 1.0f;
+        const float f1 = need1 ? ex2_approx(m1 - mn1) : 1.0f;
         if (j > 0) {
           // O is quiescent once PV_{j-1} is done (PV_j waits for this tile's P).
           ok = mbar_wait_bounded(pv_done, (j - 1) & 1, a.err, 8, abort_flag, a.limit_ns);
@@ -439,35 +473,52 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           pv_waited = true;
           tc_fence_after();
-          // This thread's 32 columns of the row's O, in 16-column pieces.
+          // In two 32-column pieces: the 64 scores are live here.
 #pragma unroll 1
-          for (int c = 0; c < 2; c++) {
+          for (int hh = 0; hh < 2; hh++) {
             uint32_t o[16];
-            tmem_ld_32x32b_x16(lane_base + colO + (uint32_t)(16 * c), o);
+            tmem_ld_16x256b_x4(lane_addr + kColO + 32u * hh, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st_32x32b_x16(lane_base + colO + (uint32_t)(16 * c), o);
+            for (int c = 0; c < 4; c++) {
+              o[4 * c] = __float_as_uint(__uint_as_float(o[4 * c]) * f0);
+              o[4 * c + 1] = __float_as_uint(__uint_as_float(o[4 * c + 1]) * f0);
+              o[4 * c + 2] = __float_as_uint(__uint_as_float(o[4 * c + 2]) * f1);
+              o[4 * c + 3] = __float_as_uint(__uint_as_float(o[4 * c + 3]) * f1);
+            }
+            tmem_st_16x256b_x4(lane_addr + kColO + 32u * hh, o);
           }
         }
-        if (need) {
-          l *= f;
-          m = mnew;
+        if (need0) {
+          l0 *= f0;
+          m0 = mn0;
+        }
+        if (need1) {
+          l1 *= f1;
+          m1 = mn1;
         }
       }
-      // Pairs of keys through the packed f32x2 FMA and add: t = s * c - m,
-      // p = 2^t, per-lane sums in two pairs of accumulators.
-      float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-      const float2 scale2 = make_float2(kScaleLog2, kScaleLog2), negm2 = make_float2(-m, -m);
+      // p = 2^(s * c - m) per key pair (packed f32x2 FMA and add); the pair
+      // of row 0 and the pair of row 1 of each group become the two fp16
+      // columns this thread stores (16x128b: registers 2c, 2c + 1).
+      float2 ps0 = make_float2(0.0f, 0.0f), ps1 = make_float2(0.0f, 0.0f);
+      const float2 scale2 = make_float2(kScaleLog2, kScaleLog2);
+      const float2 negm0 = make_float2(-m0, -m0), negm1 = make_float2(-m1, -m1);
 #pragma unroll
-      for (int i = 0; i < 32; i++) {
-        const float2 t = ffma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
-                               scale2, negm2);
-        const float2 pp = make_float2(ex2_approx(t.x), ex2_approx(t.y));
-        ps[i & 1] = fadd2(ps[i & 1], pp);
-        r[i] = pack_half2_rn(pp.x, pp.y);  // fp16 pair of the A operand: key 2i low, 2i + 1 high
+      for (int c = 0; c < 16; c++) {
+        const float2 t0 = ffma2(make_float2(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1])),
+                                scale2, negm0);
+        const float2 t1 = ffma2(make_float2(__uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3])),
+                                scale2, negm1);
+        const float2 p0 = make_float2(ex2_approx(t0.x), ex2_approx(t0.y));
+        const float2 p1 = make_float2(ex2_approx(t1.x), ex2_approx(t1.y));
+        ps0 = fadd2(ps0, p0);
+        ps1 = fadd2(ps1, p1);
+        r[2 * c] = pack_half2_rn(p0.x, p0.y);  // registers 2c, 2c + 1 were read at group c / 2
+        r[2 * c + 1] = pack_half2_rn(p1.x, p1.y);
       }
-      l += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y);
+      l0 += ps0.x + ps0.y;
+      l1 += ps1.x + ps1.y;
       // P_j goes over P_{j-1} once PV_{j-1} has read it.
       if (j > 0 && !pv_waited) {
         ok = mbar_wait_bounded(pv_done, (j - 1) & 1, a.err, 12, abort_flag, a.limit_ns);
@@ -477,47 +528,52 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc_fence_after();
       }
-      tmem_st_32x32b_x32(lane_base + colP, sub32(r, 0));
+      tmem_st_16x128b_x16(lane_addr + kColP, reinterpret_cast<const uint32_t(&)[32]>(r));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // The row's l: both halves summed with the same maxima.
     if (ok) {
-      xl[hf * kQ + row] = l;
-      mbar_arrive(&xbar[quad]);
-      ok = mbar_wait_bounded(&xbar[quad], T & 1, a.err, 14, abort_flag, a.limit_ns);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        l += xl[(hf ^ 1) * kQ + row];
-        ok = mbar_wait_bounded(pv_done, (T - 1) & 1, a.err, 11, abort_flag, a.limit_ns);
-        ok = __all_sync(0xffffffffu, ok);
+      // The rows' sums over their four threads.
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
       }
+      ok = mbar_wait_bounded(pv_done, (T - 1) & 1, a.err, 11, abort_flag, a.limit_ns);
+      ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc_fence_after();
       uint32_t o[32];
-      tmem_ld_32x32b_x32(lane_base + colO, o);
+      tmem_ld_16x256b_x8(lane_addr + kColO, o);
       tmem_ld_wait();
       ok = mbar_wait_bounded(g_full, 0, a.err, 16, abort_flag, a.limit_ns);
-      if (ok && qrow < a.S) {
-        // Dimensions 32 hf .. 32 hf + 31 of the head; the gate from K stage
-        // hf (16-byte chunk i of the row at i ^ (row & 7)).  The sigmoid in
-        // fast single-precision form (ex2.approx-based exp and division,
-        // relative error ~1e-6, far under the fp16 operands' rounding).
-        const size_t off = ((size_t)b * a.S + qrow) * a.D + (size_t)hd * kDH + 32 * hf;
-        const uint8_t* grow = sK + hf * kKBytes + row * kRow;
-        float4* out = reinterpret_cast<float4*>(a.mix + off);
-        const float inv_l = __fdiv_rn(1.0f, l);
+      if (ok) {
+        // Dimensions 8c + 2jj, + 1 of the head for the two rows; the gate
+        // from K stage d / 32 (16-byte chunk (d % 32) / 4 of the row at
+        // chunk ^ (row & 7)).  The sigmoid in fast single-precision form
+        // (ex2.approx-based exp and division, relative error ~1e-6, far
+        // under the fp16 operands' rounding).
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const float4 gv = *reinterpret_cast<const float4*>(grow + ((i ^ (row & 7)) << 4));
-          float4 ov;
-          ov.x = __uint_as_float(o[4 * i]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.x));
-          ov.y = __uint_as_float(o[4 * i + 1]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.y));
-          ov.z = __uint_as_float(o[4 * i + 2]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.z));
-          ov.w = __uint_as_float(o[4 * i + 3]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.w));
-          out[i] = ov;
+        for (int h = 0; h < 2; h++) {
+          const int rr = h ? rr1 : rr0;
+          const int qrow = q0 + rr;
+          if (qrow >= a.S) continue;
+          const float inv_l = __fdiv_rn(1.0f, h ? l1 : l0);
+          float* orow = a.mix + ((size_t)b * a.S + qrow) * a.D + (size_t)hd * kDH;
+#pragma unroll
+          for (int c = 0; c < 8; c++) {
+            const int d = 8 * c + 2 * jj;
+            const uint8_t* gch = sK + (d >> 5) * kKBytes + rr * kRow +
+                                 ((((d & 31) >> 2) ^ (rr & 7)) << 4) + (d & 3) * 4;
+            const float2 gv = *reinterpret_cast<const float2*>(gch);
+            float2 ov;
+            ov.x = __uint_as_float(o[4 * c + 2 * h]) * inv_l * __fdividef(1.0f, 1.0f + __expf(-gv.x));
+            ov.y = __uint_as_float(o[4 * c + 2 * h + 1]) * inv_l *
+                   __fdividef(1.0f, 1.0f + __expf(-gv.y));
+            *reinterpret_cast<float2*>(orow + d) = ov;
+          }
         }
       }
     }
