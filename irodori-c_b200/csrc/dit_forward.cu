@@ -128,54 +128,92 @@ __global__ void __launch_bounds__(32) linear_rows_kernel(const float* __restrict
   y[(size_t)m * N + n] = v;
 }
 
-// y[M, 32] = x[M, K] . w[32, K]^T (+ bias), the output head: W^T staged in
-// shared memory once per persistent block ([K][32], 128 KB for K = 1024), one
-// warp per row, lane j summing output j in increasing k from a conflict-free
-// 128-byte shared row per k and the broadcast input row.
-constexpr size_t kNarrowSmemMax = 160 * 1024;
+// y[M, 32] = x[M, K] . w[32, K]^T (+ bias), the output head, on a persistent
+// grid: W^T staged in shared memory once per block ([K][32], 128 KB for
+// K = 1024); groups of 128 input rows stream through shared memory in chunks
+// of 32 k by cp.async, double-buffered so the next chunk lands while this one
+// is summed.  Each warp sums 8 rows: lane j holds output j of its rows, in
+// increasing k (the reference's order), reading W^T[k][j] from a
+// conflict-free 128-byte row and the rows' x[k .. k+3] as broadcasts.
+constexpr size_t kNarrowSmemMax = 160 * 1024;  // W^T
+constexpr int kNarrowRows = 128;               // rows per group (16 warps x 8)
+constexpr int kNarrowKC = 32;                  // k per staged chunk
+constexpr int kNarrowThreads = 512;
+constexpr size_t kNarrowXBytes = 2 * kNarrowRows * kNarrowKC * sizeof(float);  // 32 KB
 
-__global__ void __launch_bounds__(1024, 1) linear_narrow_kernel(const float* __restrict__ x,
-                                                                const float* __restrict__ w,
-                                                                const float* __restrict__ bias,
-                                                                float* __restrict__ y, int M,
-                                                                int K, int silu) {
-  extern __shared__ float wt[];  // [K][32]
-  for (int i = threadIdx.x; i < K * 32; i += 1024) {
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gsrc)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kNarrowThreads, 1) linear_narrow_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+    float* __restrict__ y, int M, int K, int silu) {
+  extern __shared__ float4 narrow_smem[];
+  float* wt = reinterpret_cast<float*>(narrow_smem);  // [K][32]
+  float* xs = wt + (size_t)K * 32;                    // [2][kNarrowRows][kNarrowKC]
+  for (int i = threadIdx.x; i < K * 32; i += kNarrowThreads) {
     const int n = i & 31, k = i >> 5;
     wt[i] = w[(size_t)n * K + k];
   }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float b = bias ? bias[lane] : 0.0f;
-  // Four rows per warp at a time: four independent sums per lane and four
-  // input rows in flight.
-  for (int m0 = (blockIdx.x * 32 + warp) * 4; m0 < M; m0 += gridDim.x * 32 * 4) {
-    const float4* x4[4];
-#pragma unroll
-    for (int r = 0; r < 4; r++)
-      x4[r] = reinterpret_cast<const float4*>(x + (size_t)min(m0 + r, M - 1) * K);
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 2
-    for (int k4 = 0; k4 < K / 4; k4++) {
-      float4 a[4];
-#pragma unroll
-      for (int r = 0; r < 4; r++) a[r] = x4[r][k4];
-      const float* wk = wt + k4 * 128 + lane;
-      const float w0 = wk[0], w1 = wk[32], w2 = wk[64], w3 = wk[96];
-#pragma unroll
-      for (int r = 0; r < 4; r++) {
-        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].x, w0));
-        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].y, w1));
-        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].z, w2));
-        acc[r] = __fadd_rn(acc[r], __fmul_rn(a[r].w, w3));
+  const int nk = (K + kNarrowKC - 1) / kNarrowKC;
+  const int groups = (M + kNarrowRows - 1) / kNarrowRows;
+  // One chunk: 128 rows x 32 floats = 1024 16-byte pieces, two per thread
+  // (rows past M repeat row M - 1; their sums are not stored).
+  auto stage = [&](int g, int kc, int buf) {
+    const int kw = min(kNarrowKC, K - kc * kNarrowKC) / 4;  // float4 per row in this chunk
+    for (int i = threadIdx.x; i < kNarrowRows * (kNarrowKC / 4); i += kNarrowThreads) {
+      const int r = i / (kNarrowKC / 4), c4 = i % (kNarrowKC / 4);
+      if (c4 < kw) {
+        const int row = min(g * kNarrowRows + r, M - 1);
+        cp_async16(xs + ((size_t)buf * kNarrowRows + r) * kNarrowKC + 4 * c4,
+                   x + (size_t)row * K + (size_t)kc * kNarrowKC + 4 * c4);
       }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+    float acc[8];
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-      if (m0 + r >= M) break;
+    for (int r = 0; r < 8; r++) acc[r] = 0.0f;
+    __syncthreads();  // W^T staged; the previous group's last chunk is read
+    stage(g, 0, 0);
+    for (int kc = 0; kc < nk; kc++) {
+      if (kc + 1 < nk) {
+        stage(g, kc + 1, (kc + 1) & 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      __syncthreads();
+      const float* xb = xs + ((size_t)(kc & 1) * kNarrowRows + warp * 8) * kNarrowKC;
+      const float* wb = wt + (size_t)kc * kNarrowKC * 32 + lane;
+      const int kl = min(kNarrowKC, K - kc * kNarrowKC);
+      for (int k = 0; k < kl; k += 4) {
+        const float w0 = wb[(k + 0) * 32], w1 = wb[(k + 1) * 32];
+        const float w2 = wb[(k + 2) * 32], w3 = wb[(k + 3) * 32];
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+          const float4 a = *reinterpret_cast<const float4*>(xb + r * kNarrowKC + k);
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.x, w0));
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.y, w1));
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.z, w2));
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.w, w3));
+        }
+      }
+      __syncthreads();  // this buffer is staged over two chunks from now
+    }
+#pragma unroll
+    for (int r = 0; r < 8; r++) {
+      const int m = g * kNarrowRows + warp * 8 + r;
+      if (m >= M) break;
       float v = __fadd_rn(acc[r], b);
       if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-      y[(size_t)(m0 + r) * 32 + lane] = v;
+      y[(size_t)m * 32 + lane] = v;
     }
   }
 }
@@ -189,17 +227,17 @@ int linear_ref(const float* x, const float* w, const float* bias, float* y, int 
   if (ex_cfg <= 1 && aligned && N == 32 && (size_t)K * 32 * 4 <= kNarrowSmemMax &&
       (K & 3) == 0 && M > 64) {
     static bool attr = false;
-    const int smem = K * 32 * 4;
+    const int smem = K * 32 * 4 + (int)kNarrowXBytes;
     if (!attr) {
       cudaFuncSetAttribute(linear_narrow_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kNarrowSmemMax);
+                           (int)(kNarrowSmemMax + kNarrowXBytes));
       attr = true;
     }
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = std::min(sms, cdiv(M, 128));
-    linear_narrow_kernel<<<grid, 1024, smem, s>>>(x, w, bias, y, M, K, silu);
+    const int grid = std::min(sms, cdiv(M, kNarrowRows));
+    linear_narrow_kernel<<<grid, kNarrowThreads, smem, s>>>(x, w, bias, y, M, K, silu);
   } else if (ex_cfg <= 1 && aligned && M <= 64) {
     const long long warps = (long long)M * cdiv(N, 32);
     linear_rows_kernel<<<(unsigned)warps, 32, 0, s>>>(x, w, bias, y, M, N, K, silu);

@@ -98,6 +98,23 @@ def test_stage_entry_points_match_reference():
     assert err.max() <= 1e-5 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("rows", [65, 1000, 4099])
+def test_output_head_bit_exact_many_rows(rows):
+    """The output head's persistent row-group kernel (groups of 128 rows,
+    ragged last group, k in staged chunks) against the reference's
+    iro_dit_output, bit for bit."""
+    state, ck, cv, mask, blocks, head = inputs.dit_model_case(19, 1, 1, 1, 8, 4)
+    m = build_model(blocks, head)
+    D = head["in_w"].shape[0]
+    rng = np.random.default_rng(rows)
+    hid = (rng.standard_normal((rows, D)) * 2).astype(np.float32)
+    vel = iro.DevBuf((rows, 32), np.float32)
+    m.output(iro.DevBuf.from_host(hid), 1, rows, vel)
+    iro.synchronize()
+    want = oracle.ref_dit_output(head["out_norm"], head["out_w"], head["out_b"], hid, 1, rows)
+    assert (vel.get().view(np.uint32) == want.view(np.uint32)).all()
+
+
 def test_euler_step_and_sampler_match_fixture():
     g = np.load(os.path.join(GOLDEN, "dit_step.npz"))
     seed, layers, R, cfg, S, C = (int(v) for v in g["case"])
