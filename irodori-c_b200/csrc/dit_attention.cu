@@ -1,7 +1,7 @@
 // dit_attention.cu — the DiT block's joint attention (dit.c:806-862) on the
 // 5th-generation tensor cores: fp16 operands, fp32 accumulation.
 //
-// One CTA per (128-query tile, head, batch row), two CTAs per SM (82 KB of
+// One CTA per (128-query tile, head, batch row), two CTAs per SM (83 KB of
 // shared memory and 256 TMEM columns each).  Keys are the row's S self
 // tokens followed by its context block (C tokens, invalid ones masked out),
 // in tiles of 128:
@@ -15,9 +15,11 @@
 //               into TMEM columns [0, 128);
 //               O += P_j V_j   (A = P_j as fp16 pairs in TMEM columns
 //               [128, 192), B = V_j^T K-major in shared memory) into [192, 256)
-//   4 warps     one query row per thread: scores from TMEM, scale 1/8, mask,
-//               online softmax, P_j packed to fp16 pairs into TMEM; at the
-//               end O / l times the sigmoid gate (ops.c:786-789) to `mix`.
+//   8 warps     16 query rows each, four threads per row (16-lane TMEM
+//               loads): scores, scale 1/8, mask, online softmax with the
+//               row maximum and sum by shuffles, P_j packed to fp16 pairs
+//               into TMEM; at the end O / l times the sigmoid gate
+//               (ops.c:786-789) to `mix`.
 //
 // The softmax warps release S_j as soon as it sits in registers, so S_{j+1}
 // runs on the tensor cores during softmax_j, and PV_j right after it; P_{j+1}

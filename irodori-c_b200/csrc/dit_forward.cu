@@ -71,21 +71,34 @@ __global__ void __launch_bounds__(256) linear_ref_kernel(const float* __restrict
     }
     __syncthreads();
   }
+  // A thread's TN consecutive outputs of a row go out as one vector store
+  // when they are whole and aligned (TN = 4, N % 4 == 0).
+  const bool vec = TN == 4 && (N & 3) == 0 && n0 + tx * TN + TN <= N &&
+                   (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
 #pragma unroll
   for (int i = 0; i < TM; i++) {
     const int m = m0 + ty * TM + i;
     if (m >= M) continue;
+    float v[TN];
 #pragma unroll
     for (int j = 0; j < TN; j++) {
       const int n = n0 + tx * TN + j;
+      v[j] = 0.0f;
       if (n >= N) continue;
-      float v = __fadd_rn(acc[i][j], bias ? bias[n] : 0.0f);
-      if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-      if (ex_cfg <= 1) {
-        y[(size_t)m * N + n] = v;
+      v[j] = __fadd_rn(acc[i][j], bias ? bias[n] : 0.0f);
+      if (silu) v[j] = __fdiv_rn(v[j], __fadd_rn(1.0f, expf(-v[j])));
+    }
+    const int c0 = n0 + tx * TN;
+    const size_t r = (size_t)(m / ex_S), t = (size_t)(m % ex_S);
+    const int copies = ex_cfg <= 1 ? 1 : ex_cfg;
+    for (int c = 0; c < copies; c++) {
+      float* yrow = ex_cfg <= 1 ? y + (size_t)m * N : y + ((r * ex_cfg + c) * ex_S + t) * N;
+      if (vec) {
+        *reinterpret_cast<float4*>(yrow + c0) = make_float4(v[0], v[1 % TN], v[2 % TN], v[3 % TN]);
       } else {
-        const size_t r = (size_t)(m / ex_S), t = (size_t)(m % ex_S);
-        for (int c = 0; c < ex_cfg; c++) y[((r * ex_cfg + c) * ex_S + t) * N + n] = v;
+#pragma unroll
+        for (int j = 0; j < TN; j++)
+          if (c0 + j < N) yrow[c0 + j] = v[j];
       }
     }
   }
@@ -161,30 +174,33 @@ __global__ void __launch_bounds__(kNarrowThreads, 1) linear_narrow_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float b = bias ? bias[lane] : 0.0f;
   const int nk = (K + kNarrowKC - 1) / kNarrowKC;
-  const int groups = (M + kNarrowRows - 1) / kNarrowRows;
+  // Each block owns one contiguous share of the rows (the last group of a
+  // share may be partial), so no block sums more than ceil(M / grid) rows.
+  const int share = (M + gridDim.x - 1) / gridDim.x;
+  const int rbeg = blockIdx.x * share, rend = min(M, rbeg + share);
   // One chunk: 128 rows x 32 floats = 1024 16-byte pieces, two per thread
-  // (rows past M repeat row M - 1; their sums are not stored).
-  auto stage = [&](int g, int kc, int buf) {
+  // (rows past the share repeat its last row; their sums are not stored).
+  auto stage = [&](int g0, int kc, int buf) {
     const int kw = min(kNarrowKC, K - kc * kNarrowKC) / 4;  // float4 per row in this chunk
     for (int i = threadIdx.x; i < kNarrowRows * (kNarrowKC / 4); i += kNarrowThreads) {
       const int r = i / (kNarrowKC / 4), c4 = i % (kNarrowKC / 4);
       if (c4 < kw) {
-        const int row = min(g * kNarrowRows + r, M - 1);
+        const int row = min(g0 + r, rend - 1);
         cp_async16(xs + ((size_t)buf * kNarrowRows + r) * kNarrowKC + 4 * c4,
                    x + (size_t)row * K + (size_t)kc * kNarrowKC + 4 * c4);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+  for (int g0 = rbeg; g0 < rend; g0 += kNarrowRows) {
     float acc[8];
 #pragma unroll
     for (int r = 0; r < 8; r++) acc[r] = 0.0f;
     __syncthreads();  // W^T staged; the previous group's last chunk is read
-    stage(g, 0, 0);
+    stage(g0, 0, 0);
     for (int kc = 0; kc < nk; kc++) {
       if (kc + 1 < nk) {
-        stage(g, kc + 1, (kc + 1) & 1);
+        stage(g0, kc + 1, (kc + 1) & 1);
         asm volatile("cp.async.wait_group 1;" ::: "memory");
       } else {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -193,24 +209,28 @@ __global__ void __launch_bounds__(kNarrowThreads, 1) linear_narrow_kernel(
       const float* xb = xs + ((size_t)(kc & 1) * kNarrowRows + warp * 8) * kNarrowKC;
       const float* wb = wt + (size_t)kc * kNarrowKC * 32 + lane;
       const int kl = min(kNarrowKC, K - kc * kNarrowKC);
-      for (int k = 0; k < kl; k += 4) {
-        const float w0 = wb[(k + 0) * 32], w1 = wb[(k + 1) * 32];
-        const float w2 = wb[(k + 2) * 32], w3 = wb[(k + 3) * 32];
+      // Warps whose 8 rows all lie past the block's share (the tail of a
+      // partial group) skip the sums.
+      if (g0 + warp * 8 < rend) {
+        for (int k = 0; k < kl; k += 4) {
+          const float w0 = wb[(k + 0) * 32], w1 = wb[(k + 1) * 32];
+          const float w2 = wb[(k + 2) * 32], w3 = wb[(k + 3) * 32];
 #pragma unroll
-        for (int r = 0; r < 8; r++) {
-          const float4 a = *reinterpret_cast<const float4*>(xb + r * kNarrowKC + k);
-          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.x, w0));
-          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.y, w1));
-          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.z, w2));
-          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.w, w3));
+          for (int r = 0; r < 8; r++) {
+            const float4 a = *reinterpret_cast<const float4*>(xb + r * kNarrowKC + k);
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.x, w0));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.y, w1));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.z, w2));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.w, w3));
+          }
         }
       }
       __syncthreads();  // this buffer is staged over two chunks from now
     }
 #pragma unroll
     for (int r = 0; r < 8; r++) {
-      const int m = g * kNarrowRows + warp * 8 + r;
-      if (m >= M) break;
+      const int m = g0 + warp * 8 + r;
+      if (m >= rend) break;
       float v = __fadd_rn(acc[r], b);
       if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
       y[(size_t)m * 32 + lane] = v;
@@ -236,7 +256,7 @@ int linear_ref(const float* x, const float* w, const float* bias, float* y, int 
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = std::min(sms, cdiv(M, kNarrowRows));
+    const int grid = std::min(sms, cdiv(M, 64));
     linear_narrow_kernel<<<grid, kNarrowThreads, smem, s>>>(x, w, bias, y, M, K, silu);
   } else if (ex_cfg <= 1 && aligned && M <= 64) {
     const long long warps = (long long)M * cdiv(N, 32);
