@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(256) context_prep_kernel(const float* __restri
                                                            int D, int heads, int ldc,
                                                            DevError* err) {
   __shared__ float tile[kDH][33];
+  grid_dep_wait();  // launched with programmatic stream serialization
   const int s0 = blockIdx.x * 32, h = blockIdx.y, cb = blockIdx.z;
   const int t = threadIdx.x;
   for (int i = t; i < 32 * kDH; i += 256) {
@@ -378,7 +379,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     // share its maximum and sum by shuffles.
     const int quad = warp & 3;
     const int sub = (warp - 2) >> 2;
-    const int st_id = threadIdx.x - 64;  // 0..255
     const int jj = lane & 3;             // key pair within each 8-key group
     const int lbase = quad * 32 + sub * 16;
     const int rr0 = lbase + (lane >> 2), rr1 = rr0 + 8;  // this thread's two rows
@@ -653,10 +653,14 @@ int attention_tc_launch(Ctx* c, const AttnTcRequest& r, cudaStream_t s) {
     attr_done[c->device] = true;
   }
   const AttnTcOperands o = attention_tc_operands(r);
-  context_prep_kernel<<<dim3(cdiv(o.ldc, 32), r.heads, r.context_batch), 256, 0, s>>>(
-      r.ck, r.cv, o.ck, o.cvt, r.C, r.D, r.heads, o.ldc, c->err);
-  int st = check_launch();
-  if (st) return st;
+  cudaError_t pe = launch_pdl(context_prep_kernel, dim3(cdiv(o.ldc, 32), r.heads, r.context_batch),
+                              dim3(256), 0, s, r.ck, r.cv, o.ck, o.cvt, r.C, r.D, r.heads, o.ldc,
+                              c->err);
+  if (pe != cudaSuccess) {
+    cudaGetLastError();
+    return map_cuda(pe);
+  }
+  int st = IRO_OK;
   CUtensorMap mq, mk, mv, mck, mcv;
   const long long rows = (long long)r.B * r.S, crows = (long long)r.context_batch * r.C;
   st = map2d_h(&mq, o.q, r.D, rows, kQ);

@@ -153,6 +153,7 @@ __global__ void __launch_bounds__(256) adaln_quant_kernel(const float* __restric
                                                           uint8_t* __restrict__ q,
                                                           float* __restrict__ qs,
                                                           int32_t* __restrict__ qz) {
+  grid_dep_wait();  // launched with programmatic stream serialization
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -214,10 +215,11 @@ int adaln_quant_launch(const float* x, int rows, int S, int D, float eps, int pr
                        cudaStream_t s) {
   const int V = cdiv(D / 4, 32);
   const dim3 grid(cdiv(rows, 8)), block(256);
+  cudaError_t e;
 #define IRO_AQ(N)                                                                              \
   case N:                                                                                      \
-    adaln_quant_kernel<N><<<grid, block, 0, s>>>(x, rows, S, D, eps, prow, shift, scale, q,   \
-                                                 qs, qz);                                      \
+    e = launch_pdl(adaln_quant_kernel<N>, grid, block, 0, s, x, rows, S, D, eps, prow, shift, \
+                   scale, q, qs, qz);                                                          \
     break;
   switch (V) {
     IRO_AQ(4)
@@ -229,7 +231,11 @@ int adaln_quant_launch(const float* x, int rows, int S, int D, float eps, int pr
       return IRO_ERR_UNSUPPORTED;
   }
 #undef IRO_AQ
-  return check_launch();
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return map_cuda(e);
+  }
+  return IRO_OK;
 }
 
 // Per (row, head): RMSNorm of q and k with their weights, then RoPE on the
