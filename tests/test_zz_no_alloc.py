@@ -101,3 +101,39 @@ def test_noalloc_timeouts_surface_through_synchronize():
     assert iro.swiglu_noalloc_dev(x, M, w13, w2, None, got, stream=stream) == iro.IRO_OK
     assert iro.lib().iro_cuda_synchronize(stream) == iro.IRO_OK
     assert (got.get().view(np.uint32) == want.get().view(np.uint32)).all()
+
+
+def test_noalloc_records_under_global_stream_capture():
+    """The point of the entry point: after one warm-up call it can be
+    recorded into a CUDA graph under global-mode stream capture (which fails
+    on any allocation, synchronisation or other non-capturable call made while
+    the capture is open), and the replayed graph writes the same bits as the
+    allocating entry point."""
+    import ctypes
+    import torch
+
+    iro.init(0)
+    M, D, H = 512, 1024, 2816
+    rng = np.random.default_rng(32)
+    w13, w2, _, _ = _weights(rng, D, H)
+    xd = iro.DevBuf.from_host(rng.standard_normal((M, D)).astype(np.float32))
+    want = iro.DevBuf((M, D), np.float32)
+    got = iro.DevBuf((M, D), np.float32)
+    iro.swiglu_dev(xd, M, w13, w2, None, want)
+    iro.synchronize()
+    cap = torch.cuda.Stream()
+    handle = ctypes.c_void_p(cap.cuda_stream)
+    assert iro.swiglu_noalloc_dev(xd, M, w13, w2, None, got, stream=handle) == iro.IRO_OK
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap, capture_error_mode="global"):
+        rc = iro.swiglu_noalloc_dev(xd, M, w13, w2, None, got, stream=handle)
+    assert rc == iro.IRO_OK, rc
+    got.fill_byte(0xFF)
+    iro.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert iro.lib().iro_cuda_synchronize(None) == iro.IRO_OK
+    g, w = got.get(), want.get()
+    assert (g.view(np.uint32) == w.view(np.uint32)).all()
+    del graph
