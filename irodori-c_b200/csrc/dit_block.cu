@@ -79,6 +79,9 @@ __global__ void __launch_bounds__(256) adaln_down_kernel(const AdaBatch bt,
   const float* w = bt.m[set][3 * br] + (size_t)r * D;
   float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
   int d = lane;
+  // Unrolled: four iterations' loads issue before their multiply-adds (each
+  // accumulator still sums its elements in increasing d).
+#pragma unroll 4
   for (; d + 96 < D; d += 128) {
     s0 = __fmaf_rn(a[d], w[d], s0);
     s1 = __fmaf_rn(a[d + 32], w[d + 32], s1);

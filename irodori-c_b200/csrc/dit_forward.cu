@@ -104,55 +104,20 @@ __global__ void __launch_bounds__(256) linear_ref_kernel(const float* __restrict
   }
 }
 
-// y[M, N] = x[M, K] . w[N, K]^T (+ bias) for a few rows (the conditioner):
-// one warp per (row, 32 outputs) and one warp per block, so the warps spread
-// over the SMs; lane j sums output n0 + j in increasing k (the reference's
-// order) with float4 loads of its own weight row and the broadcast input row.
-__global__ void __launch_bounds__(32) linear_rows_kernel(const float* __restrict__ x,
-                                                          const float* __restrict__ w,
-                                                          const float* __restrict__ bias,
-                                                          float* __restrict__ y, int M, int N,
-                                                          int K, int silu) {
-  const int ngroups = (N + 31) / 32;
-  const long long gw = blockIdx.x;
-  if (gw >= (long long)M * ngroups) return;
-  const int m = (int)(gw / ngroups), n = (int)(gw % ngroups) * 32 + (threadIdx.x & 31);
-  const bool active = n < N;
-  const float* xr = x + (size_t)m * K;
-  const float* wr = w + (size_t)(active ? n : 0) * K;
-  float acc = 0.0f;
-  if ((K & 3) == 0) {
-    const float4* x4 = reinterpret_cast<const float4*>(xr);
-    const float4* w4 = reinterpret_cast<const float4*>(wr);
-#pragma unroll 8
-    for (int k = 0; k < K / 4; k++) {
-      const float4 a = x4[k], b = w4[k];
-      acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
-      acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
-      acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
-      acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
-    }
-  } else {
-    for (int k = 0; k < K; k++) acc = __fadd_rn(acc, __fmul_rn(xr[k], wr[k]));
-  }
-  if (!active) return;
-  float v = __fadd_rn(acc, bias ? bias[n] : 0.0f);
-  if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-  y[(size_t)m * N + n] = v;
-}
-
-// y[M, 32] = x[M, K] . w[32, K]^T (+ bias), the output head, on a persistent
-// grid: W^T staged in shared memory once per block ([K][32], 128 KB for
-// K = 1024); groups of 128 input rows stream through shared memory in chunks
-// of 32 k by cp.async, double-buffered so the next chunk lands while this one
-// is summed.  Each warp sums 8 rows: lane j holds output j of its rows, in
-// increasing k (the reference's order), reading W^T[k][j] from a
-// conflict-free 128-byte row and the rows' x[k .. k+3] as broadcasts.
-constexpr size_t kNarrowSmemMax = 160 * 1024;  // W^T
-constexpr int kNarrowRows = 128;               // rows per group (16 warps x 8)
-constexpr int kNarrowKC = 32;                  // k per staged chunk
-constexpr int kNarrowThreads = 512;
-constexpr size_t kNarrowXBytes = 2 * kNarrowRows * kNarrowKC * sizeof(float);  // 32 KB
+// y[M, N] = x[M, K] . w[N, K]^T (+ bias) for a few rows (the conditioner,
+// M <= 8 per block): one warp per block and 32 outputs, lane j summing output
+// n0 + j of every row in increasing k (the reference's order, ops.c:221-234).
+// The reference's order makes each output one chain of K dependent adds, so
+// what bounds the kernel is how early the weights arrive: the block's 32
+// weight rows stream through shared memory in chunks of 64 k by cp.async,
+// kGemvStages chunks in flight (coalesced 16-byte pieces; rows padded to 68
+// floats so that lane j's 16-byte reads of its own row are conflict-free).
+constexpr int kGemvKC = 64;
+constexpr int kGemvLd = kGemvKC + 4;
+constexpr int kGemvRows = 8;  // input rows per block
+constexpr int kGemvStages = 6;
+constexpr size_t kGemvStageFloats = 32 * kGemvLd + kGemvRows * kGemvKC;
+constexpr size_t kGemvSmem = kGemvStages * kGemvStageFloats * sizeof(float);
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
@@ -160,80 +125,157 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
                "l"(gsrc)
                : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
-__global__ void __launch_bounds__(kNarrowThreads, 1) linear_narrow_kernel(
-    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
-    float* __restrict__ y, int M, int K, int silu) {
-  extern __shared__ float4 narrow_smem[];
-  float* wt = reinterpret_cast<float*>(narrow_smem);  // [K][32]
-  float* xs = wt + (size_t)K * 32;                    // [2][kNarrowRows][kNarrowKC]
-  for (int i = threadIdx.x; i < K * 32; i += kNarrowThreads) {
-    const int n = i & 31, k = i >> 5;
-    wt[i] = w[(size_t)n * K + k];
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float b = bias ? bias[lane] : 0.0f;
-  const int nk = (K + kNarrowKC - 1) / kNarrowKC;
-  // Each block owns one contiguous share of the rows (the last group of a
-  // share may be partial), so no block sums more than ceil(M / grid) rows.
-  const int share = (M + gridDim.x - 1) / gridDim.x;
-  const int rbeg = blockIdx.x * share, rend = min(M, rbeg + share);
-  // One chunk: 128 rows x 32 floats = 1024 16-byte pieces, two per thread
-  // (rows past the share repeat its last row; their sums are not stored).
-  auto stage = [&](int g0, int kc, int buf) {
-    const int kw = min(kNarrowKC, K - kc * kNarrowKC) / 4;  // float4 per row in this chunk
-    for (int i = threadIdx.x; i < kNarrowRows * (kNarrowKC / 4); i += kNarrowThreads) {
-      const int r = i / (kNarrowKC / 4), c4 = i % (kNarrowKC / 4);
-      if (c4 < kw) {
-        const int row = min(g0 + r, rend - 1);
-        cp_async16(xs + ((size_t)buf * kNarrowRows + r) * kNarrowKC + 4 * c4,
-                   x + (size_t)row * K + (size_t)kc * kNarrowKC + 4 * c4);
+template <int MR>
+__global__ void __launch_bounds__(32) gemv_rows_kernel(const float* __restrict__ x,
+                                                        const float* __restrict__ w,
+                                                        const float* __restrict__ bias,
+                                                        float* __restrict__ y, int M, int N,
+                                                        int K, int silu) {
+  extern __shared__ float4 gemv_smem[];
+  float* sm = reinterpret_cast<float*>(gemv_smem);
+  const int lane = threadIdx.x;
+  const int n0 = blockIdx.x * 32, m0 = blockIdx.y * MR;
+  const int mr = min(MR, M - m0);
+  const int nk = (K + kGemvKC - 1) / kGemvKC;
+  // Chunk kc into stage buffer b: weight rows n0 .. n0+31 (rows past N repeat
+  // row N-1; their sums are not stored), then the block's input rows.
+  auto stage = [&](int kc, int b) {
+    float* ws = sm + (size_t)b * kGemvStageFloats;
+    float* xs = ws + 32 * kGemvLd;
+    const int k0 = kc * kGemvKC;
+    const int p4 = min(kGemvKC, K - k0) / 4;  // 16-byte pieces per row in this chunk
+    if (p4 == kGemvKC / 4) {
+      // A whole chunk: lane l moves pieces l, l + 32, ... (row i / 16).
+#pragma unroll
+      for (int j = 0; j < 32 * (kGemvKC / 4) / 32; j++) {
+        const int i = lane + 32 * j;
+        const int r = i / (kGemvKC / 4), c = i % (kGemvKC / 4);
+        const int n = min(n0 + r, N - 1);
+        cp_async16(ws + r * kGemvLd + 4 * c, w + (size_t)n * K + k0 + 4 * c);
       }
+      for (int i = lane; i < mr * (kGemvKC / 4); i += 32) {
+        const int r = i / (kGemvKC / 4), c = i % (kGemvKC / 4);
+        cp_async16(xs + r * kGemvKC + 4 * c, x + (size_t)(m0 + r) * K + k0 + 4 * c);
+      }
+      return;
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int i = lane; i < 32 * p4; i += 32) {
+      const int r = i / p4, c = i - r * p4;
+      const int n = min(n0 + r, N - 1);
+      cp_async16(ws + r * kGemvLd + 4 * c, w + (size_t)n * K + k0 + 4 * c);
+    }
+    for (int i = lane; i < mr * p4; i += 32) {
+      const int r = i / p4, c = i - r * p4;
+      cp_async16(xs + r * kGemvKC + 4 * c, x + (size_t)(m0 + r) * K + k0 + 4 * c);
+    }
   };
-  for (int g0 = rbeg; g0 < rend; g0 += kNarrowRows) {
-    float acc[8];
+  float acc[MR];
 #pragma unroll
-    for (int r = 0; r < 8; r++) acc[r] = 0.0f;
-    __syncthreads();  // W^T staged; the previous group's last chunk is read
-    stage(g0, 0, 0);
-    for (int kc = 0; kc < nk; kc++) {
-      if (kc + 1 < nk) {
-        stage(g0, kc + 1, (kc + 1) & 1);
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-      } else {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-      }
-      __syncthreads();
-      const float* xb = xs + ((size_t)(kc & 1) * kNarrowRows + warp * 8) * kNarrowKC;
-      const float* wb = wt + (size_t)kc * kNarrowKC * 32 + lane;
-      const int kl = min(kNarrowKC, K - kc * kNarrowKC);
-      // Warps whose 8 rows all lie past the block's share (the tail of a
-      // partial group) skip the sums.
-      if (g0 + warp * 8 < rend) {
-        for (int k = 0; k < kl; k += 4) {
-          const float w0 = wb[(k + 0) * 32], w1 = wb[(k + 1) * 32];
-          const float w2 = wb[(k + 2) * 32], w3 = wb[(k + 3) * 32];
+  for (int r = 0; r < MR; r++) acc[r] = 0.0f;
 #pragma unroll
-          for (int r = 0; r < 8; r++) {
-            const float4 a = *reinterpret_cast<const float4*>(xb + r * kNarrowKC + k);
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.x, w0));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.y, w1));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.z, w2));
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(a.w, w3));
-          }
+  for (int b = 0; b < kGemvStages - 1; b++) {
+    if (b < nk) stage(b, b);
+    cp_async_commit();
+  }
+  for (int kc = 0; kc < nk; kc++) {
+    // The buffer chunk kc + stages - 1 goes to was last read by chunk kc - 1,
+    // which every lane finished before the barrier at the end of its turn.
+    if (kc + kGemvStages - 1 < nk) stage(kc + kGemvStages - 1, (kc + kGemvStages - 1) % kGemvStages);
+    cp_async_commit();
+    cp_async_wait<kGemvStages - 1>();
+    __syncwarp();
+    const float* ws = sm + (size_t)(kc % kGemvStages) * kGemvStageFloats;
+    const float* xs = ws + 32 * kGemvLd;
+    const int kl = min(kGemvKC, K - kc * kGemvKC);
+    auto step4 = [&](int k) {
+      const float4 b4 = *reinterpret_cast<const float4*>(ws + lane * kGemvLd + k);
+#pragma unroll
+      for (int r = 0; r < MR; r++) {
+        if (MR == 1 || r < mr) {
+          const float4 a = *reinterpret_cast<const float4*>(xs + r * kGemvKC + k);
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.x, b4.x));
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.y, b4.y));
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.z, b4.z));
+          acc[r] = __fadd_rn(acc[r], __fmul_rn(a.w, b4.w));
         }
       }
-      __syncthreads();  // this buffer is staged over two chunks from now
-    }
+    };
+    if (kl == kGemvKC) {
+      // Unrolled so the shared-memory reads run ahead of the dependent adds.
 #pragma unroll
-    for (int r = 0; r < 8; r++) {
-      const int m = g0 + warp * 8 + r;
-      if (m >= rend) break;
-      float v = __fadd_rn(acc[r], b);
-      if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
-      y[(size_t)m * 32 + lane] = v;
+      for (int k = 0; k < kGemvKC; k += 4) step4(k);
+    } else {
+      for (int k = 0; k < kl; k += 4) step4(k);
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  const int n = n0 + lane;
+  if (n >= N) return;
+  const float bn = bias ? bias[n] : 0.0f;
+#pragma unroll
+  for (int r = 0; r < MR; r++) {
+    if (r >= mr) break;
+    float v = __fadd_rn(acc[r], bn);
+    if (silu) v = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+    y[(size_t)(m0 + r) * N + n] = v;
+  }
+}
+
+// The input projection y[M, N] = x[M, 32] . w[N, 32]^T + bias (dit.c:532-541),
+// output row m stored to ex_cfg rows ((m / ex_S) * ex_cfg + c) * ex_S + m % ex_S
+// (one request's row broadcast to its CFG rows, sampler.c:256-262).  Each
+// thread keeps the weights of its two outputs in registers (64 floats) and
+// walks the block's rows; a row's 32 inputs are one broadcast read per 4.
+// 128 threads cover 256 outputs (blockIdx.y); each output sums k in
+// increasing order, then adds the bias, as the reference does.
+constexpr int kInK = 32;
+constexpr int kInThreads = 128;
+
+__global__ void __launch_bounds__(kInThreads) input_proj_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ w,
+                                                               const float* __restrict__ bias,
+                                                               float* __restrict__ y, int M,
+                                                               int N, int ex_cfg, int ex_S) {
+  const int n = blockIdx.y * (2 * kInThreads) + 2 * threadIdx.x;
+  float w0[kInK], w1[kInK];
+#pragma unroll
+  for (int k4 = 0; k4 < kInK / 4; k4++) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(w + (size_t)n * kInK) + k4);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(w + (size_t)(n + 1) * kInK) + k4);
+    w0[4 * k4] = a.x; w0[4 * k4 + 1] = a.y; w0[4 * k4 + 2] = a.z; w0[4 * k4 + 3] = a.w;
+    w1[4 * k4] = b.x; w1[4 * k4 + 1] = b.y; w1[4 * k4 + 2] = b.z; w1[4 * k4 + 3] = b.w;
+  }
+  const float b0 = bias ? bias[n] : 0.0f, b1 = bias ? bias[n + 1] : 0.0f;
+  const int copies = ex_cfg <= 1 ? 1 : ex_cfg;
+  for (int m = blockIdx.x; m < M; m += gridDim.x) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)m * kInK);
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+    for (int k4 = 0; k4 < kInK / 4; k4++) {
+      const float4 v = __ldg(xr + k4);
+      a0 = __fadd_rn(a0, __fmul_rn(v.x, w0[4 * k4]));
+      a1 = __fadd_rn(a1, __fmul_rn(v.x, w1[4 * k4]));
+      a0 = __fadd_rn(a0, __fmul_rn(v.y, w0[4 * k4 + 1]));
+      a1 = __fadd_rn(a1, __fmul_rn(v.y, w1[4 * k4 + 1]));
+      a0 = __fadd_rn(a0, __fmul_rn(v.z, w0[4 * k4 + 2]));
+      a1 = __fadd_rn(a1, __fmul_rn(v.z, w1[4 * k4 + 2]));
+      a0 = __fadd_rn(a0, __fmul_rn(v.w, w0[4 * k4 + 3]));
+      a1 = __fadd_rn(a1, __fmul_rn(v.w, w1[4 * k4 + 3]));
+    }
+    const float2 out = make_float2(__fadd_rn(a0, b0), __fadd_rn(a1, b1));
+    const size_t r = (size_t)(m / ex_S), t = (size_t)(m % ex_S);
+    for (int c = 0; c < copies; c++) {
+      float* yrow = ex_cfg <= 1 ? y + (size_t)m * N : y + ((r * ex_cfg + c) * ex_S + t) * N;
+      *reinterpret_cast<float2*>(yrow + n) = out;
     }
   }
 }
@@ -244,26 +286,43 @@ __global__ void __launch_bounds__(kNarrowThreads, 1) linear_narrow_kernel(
 int linear_ref(const float* x, const float* w, const float* bias, float* y, int M, int N, int K,
                int silu, cudaStream_t s, int ex_cfg = 1, int ex_S = 1) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15u) == 0;
-  if (ex_cfg <= 1 && aligned && N == 32 && (size_t)K * 32 * 4 <= kNarrowSmemMax &&
-      (K & 3) == 0 && M > 64) {
-    static bool attr = false;
-    const int smem = K * 32 * 4 + (int)kNarrowXBytes;
-    if (!attr) {
-      cudaFuncSetAttribute(linear_narrow_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)(kNarrowSmemMax + kNarrowXBytes));
-      attr = true;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (K == kInK && !silu && aligned && N % (2 * kInThreads) == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 7u) == 0 && M > 64) {
+    // One wave of resident blocks; each walks its share of the rows.
+    static int occ = 0;
+    if (occ <= 0 &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, input_proj_kernel, kInThreads, 0) !=
+            cudaSuccess) {
+      cudaGetLastError();
+      occ = 4;
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = std::min(sms, cdiv(M, 64));
-    linear_narrow_kernel<<<grid, kNarrowThreads, smem, s>>>(x, w, bias, y, M, K, silu);
-  } else if (ex_cfg <= 1 && aligned && M <= 64) {
-    const long long warps = (long long)M * cdiv(N, 32);
-    linear_rows_kernel<<<(unsigned)warps, 32, 0, s>>>(x, w, bias, y, M, N, K, silu);
-  } else
+    const int col_blocks = N / (2 * kInThreads);
+    const int row_blocks = std::min(M, std::max(1, std::max(occ, 1) * sms / col_blocks));
+    input_proj_kernel<<<dim3(row_blocks, col_blocks), kInThreads, 0, s>>>(x, w, bias, y, M, N,
+                                                                          ex_cfg, ex_S);
+  } else if (ex_cfg <= 1 && aligned && (K & 3) == 0 && M <= 64) {
+    // Rows per block: the fewest that cover M in at most eight-row blocks
+    // (each output's chain of adds is per row; idle row slots cost issue).
+    auto go = [&](auto kernel, int mr) {
+      static bool attr[4] = {false, false, false, false};
+      const int slot = mr == 1 ? 0 : mr == 2 ? 1 : mr == 4 ? 2 : 3;
+      if (!attr[slot]) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
+        attr[slot] = true;
+      }
+      kernel<<<dim3(cdiv(N, 32), cdiv(M, mr)), 32, kGemvSmem, s>>>(x, w, bias, y, M, N, K, silu);
+    };
+    if (M == 1) go(gemv_rows_kernel<1>, 1);
+    else if (M == 2) go(gemv_rows_kernel<2>, 2);
+    else if (M <= 4) go(gemv_rows_kernel<4>, 4);
+    else go(gemv_rows_kernel<8>, 8);
+  } else {
     linear_ref_kernel<64, 64, 4, 4><<<dim3(cdiv(N, 64), cdiv(M, 64)), 256, 0, s>>>(
         x, w, bias, y, M, N, K, silu, ex_cfg, ex_S);
+  }
   return check_launch();
 }
 
@@ -320,6 +379,245 @@ __global__ void __launch_bounds__(256) rmsnorm_ref_kernel(const float* x,
     float* ym = y + (size_t)m * D;
     for (int d = t; d < D; d += 256) ym[d] = __fmul_rn(__fmul_rn(xm[d], inv), w[d]);
   }
+}
+
+// The output head, vel[M, 32] = rmsnorm(x)[M, D] . w[32, D]^T + b
+// (dit.c:1070-1090), in one kernel: rmsnorm(x)[d] = (x[d] * inv) * g[d] with
+// inv = 1 / sqrt(mean of squares + eps), the squares summed in increasing d
+// (ops.c:738-747), and each output summed in increasing k, then the bias
+// (ops.c:221-234): the reference's operations in its order, so the result is
+// bit-identical to its IEEE build.
+//
+// A persistent grid; each block owns one contiguous share of the rows and
+// walks it in groups of up to 192 (8 warps x 24 rows; a group is the whole
+// share at config-3 sizes, and 24-row warp tiles spread it evenly over the
+// four schedulers).  W^T ([D][32],
+// 128 KB at D = 1024) and g stay in shared memory.  A group's rows stream
+// through a ring of STAGES chunks of 32 k (128 bytes per row, cp.async,
+// several in flight) twice: the first pass sums each row's squares (thread t
+// owns row t), the
+// second normalises each landed chunk in place (thread t its row again) and
+// accumulates the outputs.  In the second pass lane (g, q) = (lane / 4,
+// lane % 4) of warp w owns rows 24w + g + 8i (i < 3) and outputs 8q .. 8q+7:
+// each 16-byte read of a row's x serves 8 outputs and each 32-byte read of
+// W^T[k] serves 3 rows, so the shared-memory reads per multiply-add are a
+// fraction of one row per lane.  The second pass reads the group again from
+// L2 (up to 768 KB per block), so the normalised rows are never written out.
+//
+// Chunk layout: row r's 16-byte piece c sits at piece c ^ (r & 7), so the
+// reads of eight different rows at the same k (and of a thread's own row)
+// are free of bank conflicts.
+constexpr int kHeadRPL = 3;                            // rows per lane in the sums
+constexpr int kHeadWarpRows = 8 * kHeadRPL;            // rows per warp
+constexpr int kHeadThreads = 256;
+constexpr int kHeadMaxRows = (kHeadThreads / 32) * kHeadWarpRows;  // 192
+constexpr int kHeadKC = 32;
+
+__device__ __forceinline__ int head_idx(int r, int k) {
+  return r * kHeadKC + ((((k >> 2) ^ (r & 7))) << 2) + (k & 3);
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kHeadThreads, 1) out_head_kernel(
+    const float* __restrict__ x, const float* __restrict__ g, const float* __restrict__ w,
+    const float* __restrict__ bias, float* __restrict__ y, int M, int D, float eps, int GR) {
+  extern __shared__ float4 head_smem[];
+  float* wt = reinterpret_cast<float*>(head_smem);  // [D][32]
+  float* gs = wt + (size_t)D * 32;                   // [D]
+  float* xs = gs + D;                                // [STAGES][GR][kHeadKC]
+  const size_t chunk_floats = (size_t)GR * kHeadKC;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lg = lane >> 2, lq = lane & 3;
+  // W^T in 32 x 32 tiles: lane l reads column k = 32t + l of all 32 rows
+  // (coalesced), then writes its W^T row as eight 16-byte pieces.
+  for (int t = warp; t < D / 32; t += kHeadThreads / 32) {
+    const int k = 32 * t + lane;
+    float v[32];
+#pragma unroll
+    for (int n = 0; n < 32; n++) v[n] = w[(size_t)n * D + k];
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      *reinterpret_cast<float4*>(wt + (size_t)k * 32 + 4 * j) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  for (int i = tid; i < D; i += kHeadThreads) gs[i] = g[i];
+  float bq[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) bq[j] = bias ? bias[8 * lq + j] : 0.0f;
+  const int nk = (D + kHeadKC - 1) / kHeadKC;
+  const int share = (M + gridDim.x - 1) / gridDim.x;
+  const int rbeg = blockIdx.x * share, rend = min(M, rbeg + share);
+  // One chunk: GR rows x 8 pieces of 16 bytes (rows past the share repeat its
+  // last row; their results are not stored).
+  auto stage = [&](int g0, int kc) {
+    float* dst = xs + (size_t)(kc % STAGES) * chunk_floats;
+    const int kw = min(kHeadKC, D - kc * kHeadKC) / 4;
+    for (int i = tid; i < GR * (kHeadKC / 4); i += kHeadThreads) {
+      const int r = i >> 3, c = i & 7;
+      if (c < kw) {
+        const int row = min(g0 + r, rend - 1);
+        cp_async16(dst + r * kHeadKC + ((c ^ (r & 7)) << 2),
+                   x + (size_t)row * D + (size_t)kc * kHeadKC + 4 * c);
+      }
+    }
+  };
+  // Streams chunks 0 .. nk-1 of the group through the ring; body(kc, buf)
+  // runs once chunk kc has landed and is visible to every thread.
+  auto stream = [&](int g0, auto&& body) {
+#pragma unroll
+    for (int j = 0; j < STAGES - 1; j++) {
+      if (j < nk) stage(g0, j);
+      cp_async_commit();
+    }
+    for (int kc = 0; kc < nk; kc++) {
+      if (kc + STAGES - 1 < nk) stage(g0, kc + STAGES - 1);
+      cp_async_commit();
+      cp_async_wait<STAGES - 1>();
+      __syncthreads();
+      body(kc, xs + (size_t)(kc % STAGES) * chunk_floats);
+      __syncthreads();  // the buffer is staged again STAGES - 1 chunks later
+    }
+    cp_async_wait<0>();
+  };
+  __syncthreads();  // W^T and g staged
+  const bool own_row = tid < GR;  // thread t owns row t of each group
+  for (int g0 = rbeg; g0 < rend; g0 += GR) {
+    // Pass 1: thread t sums the squares of row t in increasing d.
+    float ms = 0.0f;
+    stream(g0, [&](int kc, float* buf) {
+      if (!own_row) return;
+      const int kl = min(kHeadKC, D - kc * kHeadKC);
+      for (int k = 0; k < kl; k += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(buf + head_idx(tid, k));
+        ms = __fadd_rn(ms, __fmul_rn(v.x, v.x));
+        ms = __fadd_rn(ms, __fmul_rn(v.y, v.y));
+        ms = __fadd_rn(ms, __fmul_rn(v.z, v.z));
+        ms = __fadd_rn(ms, __fmul_rn(v.w, v.w));
+      }
+    });
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ms, (float)D), eps)));
+    // Pass 2: normalise each chunk in place (thread t: row t), then the sums.
+    float acc[kHeadRPL][8];
+#pragma unroll
+    for (int i = 0; i < kHeadRPL; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+    // A warp wholly past the group (or the share) skips the sums.
+    const bool active = warp * kHeadWarpRows < GR && g0 + warp * kHeadWarpRows < rend;
+    stream(g0, [&](int kc, float* buf) {
+      const int k0 = kc * kHeadKC;
+      const int kl = min(kHeadKC, D - k0);
+      for (int k = 0; k < kl && own_row; k += 4) {
+        float4* p = reinterpret_cast<float4*>(buf + head_idx(tid, k));
+        float4 v = *p;
+        const float4 gg = *reinterpret_cast<const float4*>(gs + k0 + k);
+        v.x = __fmul_rn(__fmul_rn(v.x, inv), gg.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, inv), gg.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, inv), gg.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, inv), gg.w);
+        *p = v;
+      }
+      __syncthreads();
+      if (!active) return;
+      for (int k = 0; k < kl; k += 4) {
+        float4 a[kHeadRPL];
+#pragma unroll
+        for (int i = 0; i < kHeadRPL; i++)
+          a[i] = *reinterpret_cast<const float4*>(
+              buf + head_idx(min(warp * kHeadWarpRows + lg + 8 * i, GR - 1), k));
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const float4* wr = reinterpret_cast<const float4*>(wt + (size_t)(k0 + k + kk) * 32 + 8 * lq);
+          const float4 wl = wr[0], wh = wr[1];
+          const float wv[8] = {wl.x, wl.y, wl.z, wl.w, wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+          for (int i = 0; i < kHeadRPL; i++) {
+            const float xv = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xv, wv[j]));
+          }
+        }
+      }
+    });
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < kHeadRPL; i++) {
+        const int m = g0 + warp * kHeadWarpRows + lg + 8 * i;
+        if (m >= rend || warp * kHeadWarpRows + lg + 8 * i >= GR) continue;
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[j] = __fadd_rn(acc[i][j], bq[j]);
+        float4* dst = reinterpret_cast<float4*>(y + (size_t)m * 32 + 8 * lq);
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  }
+}
+
+size_t out_head_smem(int D, int stages, int GR) {
+  return sizeof(float) * ((size_t)D * 32 + D + (size_t)stages * GR * kHeadKC);
+}
+
+constexpr size_t kHeadSmemCap = 227 * 1024;
+
+// Launch geometry of the fused output head: one block per SM (at most one
+// per 64 rows), each over a contiguous share of the rows in groups of GR.
+struct HeadPlan {
+  int grid, GR, stages;  // stages 0: the fused kernel does not apply
+};
+
+HeadPlan out_head_plan(const IroDiTModelDev* m, const float* x, const float* vel, int rows) {
+  HeadPlan p{0, 0, 0};
+  const int D = m->block[0].model_dim;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(m->out_w) |
+                         reinterpret_cast<uintptr_t>(m->out_norm) |
+                         reinterpret_cast<uintptr_t>(vel)) & 15u) == 0;
+  if (m->latent_dim != 32 || !aligned || D % 32 != 0 || rows <= 0) return p;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  p.grid = std::min(sms, cdiv(rows, 64));
+  p.GR = std::min(kHeadMaxRows, cdiv(rows, p.grid));
+  if (out_head_smem(D, 4, p.GR) <= kHeadSmemCap) p.stages = 4;
+  else if (out_head_smem(D, 3, p.GR) <= kHeadSmemCap) p.stages = 3;
+  return p;
+}
+
+bool output_head_fused(const IroDiTModelDev* m, const float* x, const float* vel, int rows) {
+  return out_head_plan(m, x, vel, rows).stages > 0;
+}
+
+template <int STAGES>
+int launch_out_head(const IroDiTModelDev* m, const float* x, int rows, float* vel,
+                    const HeadPlan& p, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(out_head_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kHeadSmemCap);
+    attr = true;
+  }
+  const int D = m->block[0].model_dim;
+  out_head_kernel<STAGES><<<p.grid, kHeadThreads, out_head_smem(D, STAGES, p.GR), s>>>(
+      x, m->out_norm, m->out_w, m->out_b, vel, rows, D, m->norm_eps, p.GR);
+  return check_launch();
+}
+
+// The output head on `rows` hidden rows into vel [rows, 32]: the fused kernel
+// when its shared memory fits (D <= 1280 with 3-4 chunks in flight), else
+// the RMSNorm into `scratch` [rows, D] (may be x itself) and the general
+// linear.
+int output_head(const IroDiTModelDev* m, const float* x, int rows, float* vel, float* scratch,
+                cudaStream_t s) {
+  const HeadPlan p = out_head_plan(m, x, vel, rows);
+  if (p.stages == 4) return launch_out_head<4>(m, x, rows, vel, p, s);
+  if (p.stages == 3) return launch_out_head<3>(m, x, rows, vel, p, s);
+  const int D = m->block[0].model_dim;
+  rmsnorm_ref_kernel<<<cdiv(rows, kNR), 256, 0, s>>>(x, m->out_norm, scratch, rows, D,
+                                                     m->norm_eps);
+  int st = check_launch();
+  if (st) return st;
+  return linear_ref(scratch, m->out_w, m->out_b, vel, rows, m->latent_dim, D, 0, s);
 }
 
 // sampler.c:283-297: guided = v_cond + sum_i scale_i (v_cond - v_uncond_i),
@@ -517,9 +815,7 @@ int step_impl(Ctx* c, const IroDiTModelDev* m, float* state, int R, int cfg, int
   }
   // Output head (normalised in place: x is rebuilt from the state next
   // step) into the velocity, then the guided Euler update.
-  rmsnorm_ref_kernel<<<cdiv(B * S, kNR), 256, 0, s>>>(x, m->out_norm, x, B * S, D, m->norm_eps);
-  if ((st = check_launch())) return st;
-  if ((st = linear_ref(x, m->out_w, m->out_b, vel, B * S, L, D, 0, s))) return st;
+  if ((st = output_head(m, x, B * S, vel, x, s))) return st;
   if (vel_out) return IRO_OK;
   const float dt = t_next - t;
   const float s1 = cfg > 1 ? scales[0] : 0.0f, s2 = cfg > 2 ? scales[1] : 0.0f;
@@ -764,13 +1060,11 @@ int iro_dit_output_dev(const IroDiTModelDev* m, const float* x, int B, int S, fl
   cudaStream_t s = pick_stream(c, stream);
   const int D = m->block[0].model_dim, rows = B * S;
   float* norm = static_cast<float*>(workspace);
-  if (!norm) {
+  if (!norm && !output_head_fused(m, x, velocity, rows)) {
     norm = static_cast<float*>(arena_get(c, sizeof(float) * (size_t)rows * D, &st));
     if (!norm) return st;
   }
-  rmsnorm_ref_kernel<<<cdiv(rows, kNR), 256, 0, s>>>(x, m->out_norm, norm, rows, D, m->norm_eps);
-  if ((st = check_launch())) return st;
-  return linear_ref(norm, m->out_w, m->out_b, velocity, rows, m->latent_dim, D, 0, s);
+  return output_head(m, x, rows, velocity, norm, s);
 }
 
 }  // extern "C"

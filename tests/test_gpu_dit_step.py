@@ -98,11 +98,12 @@ def test_stage_entry_points_match_reference():
     assert err.max() <= 1e-5 * np.abs(want).max()
 
 
-@pytest.mark.parametrize("rows", [65, 1000, 4099])
+@pytest.mark.parametrize("rows", [65, 1000, 4099, 40000])
 def test_output_head_bit_exact_many_rows(rows):
-    """The output head's persistent row-group kernel (groups of 128 rows,
-    ragged last group, k in staged chunks) against the reference's
-    iro_dit_output, bit for bit."""
+    """The fused output head (RMSNorm and the 32-channel linear in one
+    persistent kernel: row shares of up to 256-row groups, ragged last warp,
+    several groups per block at 40000 rows, k in staged chunks) against the
+    reference's iro_dit_output, bit for bit."""
     state, ck, cv, mask, blocks, head = inputs.dit_model_case(19, 1, 1, 1, 8, 4)
     m = build_model(blocks, head)
     D = head["in_w"].shape[0]
