@@ -234,18 +234,34 @@ __global__ void __launch_bounds__(32) gemv_rows_kernel(const float* __restrict__
 // output row m stored to ex_cfg rows ((m / ex_S) * ex_cfg + c) * ex_S + m % ex_S
 // (one request's row broadcast to its CFG rows, sampler.c:256-262).  Each
 // thread keeps the weights of its two outputs in registers (64 floats) and
-// walks the block's rows; a row's 32 inputs are one broadcast read per 4.
-// 128 threads cover 256 outputs (blockIdx.y); each output sums k in
-// increasing order, then adds the bias, as the reference does.
+// walks the block's rows; the rows' inputs (128 bytes each) arrive through a
+// ring of kInAhead rows in shared memory by cp.async, several rows ahead, and
+// are read as broadcasts.  128 threads cover 256 outputs (blockIdx.y); each
+// output sums k in increasing order, then adds the bias, as the reference
+// does.
 constexpr int kInK = 32;
 constexpr int kInThreads = 128;
+constexpr int kInAhead = 8;
 
 __global__ void __launch_bounds__(kInThreads) input_proj_kernel(const float* __restrict__ x,
                                                                const float* __restrict__ w,
                                                                const float* __restrict__ bias,
                                                                float* __restrict__ y, int M,
                                                                int N, int ex_cfg, int ex_S) {
+  __shared__ __align__(16) float xs[kInAhead][kInK];
   const int n = blockIdx.y * (2 * kInThreads) + 2 * threadIdx.x;
+  // Row i of this block is blockIdx.x + i * gridDim.x; threads 0-7 move its
+  // eight 16-byte pieces.
+  const int nrows = M > (int)blockIdx.x ? (M - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto fetch = [&](int i) {
+    if (i < nrows && threadIdx.x < kInK / 4) {
+      const int m = blockIdx.x + i * gridDim.x;
+      cp_async16(&xs[i % kInAhead][4 * threadIdx.x], x + (size_t)m * kInK + 4 * threadIdx.x);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < kInAhead - 1; i++) fetch(i);
   float w0[kInK], w1[kInK];
 #pragma unroll
   for (int k4 = 0; k4 < kInK / 4; k4++) {
@@ -256,12 +272,17 @@ __global__ void __launch_bounds__(kInThreads) input_proj_kernel(const float* __r
   }
   const float b0 = bias ? bias[n] : 0.0f, b1 = bias ? bias[n + 1] : 0.0f;
   const int copies = ex_cfg <= 1 ? 1 : ex_cfg;
-  for (int m = blockIdx.x; m < M; m += gridDim.x) {
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)m * kInK);
+  for (int i = 0; i < nrows; i++) {
+    // The ring slot row i + kInAhead - 1 goes to was read for row i - 1,
+    // which every thread finished before the barrier at the end of its turn.
+    fetch(i + kInAhead - 1);
+    cp_async_wait<kInAhead - 1>();
+    __syncthreads();
+    const float4* xr = reinterpret_cast<const float4*>(xs[i % kInAhead]);
     float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
     for (int k4 = 0; k4 < kInK / 4; k4++) {
-      const float4 v = __ldg(xr + k4);
+      const float4 v = xr[k4];
       a0 = __fadd_rn(a0, __fmul_rn(v.x, w0[4 * k4]));
       a1 = __fadd_rn(a1, __fmul_rn(v.x, w1[4 * k4]));
       a0 = __fadd_rn(a0, __fmul_rn(v.y, w0[4 * k4 + 1]));
@@ -271,6 +292,8 @@ __global__ void __launch_bounds__(kInThreads) input_proj_kernel(const float* __r
       a0 = __fadd_rn(a0, __fmul_rn(v.w, w0[4 * k4 + 3]));
       a1 = __fadd_rn(a1, __fmul_rn(v.w, w1[4 * k4 + 3]));
     }
+    __syncthreads();
+    const int m = blockIdx.x + i * gridDim.x;
     const float2 out = make_float2(__fadd_rn(a0, b0), __fadd_rn(a1, b1));
     const size_t r = (size_t)(m / ex_S), t = (size_t)(m % ex_S);
     for (int c = 0; c < copies; c++) {
@@ -278,6 +301,7 @@ __global__ void __launch_bounds__(kInThreads) input_proj_kernel(const float* __r
       *reinterpret_cast<float2*>(yrow + n) = out;
     }
   }
+  cp_async_wait<0>();
 }
 
 // ex_cfg > 1: output row m is written to the ex_cfg rows
