@@ -1,6 +1,6 @@
 """Benchmark of the B200 int8 W8A8 path (one JSON line on rank 0).
 
-Headline: the int8 SwiGLU MLP block of the DiT, x fp32
+Headline (benchmark config 2): the int8 SwiGLU MLP block of the DiT, x fp32
 [M=2048, D=1024] N(0,1); W1, W3 [2816, 1024] and W2 [1024, 2816] N(0,0.02)
 quantised per output channel; a seeded fp32 bias on every projection;
 per-row activation quantisation (the reference's asymmetric u8 + zero point,
@@ -15,13 +15,13 @@ rotate through NSETS distinct input/weight sets whose total exceeds the
 
 The same line carries the metric's second half and config 4 as nested
 objects, each with the reference's own CPU code timed beside it:
-  "dit"   BASELINE config 3: whole DiT Euler steps (12 blocks, d 1024, 16
+  "dit"   benchmark config 3: whole DiT Euler steps (12 blocks, d 1024, 16
           heads, SwiGLU 2816; 8 requests x 4 CFG rows x 750 frames = 24,000
           rows per linear per GPU), steps/s and rows/s;
   "dit_ref_dims"  the same at the reference checkpoint's dimensions (d 1280,
           20 heads, 3680; the only ones the reference's dit.c compiles to),
           against the reference's dit.c forward on the host cores;
-  "conv7" BASELINE config 4: the codec's int8 kernel-7 conv, 4 x 48000
+  "conv7" benchmark config 4: the codec's int8 kernel-7 conv, 4 x 48000
           frames, 512 -> 512 channels.
 Synthetic seeded data throughout: there is no dataset or checkpoint for this
 path.
@@ -62,7 +62,7 @@ DTYPE = "int8 (u8 x s8 -> s32, fp32 dequant epilogue)"
 DATA = "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) biases)"
 ONEMKL = "oneMKL absent on this host: the reference's scalar exact int8 GEMM (ops.c:350-365)"
 
-# BASELINE config 3 and the reference checkpoint's dimensions.
+# benchmark config 3 and the reference checkpoint's dimensions.
 DIT_DIMS = {"cfg3": (1024, 16, 2816), "reference": (1280, 20, 3680)}
 DIT_RANK, DIT_LAYERS, DIT_CFG, DIT_S, DIT_C = 192, 12, 4, 750, 128
 DIT_REQUESTS = 8                   # per GPU
@@ -947,7 +947,7 @@ def run_reference(args):
 
 
 def run_dit(args):
-    """BASELINE config 3 alone (or --dit-dims reference): DiT Euler steps."""
+    """benchmark config 3 alone (or --dit-dims reference): DiT Euler steps."""
     iro, dist, stream, world, rank, local, barrier, max_ranks = _gpu_setup(args)
     clocks = ClockSampler(physical_gpu(local))
     clocks.start()
@@ -966,7 +966,7 @@ def run_dit(args):
 
 
 def run_conv7(args):
-    """BASELINE config 4 alone: the codec's int8 kernel-7 conv."""
+    """benchmark config 4 alone: the codec's int8 kernel-7 conv."""
     iro, dist, stream, world, rank, local, barrier, max_ranks = _gpu_setup(args)
     ms, wq, inp, bias = leg_conv7(args, iro, stream, max_ranks)
     if world > 1:
@@ -988,7 +988,7 @@ SWEEP_REQUESTS = (1, 8, 64, 512)
 
 
 def run_sweep(args):
-    """BASELINE config 5.  (ii) The isolated int8 linear (quantised x in,
+    """benchmark config 5.  (ii) The isolated int8 linear (quantised x in,
     fp32 y = dequant + bias out; iro_int8_linear_dev) at M in {64, 256, 4096,
     65536} x N in {1024, 2816, 4096}, K = 1024, inputs with config 1's
     distributions: TOPS, fraction of the int8 peak and HBM GB/s of the

@@ -1,7 +1,7 @@
 """GPU parity of the codec's W8A8 kernel-7 convolution (dacvae.c:543-688)
 against the reference fixtures and the CPU oracle, bit-exact.
 
-Full-size check (4 x 48000 frames, 512 -> 512 channels,
+Full-size check (benchmark config 4: 4 x 48000 frames, 512 -> 512 channels,
 kernel 7): the GPU runs the whole batch; the oracle recomputes sampled
 windows of output rows.  Each window's input slice is cut out with explicit
 zero rows where it crosses the sequence ends.  That is exact: 0 is always
