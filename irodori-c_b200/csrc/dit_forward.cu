@@ -316,7 +316,8 @@ int linear_ref(const float* x, const float* w, const float* bias, float* y, int 
   if (K == kInK && !silu && aligned && N % (2 * kInThreads) == 0 &&
       (reinterpret_cast<uintptr_t>(y) & 7u) == 0 && M > 64) {
     // One wave of resident blocks; each walks its share of the rows.
-    static int occ = 0;
+    static int occ_dev[64] = {0};
+    int& occ = occ_dev[dev & 63];
     if (occ <= 0 &&
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, input_proj_kernel, kInThreads, 0) !=
             cudaSuccess) {
@@ -330,12 +331,14 @@ int linear_ref(const float* x, const float* w, const float* bias, float* y, int 
   } else if (ex_cfg <= 1 && aligned && (K & 3) == 0 && M <= 64) {
     // Rows per block: the fewest that cover M in at most eight-row blocks
     // (each output's chain of adds is per row; idle row slots cost issue).
+    // The shared-memory opt-in is a per-device attribute of each kernel (the
+    // four instantiations share this lambda's type, hence the slot).
     auto go = [&](auto kernel, int mr) {
-      static bool attr[4] = {false, false, false, false};
+      static bool attr[4][64] = {};
       const int slot = mr == 1 ? 0 : mr == 2 ? 1 : mr == 4 ? 2 : 3;
-      if (!attr[slot]) {
+      if (!attr[slot][dev & 63]) {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvSmem);
-        attr[slot] = true;
+        attr[slot][dev & 63] = true;
       }
       kernel<<<dim3(cdiv(N, 32), cdiv(M, mr)), 32, kGemvSmem, s>>>(x, w, bias, y, M, N, K, silu);
     };
@@ -615,11 +618,13 @@ bool output_head_fused(const IroDiTModelDev* m, const float* x, const float* vel
 template <int STAGES>
 int launch_out_head(const IroDiTModelDev* m, const float* x, int rows, float* vel,
                     const HeadPlan& p, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr[64] = {false};  // the shared-memory opt-in is per device
+  if (!attr[dev & 63]) {
     cudaFuncSetAttribute(out_head_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kHeadSmemCap);
-    attr = true;
+    attr[dev & 63] = true;
   }
   const int D = m->block[0].model_dim;
   out_head_kernel<STAGES><<<p.grid, kHeadThreads, out_head_smem(D, STAGES, p.GR), s>>>(
